@@ -1,0 +1,425 @@
+"""MoE expert-layer benchmark (router -> permute -> grouped GEMMs -> combine).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload qwen3-30b-a3b|gpt-oss-20b|qwen3-235b-a22b]
+
+One step runs the layer once for every batch size of the workload (decode and
+prefill batches of one layer shape) on seeded synthetic weights and tokens
+with the workload's shapes (random-init, quantised as the checkpoints are).
+``value`` is tokens/s over the step: sum of batch tokens / sum of device
+time, each batch replayed from a CUDA graph with L2 flushed (a 256 MiB write)
+before it, timed with CUDA events. ``e2e`` is the same metric through the
+public modules (router + ParallelExperts forward, eager) with the tokens
+copied from pinned host memory and the outputs copied back every batch.
+
+N > 1 (torchrun, one rank per GPU): replicated-token expert parallelism, the
+reference's record_* layout: every rank routes all tokens and runs its
+E/N experts; contributions are exchanged with one NCCL all-reduce and combined
+in global expert order. Work per step is fixed (strong scaling).
+
+``--impl reference`` times the reference algorithm on the host CPU (the
+torch restatement in oracle/, reference numerics), rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+from types import SimpleNamespace
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from moe_serving_profile_b200 import _lib, experts as X, layout, ops  # noqa: E402
+from moe_serving_profile_b200 import synthetic as S  # noqa: E402
+from moe_serving_profile_b200.parallel import ParallelGroup  # noqa: E402
+from moe_serving_profile_b200.router import GptOssRouter, Qwen3Router  # noqa: E402
+
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+L2_FLUSH_BYTES = 256 << 20
+METRIC = "MoE-layer tokens/s at 1/2/4/8 B200 (decode & prefill), % HBM/tensor roofline"
+
+
+def peaks():
+    if PEAKS.exists():
+        p = json.loads(PEAKS.read_text())
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, flag in zip(self.NAMES, parts[2:]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- workload
+def build_layer(cfg, dev, ep: int, rank: int, seed: int = 1):
+    """Router module + rank-local packed experts for one synthetic layer."""
+    epr = cfg.experts // ep
+    sl = slice(rank * epr, (rank + 1) * epr)
+    if cfg.family == "qwen3":
+        w = S.make_qwen(cfg, seed, dev)
+        router = Qwen3Router(SimpleNamespace(num_experts_per_tok=cfg.top_k, num_experts=cfg.experts,
+                                             norm_topk_prob=cfg.norm_topk, hidden_size=cfg.hidden)).to(dev)
+        router.weight.data = w.router
+        if w.router_bias is not None:
+            router.bias = w.router_bias
+        packed = layout.fp8_experts(w.gate[sl], w.gate_scale[sl], w.up[sl], w.up_scale[sl],
+                                    w.down[sl], w.down_scale[sl], cfg.block)
+    else:
+        w = S.make_gpt_oss(cfg, seed, dev)
+        router = GptOssRouter(SimpleNamespace(num_experts_per_tok=cfg.top_k,
+                                              num_local_experts=cfg.experts,
+                                              hidden_size=cfg.hidden)).to(dev)
+        router.weight.data = w.router
+        router.bias.data = w.router_bias
+        packed = layout.gpt_oss_mxfp4_experts(w.gu_blocks[sl], w.gu_scales[sl], w.gu_bias[sl],
+                                              w.dn_blocks[sl], w.dn_scales[sl], w.dn_bias[sl],
+                                              cfg.alpha, cfg.limit)
+    del w
+    torch.cuda.empty_cache()
+    return router, packed
+
+
+def layer_call(cfg, router, packed, x, parallel, rank, ep):
+    _, scores, idx = router(x)
+    return X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts,
+                           expert_begin=rank * (cfg.experts // ep), parallel=parallel,
+                           numerics="reference")
+
+
+def kernel_launches(T: int, K: int) -> int:
+    """Our kernels per layer call: router (2) + permute (1 or 3) + 2 GEMMs + combine."""
+    return 2 + (1 if T * K <= 8192 else 3) + 2 + 1
+
+
+# --------------------------------------------------------------------------- CPU leg
+_CPU_WEIGHTS = {}
+
+
+def cpu_layer_time(cfg, T: int, seed: int = 1) -> float:
+    """Seconds for one reference-numerics layer call (router + experts) on the host CPU."""
+    from oracle import oracle
+    if cfg.name not in _CPU_WEIGHTS:
+        _CPU_WEIGHTS[cfg.name] = (S.make_qwen(cfg, seed, "cpu") if cfg.family == "qwen3"
+                                  else S.make_gpt_oss(cfg, seed, "cpu"))
+    w = _CPU_WEIGHTS[cfg.name]
+    x = S.make_hidden(T, cfg.hidden, T, "cpu")
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        if cfg.family == "qwen3":
+            probs, scores, idx, _ = oracle.qwen_router(x, w.router, cfg.top_k, cfg.norm_topk)
+            oracle.qwen_layer(x, idx, scores, w.gate, w.gate_scale, w.up, w.up_scale, w.down,
+                              w.down_scale, cfg.block)
+        else:
+            logits, scores, idx = oracle.gpt_oss_router(x, w.router, w.router_bias, cfg.top_k)
+            oracle.gpt_oss_layer(x, idx, scores, w.gu_blocks, w.gu_scales, w.gu_bias, w.dn_blocks,
+                                 w.dn_scales, w.dn_bias, cfg.alpha, cfg.limit)
+        return time.perf_counter() - t0
+
+
+def cpu_sweep(cfg, budget_s: float):
+    """tokens/s of the reference path on the host over the workload's batches.
+    Batches up to 64 tokens run whole; larger ones run a 64- or 512-token
+    sample and are scaled linearly by tokens (at >= 64 tokens nearly every
+    expert is in use, so the per-token cost is close to flat; linear scaling
+    slightly understates the CPU at the largest batches). Returns
+    (tokens/s, sample text)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    total_t, total_s, parts = 0, 0.0, []
+    sample_T = 512 if budget_s >= 30 else 64
+    measured = {}
+    for T in cfg.batches:
+        run = T if T <= 64 else sample_T
+        if run not in measured:
+            measured[run] = cpu_layer_time(cfg, run)
+        sec = measured[run] * (T / run)
+        total_t += T
+        total_s += sec
+        parts.append(f"T={T}" + ("" if run == T else f" (scaled from {run})"))
+    return total_t / total_s, ", ".join(parts)
+
+
+def reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    for _ in range(args.warmup):
+        cpu_sweep(cfg, budget)
+    vals = []
+    for _ in range(args.steps):
+        v, sample = cpu_sweep(cfg, budget)
+        vals.append(v)
+    value = statistics.median(vals)
+    cores = torch.get_num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sum(cfg.batches) / value * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "batches": list(cfg.batches), "path": "reference numerics "
+                   "(dequantise-then-BF16 per expert, ordered merge) on host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--workload", default="qwen3-30b-a3b")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = S.CONFIGS[args.workload]
+    if args.impl == "reference":
+        return reference_arm(args, cfg)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    parallel = ParallelGroup(world) if world > 1 else None
+    hbm, tf_burst, tf_sust, peak_kind = peaks()
+
+    router, packed = build_layer(cfg, dev, world, rank)
+    batches = list(cfg.batches)
+    xs = {T: S.make_hidden(T, cfg.hidden, seed=1000 + T, device=dev) for T in batches}
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    # ---- CUDA graphs, one per batch size
+    graphs, outs = {}, {}
+    with torch.cuda.stream(stream):
+        for T in batches:
+            for _ in range(2):
+                layer_call(cfg, router, packed, xs[T], parallel, rank, world)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    for T in batches:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            outs[T] = layer_call(cfg, router, packed, xs[T], parallel, rank, world)
+        graphs[T] = g
+    torch.cuda.synchronize(dev)
+
+    def step(record):
+        times = {}
+        with torch.cuda.stream(stream):
+            for T in batches:
+                flush.fill_(T & 0xff)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                graphs[T].replay()
+                e.record(stream)
+                times[T] = (s, e)
+        return times
+
+    for _ in range(max(3, args.warmup)):
+        step(False)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    per_batch_ms = {T: 0.0 for T in batches}
+    with ClockSampler(local) as clocks:
+        recs = [step(True) for _ in range(args.steps)]
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for rec in recs:
+        for T, (s, e) in rec.items():
+            per_batch_ms[T] += s.elapsed_time(e) / args.steps
+    step_ms = sum(per_batch_ms.values())
+    if world > 1:
+        t = torch.tensor([step_ms] + [per_batch_ms[T] for T in batches], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, per = float(t[0]), t[1:].tolist()
+        per_batch_ms = dict(zip(batches, per))
+    tokens = sum(batches)
+    value = tokens / (step_ms / 1e3)
+
+    # ---- per-batch roofline (algorithmic bytes from the actual routing)
+    per_batch = []
+    for T in batches:
+        with torch.cuda.stream(stream):
+            _, _, idx = router(xs[T])
+            counts = torch.bincount(idx.flatten(), minlength=cfg.experts).cpu()
+        ms = per_batch_ms[T]
+        byts = S.algorithmic_bytes(cfg, T, counts)
+        flops = S.algorithmic_flops(cfg, T)
+        gbs = byts / (ms / 1e3) / 1e9
+        tfs = flops / (ms / 1e3) / 1e12
+        per_batch.append({"tokens": T, "ms": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+                          "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                          "tflops": round(tfs, 2), "tensor_frac": round(tfs / tf_burst, 4),
+                          "used_experts": int((counts > 0).sum()),
+                          "expert_load_cv": round(S.expert_load_cv(counts), 3)})
+
+    # ---- dominant kernel: gate/up grouped GEMM of the largest batch, timed alone
+    Tm = max(batches)
+    with torch.cuda.stream(stream):
+        x = xs[Tm]
+        _, scores, idx = router(x)
+        perm = ops.permute(idx, cfg.experts)
+        act = torch.empty(Tm * cfg.top_k, packed.i_pad, device=dev, dtype=torch.bfloat16)
+        kw = dict(K=cfg.top_k, num_experts=cfg.experts, expert_begin=rank * (cfg.experts // world),
+                  tokens=Tm, out=act)
+        for _ in range(3):
+            X.gate_up(packed, x, perm, **kw)
+        n_rep, kms = 10, 0.0
+        for _ in range(n_rep):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            X.gate_up(packed, x, perm, **kw)
+            e.record(stream)
+            e.synchronize()
+            kms += s.elapsed_time(e) / n_rep
+    local_rows = int(perm.offsets[rank * (cfg.experts // world) + packed.n_experts]
+                     - perm.offsets[rank * (cfg.experts // world)])
+    gemm_flops = 2 * local_rows * cfg.hidden * 2 * cfg.inter
+    achieved = gemm_flops / (kms / 1e3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(f"{cfg.name}:gate_up:T{Tm}")
+    roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_burst,
+                "unit": "TFLOP/s", "frac": round(achieved / tf_burst, 4), "traffic": traffic,
+                "kernel": f"gate/up grouped GEMM, T={Tm}", "peak_kind": f"{peak_kind} bf16 burst",
+                "kernel_ms": round(kms, 4)}
+
+    # ---- end to end through the public modules with host buffers
+    host_x = {T: xs[T].cpu().pin_memory() for T in batches}
+    host_o = {T: torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory() for T in batches}
+    h2d = sum(T * cfg.hidden * 2 for T in batches)
+    d2h = h2d
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            for T in batches:
+                xd = host_x[T].to(dev, non_blocking=True)
+                o = layer_call(cfg, router, packed, xd, parallel, rank, world)
+                host_o[T].copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = s.elapsed_time(e) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    e2e_value = tokens / (e2e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample = cpu_sweep(cfg, budget_s=20.0)
+        cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"reference numerics on host CPU: {sample}"}
+
+    launches = args.steps * sum(kernel_launches(T, cfg.top_k) for T in batches)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, quantised like the checkpoints)",
+            "config": {"workload": cfg.name, "batches": batches, "hidden": cfg.hidden,
+                       "experts": cfg.experts, "top_k": cfg.top_k, "intermediate": cfg.inter,
+                       "weights": cfg.storage, "parallelism": f"ep{world} replicated-token",
+                       "l2": "flushed (256 MiB write) before every batch", "timing": "CUDA graph "
+                       "replay per batch, CUDA events"},
+            "per_batch": per_batch, "roofline": roofline,
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches, "clocks": clocks.summary(), "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    for g in graphs.values():
+        del g
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

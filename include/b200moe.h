@@ -1,0 +1,219 @@
+/*
+ * b200moe — C ABI of the sm_100a MoE expert layer.
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t
+ * (passed as void*), enqueues work on that stream without any host
+ * synchronisation, and returns an int status (B200MOE_OK or an error code;
+ * b200moe_last_error() gives the message for the calling thread). The
+ * library never allocates or frees caller memory: all outputs and workspaces
+ * are owned by the caller (torch's caching allocator on the Python side).
+ *
+ * The reference (moe_serving, pure Python) has no foreign-function boundary;
+ * each function names the reference code path it replaces, by file:line in
+ * the reference project. Router formulas live in Transformers; the cited
+ * lines are those of the installed transformers 5.5.0 proxy of the pinned
+ * 5.20.0 tree (models/qwen3_moe/modeling_qwen3_moe.py and
+ * models/gpt_oss/modeling_gpt_oss.py).
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+#define B200MOE_OK 0
+#define B200MOE_ERR_INVALID 1     /* bad argument / shape */
+#define B200MOE_ERR_UNSUPPORTED 2 /* valid but outside what the kernels implement */
+#define B200MOE_ERR_CUDA 3        /* a CUDA runtime call failed */
+
+/* Device status bits (b200moe_device_status): set by kernels, never fatal. */
+#define B200MOE_STATUS_WAIT_TIMEOUT 1 /* a bounded device wait gave up */
+#define B200MOE_STATUS_BAD_TILE 2     /* inconsistent tile bookkeeping */
+#define B200MOE_STATUS_BAD_INDEX 4    /* an expert id outside [0, E) was dropped */
+
+/* Message describing the last non-zero return on this host thread. */
+const char* b200moe_last_error(void);
+
+/* Library version string. */
+const char* b200moe_version(void);
+
+/* Read (and optionally clear) the per-device status word that kernels OR
+ * B200MOE_STATUS_* bits into. Synchronises the device. */
+int b200moe_device_status(int device, int clear, int* out_status);
+
+/* ------------------------------------------------------------ router
+ * Fused router: logits = hidden[T,H] . weight[E,H]^T (+ bias) accumulated in
+ * fp32 in a fixed order (H split into 8-element vectors dealt round-robin to
+ * 32 partial sums, each sequential, then combined pairwise with offsets
+ * 16, 8, 4, 2, 1), followed by softmax / top-k / per-expert counts.
+ * Top-k order: value descending, equal values by ascending expert id.
+ *
+ * mode B200MOE_ROUTER_QWEN3 replaces Qwen3MoeTopKRouter.forward
+ *   (qwen3_moe/modeling_qwen3_moe.py:263-272), hooked at
+ *   moe_serving/qwen3_parallel.py:42-44: bf16 logits, fp32 softmax over E,
+ *   top-k, optional renormalisation; probs fp32 [T,E], scores fp32 [T,K].
+ * mode B200MOE_ROUTER_GPT_OSS replaces GptOssTopKRouter.forward
+ *   (gpt_oss/modeling_gpt_oss.py:126-131), hooked at
+ *   moe_serving/gpt_oss_parallel.py:256-258: bf16 logits with bias, top-k on
+ *   the logits, softmax over the k values in bf16; scores bf16 [T,K].
+ * mode B200MOE_ROUTER_NATIVE replaces moe_serving/moe.py:97-107 (route):
+ *   fp32 logits, fp32 softmax, top-k, renormalise with clamp 1e-20; scores
+ *   are written as bf16 [T,K] (the hidden dtype).
+ *
+ * bias: bf16 [E], required for GPT_OSS; optional for QWEN3 (added to the
+ *   fp32 sum before the bf16 rounding, as F.linear(h, W, b) does); ignored
+ *   for NATIVE.
+ * logits: workspace/output, bf16 [T,E] (QWEN3, GPT_OSS) or fp32 [T,E]
+ *   (NATIVE). With logits_given != 0 the GEMV is skipped and the selection
+ *   runs on the caller's logits (used to test selection on identical inputs).
+ * counts: int32 [E] or NULL; zeroed and filled on the stream.
+ */
+#define B200MOE_ROUTER_QWEN3 0
+#define B200MOE_ROUTER_GPT_OSS 1
+#define B200MOE_ROUTER_NATIVE 2
+
+int b200moe_router(int device, void* stream, int mode, const void* hidden,
+                   long long ld_hidden, const void* weight, const void* bias, int T, int H,
+                   int E, int K, int normalize, void* logits, void* probs, void* scores,
+                   long long* indices, int* counts, int logits_given);
+
+/* ------------------------------------------------------------ permutation
+ * Expert-contiguous permutation of the T*K (token, slot) assignments.
+ * Within an expert, rows are ordered slot-major then by token, the order of
+ * torch.where(indices.T == e) in moe_serving/parallel_numerics.py:21-26 (and
+ * the native Transformers expert loop). Replaces that host loop and the
+ * sort/histc bookkeeping of moe_serving/efficient_kernels.py:244-253 and
+ * :160-178.
+ *
+ * indices: int64 [T,K] global expert ids. Outputs (int32): counts [E],
+ * offsets [E+1] (exclusive prefix of counts), perm_src [T*K] (permuted row
+ * -> t*K + k), inverse [T*K] (t*K + k -> permuted row, -1 if dropped).
+ * Ids outside [0,E) are dropped and flagged with B200MOE_STATUS_BAD_INDEX.
+ */
+int b200moe_permute_workspace(int T, int K, int E, size_t* bytes);
+int b200moe_permute(int device, void* stream, const long long* indices, int T, int K, int E,
+                    int* counts, int* offsets, int* perm_src, int* inverse, void* workspace,
+                    size_t workspace_bytes);
+
+/* ------------------------------------------------------------ grouped GEMM
+ * One launch computes, for every expert in [expert_begin, expert_begin +
+ * n_experts) and every permuted row of that expert, either
+ *   gated (planes = 2): act[r, f] = epilogue(x_r . Wgate[e,f], x_r . Wup[e,f])
+ *   down  (planes = 1): out[r, f] = epilogue(a_r . Wdown[e,f])
+ * on tcgen05 tensor cores (BF16 x BF16 -> FP32 in TMEM). Weights are stored
+ * per local expert as [n_experts][planes][feat_pad][k_pad] in one of:
+ *   B200MOE_W_BF16     bf16
+ *   B200MOE_W_FP8      e4m3 with fp32 block scales
+ *                      scale[n_experts][planes][sc_nbr][sc_nbc], block
+ *                      sc_br x sc_bc; dequantised in shared memory to
+ *                      bf16(fp32(w) * scale), the arithmetic of
+ *                      moe_serving/qwen3_parallel.py:48-53
+ *   B200MOE_W_MXFP4    e2m1 pairs (low nibble first), 16 bytes per 32
+ *                      values, ue8m0 scales [n_experts][planes][feat_pad]
+ *                      [k_pad/32]; decoded exactly to bf16 as
+ *                      transformers' _convert_moe_packed_tensors does
+ *                      (called at moe_serving/gpt_oss_parallel.py:183-193)
+ * Epilogues:
+ *   B200MOE_EPI_SWIGLU     bf16(bf16(silu(bf16 g)) * bf16 u)
+ *                          (moe_serving/qwen3_parallel.py:84-94)
+ *   B200MOE_EPI_CLAMP_SWIGLU  +bias, clamp(g<=limit, |u|<=limit),
+ *                          g*sigmoid(alpha g)*(u+1), bf16 after each op
+ *                          (moe_serving/gpt_oss_parallel.py:195-202)
+ *   B200MOE_EPI_DOWN       bf16(acc) (+bias, bf16), then optionally
+ *                          * routing weight of the row, bf16
+ *                          (gpt_oss_parallel.py:203-204,
+ *                          parallel_numerics.py:27)
+ * Replaces the per-expert loops of qwen3_parallel.py:84-118 and
+ * gpt_oss_parallel.py:195-244 and the grouped kernels called at
+ * efficient_kernels.py:255-269 and :188-205.
+ */
+#define B200MOE_W_BF16 0
+#define B200MOE_W_FP8 1
+#define B200MOE_W_MXFP4 2
+
+#define B200MOE_EPI_SWIGLU 0
+#define B200MOE_EPI_CLAMP_SWIGLU 1
+#define B200MOE_EPI_DOWN 2
+
+typedef struct b200moe_gemm_args {
+  /* rows */
+  const int* offsets;   /* [E_global + 1] permuted-row offsets (device) */
+  int expert_begin;     /* first global expert id handled by this launch */
+  int n_experts;        /* local experts in the weight stack */
+  int max_rows;         /* upper bound on rows of these experts (T*K) */
+  int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 */
+  int split_k;          /* 0 = choose; else 1..4 (cluster split of K) */
+  /* weights (A operand) */
+  int wfmt;             /* B200MOE_W_* */
+  int planes;           /* 2 = gated gate/up, 1 = single projection */
+  int feat_pad;         /* padded features per plane, multiple of 128 */
+  int n_feat;           /* valid features per plane */
+  int k_pad;            /* padded reduction length, multiple of 64 */
+  const void* weight;   /* device */
+  const float* fp8_scale;
+  int sc_br, sc_bc, sc_nbr, sc_nbc;
+  const unsigned char* mx_scale;
+  /* activations (B operand): row r reads b_src[src(r) * ldb + k], k < k_valid,
+     src(r) = b_map ? b_map[r] / b_div : r */
+  const void* b_src;
+  long long ldb;
+  int k_valid;
+  const int* b_map;
+  int b_div;
+  /* epilogue */
+  int epilogue;         /* B200MOE_EPI_* */
+  const void* bias;     /* bf16 [n_experts][planes][feat_pad] or NULL */
+  float alpha, limit;
+  const void* row_weight;   /* routing weights [T*K] (fp32 or bf16) or NULL */
+  int row_weight_bf16;
+  const int* row_src;       /* permuted row -> t*K + k (for row_weight) */
+  void* out;                /* bf16, row r at out + r * ldo */
+  long long ldo;
+} b200moe_gemm_args;
+
+int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* args);
+
+/* sizeof(b200moe_gemm_args), so foreign bindings can check their mirror. */
+size_t b200moe_gemm_args_size(void);
+
+/* ------------------------------------------------------------ combine
+ * out[t, :] = ordered bf16 sum over the slots k of token t of the
+ * contribution rows c[inverse[t*K+k], :], starting from bf16 zero and
+ * rounding to bf16 after every add (index_add_ on a bf16 tensor).
+ *   order B200MOE_ORDER_EXPERT: ascending global expert id — the order of
+ *     moe_serving/parallel_numerics.py:21-35 (ordered_expert_merge)
+ *   order B200MOE_ORDER_RANK_SLOT: ascending (expert / experts_per_rank,
+ *     slot) — the order of index_add_ over the dest-sorted rows at
+ *     moe_serving/moe.py:123-136
+ * Only experts in [expert_lo, expert_hi) are added (the rank-local partial
+ * sum of the reference's fast mode, qwen3_parallel.py:105-118).
+ * scale_rows != 0: the contribution is bf16(f32(c) * w[t*K+k]) (weights fp32
+ * or bf16); otherwise rows are already scaled (EPI_DOWN with row_weight).
+ */
+#define B200MOE_ORDER_EXPERT 0
+#define B200MOE_ORDER_RANK_SLOT 1
+
+int b200moe_combine(int device, void* stream, const void* rows, long long ld_rows,
+                    const int* inverse, const long long* indices, int T, int K, int H,
+                    int order, int experts_per_rank, int expert_lo, int expert_hi,
+                    int scale_rows, const void* weights, int weights_bf16, void* out,
+                    long long ld_out);
+
+/* ------------------------------------------------------------ row gather
+ * dst[i, :H] = src[map[i] / div, :H] for i < n (bf16 rows). The dispatch
+ * packing of moe_serving/moe.py:127 (hidden[token_index[order]]) and the
+ * un-permute of received rows.
+ */
+int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_src,
+                        const int* map, int div, int n, int H, void* dst, long long ld_dst);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

@@ -1,0 +1,144 @@
+"""ctypes binding of ``libb200moe.so`` (the C ABI in ``include/b200moe.h``).
+
+Importing this module loads the library; a missing library is an ImportError
+(there is no CPU implementation to fall back to). ``check`` turns a non-zero
+status into ValueError (bad argument), NotImplementedError (unsupported
+shape) or RuntimeError (CUDA failure), the reference's fail-fast convention
+(moe_serving/efficient_kernels.py:1-4).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_longlong, c_size_t, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libb200moe.so"
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+STATUS_WAIT_TIMEOUT, STATUS_BAD_TILE, STATUS_BAD_INDEX = 1, 2, 4
+
+ROUTER_QWEN3, ROUTER_GPT_OSS, ROUTER_NATIVE = 0, 1, 2
+W_BF16, W_FP8, W_MXFP4 = 0, 1, 2
+EPI_SWIGLU, EPI_CLAMP_SWIGLU, EPI_DOWN = 0, 1, 2
+ORDER_EXPERT, ORDER_RANK_SLOT = 0, 1
+
+EXPORTED = (
+    "b200moe_last_error",
+    "b200moe_version",
+    "b200moe_device_status",
+    "b200moe_router",
+    "b200moe_permute_workspace",
+    "b200moe_permute",
+    "b200moe_expert_gemm",
+    "b200moe_combine",
+    "b200moe_gather_rows",
+    "b200moe_gemm_args_size",
+)
+
+
+class GemmArgs(ctypes.Structure):
+    """Mirror of ``b200moe_gemm_args``."""
+
+    _fields_ = [
+        ("offsets", c_void_p),
+        ("expert_begin", c_int),
+        ("n_experts", c_int),
+        ("max_rows", c_int),
+        ("token_tile", c_int),
+        ("split_k", c_int),
+        ("wfmt", c_int),
+        ("planes", c_int),
+        ("feat_pad", c_int),
+        ("n_feat", c_int),
+        ("k_pad", c_int),
+        ("weight", c_void_p),
+        ("fp8_scale", c_void_p),
+        ("sc_br", c_int),
+        ("sc_bc", c_int),
+        ("sc_nbr", c_int),
+        ("sc_nbc", c_int),
+        ("mx_scale", c_void_p),
+        ("b_src", c_void_p),
+        ("ldb", c_longlong),
+        ("k_valid", c_int),
+        ("b_map", c_void_p),
+        ("b_div", c_int),
+        ("epilogue", c_int),
+        ("bias", c_void_p),
+        ("alpha", c_float),
+        ("limit", c_float),
+        ("row_weight", c_void_p),
+        ("row_weight_bf16", c_int),
+        ("row_src", c_void_p),
+        ("out", c_void_p),
+        ("ldo", c_longlong),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing; build it with `python -m moe_serving_profile_b200.build`"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    lib.b200moe_last_error.restype = c_char_p
+    lib.b200moe_last_error.argtypes = []
+    lib.b200moe_version.restype = c_char_p
+    lib.b200moe_version.argtypes = []
+    lib.b200moe_device_status.restype = c_int
+    lib.b200moe_device_status.argtypes = [c_int, c_int, POINTER(c_int)]
+    lib.b200moe_router.restype = c_int
+    lib.b200moe_router.argtypes = [
+        c_int, c_void_p, c_int, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int,
+        c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+    ]
+    lib.b200moe_permute_workspace.restype = c_int
+    lib.b200moe_permute_workspace.argtypes = [c_int, c_int, c_int, POINTER(c_size_t)]
+    lib.b200moe_permute.restype = c_int
+    lib.b200moe_permute.argtypes = [
+        c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_void_p, c_size_t,
+    ]
+    lib.b200moe_expert_gemm.restype = c_int
+    lib.b200moe_expert_gemm.argtypes = [c_int, c_void_p, POINTER(GemmArgs)]
+    lib.b200moe_gemm_args_size.restype = c_size_t
+    lib.b200moe_gemm_args_size.argtypes = []
+    if lib.b200moe_gemm_args_size() != ctypes.sizeof(GemmArgs):
+        raise ImportError("b200moe_gemm_args layout differs between the library and _lib.GemmArgs")
+    lib.b200moe_combine.restype = c_int
+    lib.b200moe_combine.argtypes = [
+        c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+        c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_longlong,
+    ]
+    lib.b200moe_gather_rows.restype = c_int
+    lib.b200moe_gather_rows.argtypes = [
+        c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int, c_int, c_void_p,
+        c_longlong,
+    ]
+    return lib
+
+
+lib = _load()
+
+
+def check(rc: int, what: str) -> None:
+    if rc == OK:
+        return
+    msg = f"{what}: {lib.b200moe_last_error().decode(errors='replace')}"
+    if rc == ERR_INVALID:
+        raise ValueError(msg)
+    if rc == ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)
+
+
+def version() -> str:
+    return lib.b200moe_version().decode()
+
+
+def device_status(device: int, clear: bool = True) -> int:
+    """Synchronise ``device`` and return (and clear) its kernel status bits."""
+    out = c_int(0)
+    check(lib.b200moe_device_status(device, int(clear), ctypes.byref(out)), "device_status")
+    return out.value

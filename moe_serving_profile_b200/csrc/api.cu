@@ -1,0 +1,408 @@
+// C ABI of the b200moe library: argument validation, launch shapes, TMA
+// descriptors and the per-device status word. See include/b200moe.h.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include <algorithm>
+
+#include "b200moe.h"
+#include "gemm_params.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+// One status word per device: kernels OR StatusBits into it.
+__device__ int g_b200moe_status;
+
+namespace {
+
+thread_local std::string t_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_error = buf;
+  return code;
+}
+
+#define B200_CUDA(expr)                                                                   \
+  do {                                                                                    \
+    cudaError_t e_ = (expr);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return fail(B200MOE_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));     \
+  } while (0)
+
+#define B200_CHECK(cond, ...)                                \
+  do {                                                       \
+    if (!(cond)) return fail(B200MOE_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+int* g_status_ptr[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
+bool g_gemm_attr[kMaxDevices] = {};
+
+int use_device(int device, int** status) {
+  B200_CHECK(device >= 0 && device < kMaxDevices, "device %d out of range", device);
+  B200_CUDA(cudaSetDevice(device));
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_status_ptr[device] == nullptr) {
+    void* p = nullptr;
+    B200_CUDA(cudaGetSymbolAddress(&p, g_b200moe_status));
+    g_status_ptr[device] = static_cast<int*>(p);
+    int sms = 0;
+    B200_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    g_sm_count[device] = sms;
+  }
+  if (status) *status = g_status_ptr[device];
+  return B200MOE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+int pow2_ceil(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b200moe_last_error(void) { return t_error.c_str(); }
+
+const char* b200moe_version(void) { return "b200moe 0.1 (sm_100a)"; }
+
+size_t b200moe_gemm_args_size(void) { return sizeof(b200moe_gemm_args); }
+
+int b200moe_device_status(int device, int clear, int* out_status) {
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CHECK(out_status != nullptr, "out_status is NULL");
+  B200_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  B200_CUDA(cudaMemcpy(&v, sp, sizeof(int), cudaMemcpyDeviceToHost));
+  *out_status = v;
+  if (clear) {
+    const int zero = 0;
+    B200_CUDA(cudaMemcpy(sp, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  return B200MOE_OK;
+}
+
+int b200moe_router(int device, void* stream, int mode, const void* hidden, long long ld_hidden,
+                   const void* weight, const void* bias, int T, int H, int E, int K,
+                   int normalize, void* logits, void* probs, void* scores, long long* indices,
+                   int* counts, int logits_given) {
+  B200_CHECK(mode >= B200MOE_ROUTER_QWEN3 && mode <= B200MOE_ROUTER_NATIVE, "bad router mode %d", mode);
+  B200_CHECK(T >= 0 && E >= 1 && K >= 1, "bad sizes T=%d E=%d K=%d", T, E, K);
+  if (E > 512 || K > 32 || K > E)
+    return fail(B200MOE_ERR_UNSUPPORTED, "router supports E <= 512 and K <= min(32, E) (E=%d K=%d)", E, K);
+  B200_CHECK(logits && scores && indices, "logits, scores and indices are required");
+  if (mode == B200MOE_ROUTER_GPT_OSS) B200_CHECK(bias != nullptr, "GPT-OSS router needs a bias");
+  if (!logits_given && T > 0) {
+    B200_CHECK(hidden && weight, "hidden and weight are required");
+    if (H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "router needs H %% 8 == 0 (H=%d)", H);
+    B200_CHECK(aligned16(hidden) && aligned16(weight) && ld_hidden % 8 == 0 && ld_hidden >= H,
+               "hidden/weight must be 16-byte aligned with ld %% 8 == 0");
+  }
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (counts) B200_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * E, st));
+  if (T == 0) return B200MOE_OK;
+  if (!logits_given) {
+    B200_CUDA(b200::launch_router_logits(st, mode, hidden, ld_hidden, weight,
+                                         mode == B200MOE_ROUTER_NATIVE ? nullptr : bias, T, H, E,
+                                         logits));
+  }
+  B200_CUDA(b200::launch_router_select(st, mode, logits, T, E, K, normalize,
+                                       mode == B200MOE_ROUTER_QWEN3 ? probs : nullptr, scores,
+                                       indices, counts));
+  return B200MOE_OK;
+}
+
+int b200moe_permute_workspace(int T, int K, int E, size_t* bytes) {
+  B200_CHECK(bytes != nullptr, "bytes is NULL");
+  B200_CHECK(T >= 0 && K >= 1 && E >= 1, "bad sizes");
+  *bytes = b200::permute_workspace_bytes(T, K, E);
+  return B200MOE_OK;
+}
+
+int b200moe_permute(int device, void* stream, const long long* indices, int T, int K, int E,
+                    int* counts, int* offsets, int* perm_src, int* inverse, void* workspace,
+                    size_t workspace_bytes) {
+  B200_CHECK(T >= 0 && K >= 1 && E >= 1, "bad sizes T=%d K=%d E=%d", T, K, E);
+  if (E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "permute supports E <= 1024 (E=%d)", E);
+  B200_CHECK((long long)T * K < (1ll << 30), "T*K too large");
+  B200_CHECK(counts && offsets, "counts and offsets are required");
+  const bool empty = (long long)T * K == 0;
+  const size_t need = b200::permute_workspace_bytes(T, K, E);
+  if (!empty) {
+    B200_CHECK(indices && perm_src && inverse, "indices, perm_src and inverse are required");
+    B200_CHECK(workspace_bytes >= need && (need == 0 || workspace != nullptr),
+               "permute workspace too small: %zu < %zu", workspace_bytes, need);
+  }
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (empty) {
+    B200_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * E, st));
+    B200_CUDA(cudaMemsetAsync(offsets, 0, sizeof(int) * (E + 1), st));
+    return B200MOE_OK;
+  }
+  B200_CUDA(b200::launch_permute(st, indices, T, K, E, counts, offsets, perm_src, inverse,
+                                 workspace, sp));
+  return B200MOE_OK;
+}
+
+int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
+  B200_CHECK(a != nullptr, "args is NULL");
+  B200_CHECK(a->offsets && a->weight && a->b_src && a->out, "offsets, weight, b_src, out are required");
+  B200_CHECK(a->wfmt >= B200MOE_W_BF16 && a->wfmt <= B200MOE_W_MXFP4, "bad weight format %d", a->wfmt);
+  B200_CHECK(a->planes == 1 || a->planes == 2, "planes must be 1 or 2");
+  B200_CHECK(a->epilogue >= B200MOE_EPI_SWIGLU && a->epilogue <= B200MOE_EPI_DOWN, "bad epilogue");
+  B200_CHECK((a->epilogue == B200MOE_EPI_DOWN) == (a->planes == 1),
+             "gated epilogues need planes == 2, the down epilogue planes == 1");
+  B200_CHECK(a->n_experts >= 1 && a->expert_begin >= 0, "bad expert range");
+  B200_CHECK(a->feat_pad >= 128 && a->feat_pad % 128 == 0, "feat_pad must be a positive multiple of 128");
+  B200_CHECK(a->n_feat >= 1 && a->n_feat <= a->feat_pad, "n_feat out of range");
+  B200_CHECK(a->k_pad >= 64 && a->k_pad % 64 == 0, "k_pad must be a positive multiple of 64");
+  B200_CHECK(a->k_valid >= 1 && a->k_valid <= a->k_pad && a->k_valid % 8 == 0,
+             "k_valid must be in [1, k_pad] and a multiple of 8");
+  B200_CHECK(a->ldb >= a->k_valid && a->ldb % 8 == 0 && aligned16(a->b_src), "B rows must be 16-byte aligned");
+  B200_CHECK(aligned16(a->weight), "weight must be 16-byte aligned");
+  B200_CHECK(a->ldo >= a->n_feat, "ldo too small");
+  B200_CHECK(a->b_map == nullptr || a->b_div >= 1, "b_div must be >= 1");
+  if (a->wfmt == B200MOE_W_FP8)
+    B200_CHECK(a->fp8_scale && a->sc_br >= 1 && a->sc_bc >= 16 && a->sc_bc % 16 == 0 &&
+                   a->sc_nbr >= 1 && a->sc_nbc >= 1,
+               "fp8 weights need scales with block cols a multiple of 16");
+  if (a->wfmt == B200MOE_W_MXFP4) B200_CHECK(a->mx_scale != nullptr, "mxfp4 weights need scales");
+  if (a->row_weight) B200_CHECK(a->row_src != nullptr, "row_weight needs row_src");
+  B200_CHECK(a->token_tile == 0 || a->token_tile == 16 || a->token_tile == 32 ||
+                 a->token_tile == 64 || a->token_tile == 128 || a->token_tile == 256,
+             "token_tile must be 0 or a power of two in [16, 256]");
+  B200_CHECK(a->split_k >= 0 && a->split_k <= 4, "split_k must be 0..4");
+  if (a->max_rows <= 0) return B200MOE_OK;
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+
+  const int nkb = a->k_pad / 64;
+  int bn = a->token_tile;
+  if (bn == 0) {
+    const int avg = (a->max_rows + a->n_experts - 1) / a->n_experts;
+    bn = std::min(256, std::max(16, pow2_ceil(avg)));
+  }
+  B200_CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256, "token_tile must be 16..256, power of 2");
+  B200_CHECK(a->planes * bn <= 512, "planes * token_tile exceeds TMEM columns");
+  const int feat_tiles = a->feat_pad / 128;
+  const int max_tiles = std::min(a->n_experts, a->max_rows) + a->max_rows / bn;
+  int ks = a->split_k;
+  if (ks == 0) {
+    const int items = std::min(a->n_experts, a->max_rows) * feat_tiles;
+    ks = std::max(1, std::min(4, g_sm_count[device] / std::max(1, items)));
+  }
+  ks = std::min(ks, nkb);
+  B200_CHECK(ks >= 1 && ks <= 4, "split_k must be 1..4");
+  B200_CHECK(max_tiles <= 65535, "too many token tiles (%d)", max_tiles);
+
+  // shared memory plan
+  const uint32_t rpb = a->wfmt == B200MOE_W_FP8 ? 128u * 64u : (a->wfmt == B200MOE_W_MXFP4 ? 128u * 32u : 0u);
+  const uint32_t a_stage = 128u * 128u * a->planes;
+  const uint32_t b_stage = static_cast<uint32_t>(bn) * 128u;
+  const uint32_t red = ks > 1 ? static_cast<uint32_t>((ks - 1) * a->planes * bn * 512) : 0u;
+  const uint32_t budget = 232448u - 2048u;
+  int nr = rpb ? 4 : 0, na = 3, nb = 4;
+  auto total = [&](int r_, int a_, int b_) {
+    return r_ * rpb * a->planes + a_ * a_stage + b_ * b_stage + red + 1024u;
+  };
+  const int steps[][3] = {{0, -1, 0}, {-1, 0, 0}, {0, 0, -1}, {-1, 0, 0}, {0, 0, -1}};
+  for (const auto& s : steps) {
+    if (total(nr, na, nb) <= budget) break;
+    if (rpb == 0 && s[0] != 0) continue;
+    nr += s[0];
+    na += s[1];
+    nb += s[2];
+  }
+  if (total(nr, na, nb) > budget)
+    return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (bn=%d ks=%d)", bn, ks);
+
+  b200::GemmParams p{};
+  p.offsets = a->offsets;
+  p.expert_begin = a->expert_begin;
+  p.n_experts = a->n_experts;
+  p.bn = bn;
+  p.ks = ks;
+  p.feat_tiles = feat_tiles;
+  p.wfmt = a->wfmt;
+  p.planes = a->planes;
+  p.feat_pad = a->feat_pad;
+  p.n_feat = a->n_feat;
+  p.k_pad = a->k_pad;
+  p.nkb = nkb;
+  p.fp8_scale = a->fp8_scale;
+  p.sc_br = a->sc_br;
+  p.sc_bc = a->sc_bc;
+  p.sc_nbr = a->sc_nbr;
+  p.sc_nbc = a->sc_nbc;
+  p.mx_scale = a->mx_scale;
+  p.mx_groups = a->k_pad / 32;
+  p.b_src = static_cast<const __nv_bfloat16*>(a->b_src);
+  p.ldb = a->ldb;
+  p.k_valid = a->k_valid;
+  p.b_map = a->b_map;
+  p.b_div = a->b_map ? a->b_div : 1;
+  p.epi = a->epilogue;
+  p.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  p.alpha = a->alpha;
+  p.limit = a->limit;
+  p.row_w = a->row_weight;
+  p.row_w_bf16 = a->row_weight_bf16;
+  p.row_src = a->row_src;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.ldo = a->ldo;
+  p.status = sp;
+  p.nr = nr;
+  p.na = na;
+  p.nb = nb;
+  uint32_t off = 0;
+  p.raw_off = off;
+  off += nr * rpb * a->planes;
+  p.a_off = off;
+  off += na * a_stage;
+  p.b_off = off;
+  off += nb * b_stage;
+  p.red_off = off;
+  off += red;
+  p.bar_off = off;
+  off += 1024u;
+  const uint32_t smem = off + 1024u;  // + alignment slack
+  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(a->planes * bn)));
+
+  // weight tensor map
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap map;
+  const cuuint64_t rows = static_cast<cuuint64_t>(a->n_experts) * a->planes * a->feat_pad;
+  cuuint64_t dims[2];
+  cuuint64_t strides[1];
+  cuuint32_t box[2];
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType dt;
+  CUtensorMapSwizzle sw;
+  if (a->wfmt == B200MOE_W_BF16) {
+    dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    dims[0] = a->k_pad;
+    strides[0] = static_cast<cuuint64_t>(a->k_pad) * 2;
+    box[0] = 64;
+    sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  } else if (a->wfmt == B200MOE_W_FP8) {
+    dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    dims[0] = a->k_pad;
+    strides[0] = a->k_pad;
+    box[0] = 64;
+    sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  } else {
+    dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    dims[0] = a->k_pad / 2;
+    strides[0] = a->k_pad / 2;
+    box[0] = 32;
+    sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  }
+  dims[1] = rows;
+  box[1] = 128;
+  CUresult cr = enc(&map, dt, 2, const_cast<void*>(a->weight), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
+
+  const void* kern = b200::gemm_kernel_ptr();
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_gemm_attr[device]) {
+      B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024));
+      g_gemm_attr[device] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(feat_tiles * ks, max_tiles, 1);
+  cfg.blockDim = dim3(384, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  if (ks > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  void* args[] = {&map, &p};
+  B200_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
+  return B200MOE_OK;
+}
+
+int b200moe_combine(int device, void* stream, const void* rows, long long ld_rows,
+                    const int* inverse, const long long* indices, int T, int K, int H, int order,
+                    int experts_per_rank, int expert_lo, int expert_hi, int scale_rows,
+                    const void* weights, int weights_bf16, void* out, long long ld_out) {
+  B200_CHECK(T >= 0 && K >= 1 && H >= 8, "bad sizes");
+  if (K > 32 || H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "combine needs K <= 32 and H %% 8 == 0");
+  B200_CHECK(order == B200MOE_ORDER_EXPERT || order == B200MOE_ORDER_RANK_SLOT, "bad order");
+  B200_CHECK(order == B200MOE_ORDER_EXPERT || experts_per_rank >= 1, "experts_per_rank must be >= 1");
+  B200_CHECK(out && inverse && indices, "out, inverse and indices are required");
+  B200_CHECK(rows || T == 0, "rows is required");
+  B200_CHECK(!scale_rows || weights, "scale_rows needs weights");
+  B200_CHECK(aligned16(rows) && aligned16(out) && ld_rows % 8 == 0 && ld_out % 8 == 0,
+             "rows/out must be 16-byte aligned with ld %% 8 == 0");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_combine(static_cast<cudaStream_t>(stream), rows, ld_rows, inverse, indices,
+                                 T, K, H, order, experts_per_rank, expert_lo, expert_hi, scale_rows,
+                                 weights, weights_bf16, out, ld_out));
+  return B200MOE_OK;
+}
+
+int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_src,
+                        const int* map, int div, int n, int H, void* dst, long long ld_dst) {
+  B200_CHECK(n >= 0 && H >= 8 && div >= 1, "bad sizes");
+  if (H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "gather_rows needs H %% 8 == 0");
+  B200_CHECK(n == 0 || (src && map && dst), "src, map and dst are required");
+  B200_CHECK(aligned16(src) && aligned16(dst) && ld_src % 8 == 0 && ld_dst % 8 == 0,
+             "rows must be 16-byte aligned with ld %% 8 == 0");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_gather_rows(static_cast<cudaStream_t>(stream), src, ld_src, map, div, n, H,
+                                     dst, ld_dst));
+  return B200MOE_OK;
+}
+
+}  // extern "C"

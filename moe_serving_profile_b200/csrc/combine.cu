@@ -1,0 +1,115 @@
+// Ordered combine: out[t] = bf16 running sum of the token's contribution rows
+// in a fixed expert order, rounding to bf16 after every add (the arithmetic
+// of index_add_ on a bf16 tensor, one expert at a time). Deterministic, no
+// atomics: one CTA per token, 16-byte vectors per thread.
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kMaxK = 32;
+
+__global__ void __launch_bounds__(128) combine_kernel(
+    const __nv_bfloat16* __restrict__ rows, long long ld_rows, const int* __restrict__ inverse,
+    const long long* __restrict__ indices, int T, int K, int H, int order, int epr, int lo,
+    int hi, int scale_rows, const void* __restrict__ weights, int weights_bf16,
+    __nv_bfloat16* __restrict__ out, long long ld_out) {
+  const int t = blockIdx.x;
+  // Gather and order the token's contributions (redundantly per thread; K is small).
+  int rsel[kMaxK];
+  long long key[kMaxK];
+  float wsel[kMaxK];
+  int n = 0;
+  for (int k = 0; k < K; ++k) {
+    const long long e = indices[(long long)t * K + k];
+    const int r = inverse[(long long)t * K + k];
+    if (r < 0 || e < lo || e >= hi) continue;
+    long long kk = (order == 0) ? e * kMaxK + k : (e / epr) * kMaxK + k;
+    float wv = 1.f;
+    if (scale_rows) {
+      wv = weights_bf16
+               ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(weights)[(long long)t * K + k])
+               : reinterpret_cast<const float*>(weights)[(long long)t * K + k];
+    }
+    // insertion sort by key (stable; keys are distinct)
+    int p = n++;
+    while (p > 0 && key[p - 1] > kk) {
+      key[p] = key[p - 1];
+      rsel[p] = rsel[p - 1];
+      wsel[p] = wsel[p - 1];
+      --p;
+    }
+    key[p] = kk;
+    rsel[p] = r;
+    wsel[p] = wv;
+  }
+  const int nvec = H >> 3;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(rows + rsel[i] * ld_rows) + v);
+      const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float c0 = __uint_as_float(wd[j] << 16);
+        float c1 = __uint_as_float(wd[j] & 0xffff0000u);
+        if (scale_rows) {
+          c0 = bf16r(c0 * wsel[i]);
+          c1 = bf16r(c1 * wsel[i]);
+        }
+        acc[2 * j] = bf16r(acc[2 * j] + c0);
+        acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * ld_out)[v] = o;
+  }
+}
+
+__global__ void __launch_bounds__(128) gather_rows_kernel(const __nv_bfloat16* __restrict__ src,
+                                                           long long ld_src,
+                                                           const int* __restrict__ map, int div,
+                                                           int n, int H,
+                                                           __nv_bfloat16* __restrict__ dst,
+                                                           long long ld_dst) {
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  const long long s = map[i] / div;
+  const int nvec = H >> 3;
+  const uint4* a = reinterpret_cast<const uint4*>(src + s * ld_src);
+  uint4* b = reinterpret_cast<uint4*>(dst + i * ld_dst);
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) b[v] = __ldg(a + v);
+}
+
+}  // namespace
+
+cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
+                           const int* inverse, const long long* indices, int T, int K, int H,
+                           int order, int experts_per_rank, int expert_lo, int expert_hi,
+                           int scale_rows, const void* weights, int weights_bf16, void* out,
+                           long long ld_out) {
+  if (T == 0) return cudaSuccess;
+  combine_kernel<<<T, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(rows), ld_rows, inverse,
+                                    indices, T, K, H, order, experts_per_rank, expert_lo,
+                                    expert_hi, scale_rows, weights, weights_bf16,
+                                    static_cast<__nv_bfloat16*>(out), ld_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(cudaStream_t st, const void* src, long long ld_src,
+                               const int* map, int div, int n, int H, void* dst,
+                               long long ld_dst) {
+  if (n == 0) return cudaSuccess;
+  gather_rows_kernel<<<n, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(src), ld_src, map,
+                                        div, n, H, static_cast<__nv_bfloat16*>(dst), ld_dst);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

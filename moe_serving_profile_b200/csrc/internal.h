@@ -1,0 +1,33 @@
+// Launchers shared between the kernel translation units and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200 {
+
+// Returns a cudaError_t from the launch (cudaSuccess if enqueued).
+cudaError_t launch_router_logits(cudaStream_t st, int mode, const void* hidden, long long ldx,
+                                 const void* weight, const void* bias, int T, int H, int E,
+                                 void* logits);
+cudaError_t launch_router_select(cudaStream_t st, int mode, const void* logits, int T, int E,
+                                 int K, int normalize, void* probs, void* scores,
+                                 long long* indices, int* counts);
+
+size_t permute_workspace_bytes(int T, int K, int E);
+cudaError_t launch_permute(cudaStream_t st, const long long* indices, int T, int K, int E,
+                           int* counts, int* offsets, int* perm_src, int* inverse,
+                           void* workspace, int* status);
+
+cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
+                           const int* inverse, const long long* indices, int T, int K, int H,
+                           int order, int experts_per_rank, int expert_lo, int expert_hi,
+                           int scale_rows, const void* weights, int weights_bf16, void* out,
+                           long long ld_out);
+
+cudaError_t launch_gather_rows(cudaStream_t st, const void* src, long long ld_src,
+                               const int* map, int div, int n, int H, void* dst,
+                               long long ld_dst);
+
+}  // namespace b200

@@ -1,0 +1,153 @@
+"""The expert layer pipeline on one GPU: permute -> gate/up GEMM -> down GEMM.
+
+``run_experts`` computes, for the experts of one rank, the contribution row
+``bf16(bf16(y) * w)`` of every (token, slot) routed to them, in the global
+permuted row order (expert-major, then slot, then token). The caller combines
+the rows (``ops.combine``) after any expert-parallel exchange.
+
+Launch shapes (token tile, cluster split of K) come from ``tile_policy``,
+which depends only on T, K, the global expert count and the weight shape —
+not on the expert-parallel size — so a token's expert outputs are bitwise the
+same whether its experts run on 1 or 8 GPUs.
+"""
+
+from __future__ import annotations
+
+import math
+from functools import lru_cache
+
+import torch
+
+from moe_serving_profile_b200 import _lib, ops
+from moe_serving_profile_b200.layout import ExpertWeights
+
+
+@lru_cache(maxsize=None)
+def _sm_count(device: int) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
+
+
+def tile_policy(T: int, K: int, num_experts: int, feat_tiles: int, k_blocks: int,
+                sm_count: int) -> tuple[int, int]:
+    """(token_tile, split_k) for one grouped GEMM launch."""
+    rows = max(1.0, T * K / num_experts)
+    bn = 16
+    while bn < 256 and bn < rows:
+        bn *= 2
+    used = num_experts * (1.0 - (1.0 - K / num_experts) ** T)
+    tiles_per_expert = max(1, math.ceil(rows / bn))
+    items = max(1, round(used)) * tiles_per_expert * feat_tiles
+    ks = max(1, min(4, k_blocks, sm_count // items))
+    return bn, ks
+
+
+def run_experts(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
+                weights: torch.Tensor | None, *, K: int, num_experts: int, expert_begin: int,
+                contrib: torch.Tensor | None = None, b_map_div: int | None = None) -> torch.Tensor:
+    """Contribution rows [T*K, H] (rows of other ranks' experts are left as given).
+
+    ``hidden`` rows are gathered through ``perm.perm_src // K``; ``weights``
+    ([T, K], fp32 or bf16) scale the down projection's rows, or are skipped
+    when None (the token all-to-all path scales at combine time).
+    """
+    T, H = hidden.shape
+    if H != w.hidden:
+        raise ValueError(f"hidden size {H} does not match the experts' {w.hidden}")
+    act = gate_up(w, hidden, perm, K=K, num_experts=num_experts, expert_begin=expert_begin,
+                  b_map_div=b_map_div, tokens=T)
+    return down(w, act, perm, weights, K=K, num_experts=num_experts, expert_begin=expert_begin,
+                contrib=contrib, tokens=T)
+
+
+def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K: int,
+            num_experts: int, expert_begin: int, b_map_div: int | None = None,
+            tokens: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gated projection of every routed row: act [T*K, I_p] bf16."""
+    T = hidden.shape[0] if tokens is None else tokens
+    R = perm.perm_src.numel()
+    dev = hidden.device
+    bn, ks = tile_policy(T, K, num_experts, w.i_pad // 128, w.h_k // 64, _sm_count(dev.index))
+    act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16) if out is None else out
+    ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
+                    max_rows=R, wfmt=w.fmt, planes=2, feat_pad=w.i_pad, n_feat=w.inter,
+                    k_pad=w.h_k, weight=w.w1,
+                    fp8_scale=w.s1 if w.fmt == _lib.W_FP8 else None, fp8_block=w.block,
+                    mx_scale=w.s1 if w.fmt == _lib.W_MXFP4 else None, b_src=hidden,
+                    k_valid=hidden.shape[1], b_map=perm.perm_src,
+                    b_div=K if b_map_div is None else b_map_div, epilogue=w.gated_epilogue,
+                    bias=w.b1, alpha=w.alpha, limit=w.limit, out=act, token_tile=bn, split_k=ks)
+    return act
+
+
+def down(w: ExpertWeights, act: torch.Tensor, perm: ops.Permutation,
+         weights: torch.Tensor | None, *, K: int, num_experts: int, expert_begin: int,
+         contrib: torch.Tensor | None = None, tokens: int) -> torch.Tensor:
+    """Down projection of the gated rows, scaled by the routing weights."""
+    R = perm.perm_src.numel()
+    dev = act.device
+    bn, ks = tile_policy(tokens, K, num_experts, w.h_f // 128, w.i_pad // 64, _sm_count(dev.index))
+    if contrib is None:
+        contrib = torch.empty(R, w.hidden, device=dev, dtype=torch.bfloat16)
+    ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
+                    max_rows=R, wfmt=w.fmt, planes=1, feat_pad=w.h_f, n_feat=w.hidden,
+                    k_pad=w.i_pad, weight=w.w2,
+                    fp8_scale=w.s2 if w.fmt == _lib.W_FP8 else None, fp8_block=w.block,
+                    mx_scale=w.s2 if w.fmt == _lib.W_MXFP4 else None, b_src=act,
+                    k_valid=w.inter, epilogue=_lib.EPI_DOWN, bias=w.b2,
+                    row_weight=None if weights is None else weights.reshape(-1),
+                    row_src=perm.perm_src, out=contrib, token_tile=bn, split_k=ks)
+    return contrib
+
+
+def check_inputs(hidden: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor) -> tuple:
+    if hidden.dtype != torch.bfloat16:
+        raise ValueError(f"b200 experts compute in bfloat16, got hidden {hidden.dtype}")
+    if hidden.dim() != 2:
+        raise ValueError("hidden must be [tokens, hidden]")
+    if hidden.stride(1) != 1 or hidden.stride(0) % 8:
+        hidden = hidden.contiguous()
+    indices = indices.to(torch.int64).contiguous()
+    weights = weights.contiguous()
+    if weights.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"routing weights must be float32 or bfloat16, got {weights.dtype}")
+    if indices.shape != weights.shape or indices.shape[0] != hidden.shape[0]:
+        raise ValueError("indices / routing weights / hidden shapes disagree")
+    return hidden, indices, weights
+
+
+def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
+                  weights: torch.Tensor, *, num_experts: int, expert_begin: int,
+                  parallel=None, numerics: str = "reference") -> torch.Tensor:
+    """Replicated-token expert layer: the reference's ``ParallelExperts.forward``.
+
+    numerics "reference": contributions of all experts reach every rank and
+    are combined in ascending global expert order (bitwise independent of the
+    EP size, the contract of moe_serving/parallel_numerics.py:13-36).
+    numerics "fast": each rank combines its own experts and the partial sums
+    are all-reduced (moe_serving/qwen3_parallel.py:105-118).
+    """
+    hidden, indices, weights = check_inputs(hidden, indices, weights)
+    T, K = indices.shape
+    if T == 0:
+        return torch.empty_like(hidden)
+    perm = ops.permute(indices, num_experts)
+    size = 1 if parallel is None else parallel.size
+    if size == 1:
+        contrib = run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
+                              expert_begin=expert_begin)
+        return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
+    if numerics == "reference":
+        # Rows of other ranks' experts start at zero, so a SUM all-reduce is an
+        # exact gather of every expert's contribution rows.
+        contrib = torch.zeros(T * K, hidden.shape[1], device=hidden.device, dtype=torch.bfloat16)
+        run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
+                    expert_begin=expert_begin, contrib=contrib)
+        parallel.reduce(contrib)
+        return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
+    if numerics == "fast":
+        contrib = run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
+                              expert_begin=expert_begin)
+        partial = ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT,
+                              expert_lo=expert_begin, expert_hi=expert_begin + w.n_experts)
+        return parallel.reduce(partial)
+    raise ValueError(f"numerics must be reference or fast, got {numerics!r}")

@@ -1,0 +1,217 @@
+"""Torch-facing wrappers of the b200moe C ABI.
+
+Each function takes CUDA tensors, allocates its outputs with torch's caching
+allocator and enqueues the kernels on the current stream of the tensors'
+device. Nothing here synchronises the host. Tensors on any other device are
+rejected: the library has no CPU implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from moe_serving_profile_b200 import _lib
+from moe_serving_profile_b200._lib import check, lib
+
+
+def _dev(t: torch.Tensor, what: str) -> int:
+    if not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor (b200moe has no CPU path), got {t.device}")
+    return t.device.index
+
+
+def _stream(device: int) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _bf16_rows(t: torch.Tensor, what: str) -> None:
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{what} must be bfloat16, got {t.dtype}")
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{what} must be a 2D tensor with contiguous rows")
+
+
+# --------------------------------------------------------------------------- router
+@dataclass
+class RouterOut:
+    logits: torch.Tensor     # bf16 [T,E] (qwen3 / gpt_oss) or fp32 [T,E] (native)
+    probs: torch.Tensor | None   # fp32 [T,E] (qwen3)
+    scores: torch.Tensor     # fp32 [T,K] (qwen3) or bf16 [T,K]
+    indices: torch.Tensor    # int64 [T,K]
+    counts: torch.Tensor     # int32 [E]
+
+
+def router(mode: int, hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+           top_k: int, normalize: bool, logits: torch.Tensor | None = None) -> RouterOut:
+    """Fused router; with ``logits`` given, only the selection stage runs."""
+    device = _dev(weight if logits is None else logits, "router input")
+    E = weight.shape[0] if weight is not None else logits.shape[1]
+    if logits is None:
+        _bf16_rows(hidden, "hidden")
+        _bf16_rows(weight, "router weight")
+        if not weight.is_contiguous():
+            raise ValueError("router weight must be contiguous")
+        T, H = hidden.shape
+        if weight.shape[1] != H:
+            raise ValueError(f"router weight {tuple(weight.shape)} does not match hidden size {H}")
+        ldt = torch.float32 if mode == _lib.ROUTER_NATIVE else torch.bfloat16
+        logits_t = torch.empty(T, E, device=hidden.device, dtype=ldt)
+        given = 0
+    else:
+        T, H = logits.shape[0], 0
+        want = torch.float32 if mode == _lib.ROUTER_NATIVE else torch.bfloat16
+        if logits.dtype != want or not logits.is_contiguous():
+            raise ValueError(f"logits must be contiguous {want}")
+        logits_t = logits
+        given = 1
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or not bias.is_contiguous():
+            raise ValueError("router bias must be contiguous bfloat16")
+    dev = logits_t.device
+    probs = torch.empty(T, E, device=dev, dtype=torch.float32) if mode == _lib.ROUTER_QWEN3 else None
+    sdt = torch.float32 if mode == _lib.ROUTER_QWEN3 else torch.bfloat16
+    scores = torch.empty(T, top_k, device=dev, dtype=sdt)
+    indices = torch.empty(T, top_k, device=dev, dtype=torch.int64)
+    counts = torch.empty(E, device=dev, dtype=torch.int32)
+    check(
+        lib.b200moe_router(
+            device, _stream(device), mode,
+            _ptr(hidden) if given == 0 else None, hidden.stride(0) if given == 0 else 0,
+            _ptr(weight) if given == 0 else None, _ptr(bias),
+            T, H, E, top_k, int(normalize),
+            _ptr(logits_t), _ptr(probs), _ptr(scores), _ptr(indices), _ptr(counts), given,
+        ),
+        "router",
+    )
+    return RouterOut(logits_t, probs, scores, indices, counts)
+
+
+# --------------------------------------------------------------------------- permutation
+@dataclass
+class Permutation:
+    counts: torch.Tensor     # int32 [E]
+    offsets: torch.Tensor    # int32 [E+1]
+    perm_src: torch.Tensor   # int32 [T*K]: permuted row -> t*K + k
+    inverse: torch.Tensor    # int32 [T*K]: t*K + k -> permuted row (-1 dropped)
+
+
+def permute(indices: torch.Tensor, num_experts: int) -> Permutation:
+    device = _dev(indices, "indices")
+    if indices.dtype != torch.int64 or indices.dim() != 2 or not indices.is_contiguous():
+        raise ValueError("indices must be a contiguous int64 [T, K] tensor")
+    T, K = indices.shape
+    dev = indices.device
+    counts = torch.empty(num_experts, device=dev, dtype=torch.int32)
+    offsets = torch.empty(num_experts + 1, device=dev, dtype=torch.int32)
+    perm_src = torch.empty(T * K, device=dev, dtype=torch.int32)
+    inverse = torch.empty(T * K, device=dev, dtype=torch.int32)
+    nbytes = ctypes.c_size_t(0)
+    check(lib.b200moe_permute_workspace(T, K, num_experts, ctypes.byref(nbytes)), "permute_workspace")
+    ws = torch.empty(max(nbytes.value, 1), device=dev, dtype=torch.uint8)
+    check(
+        lib.b200moe_permute(
+            device, _stream(device), _ptr(indices), T, K, num_experts, _ptr(counts), _ptr(offsets),
+            _ptr(perm_src), _ptr(inverse), _ptr(ws), nbytes.value,
+        ),
+        "permute",
+    )
+    return Permutation(counts, offsets, perm_src, inverse)
+
+
+# --------------------------------------------------------------------------- grouped GEMM
+def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max_rows: int,
+                wfmt: int, planes: int, feat_pad: int, n_feat: int, k_pad: int,
+                weight: torch.Tensor, fp8_scale: torch.Tensor | None = None,
+                fp8_block: tuple[int, int] = (128, 128), mx_scale: torch.Tensor | None = None,
+                b_src: torch.Tensor, k_valid: int, b_map: torch.Tensor | None = None,
+                b_div: int = 1, epilogue: int, bias: torch.Tensor | None = None,
+                alpha: float = 1.702, limit: float = 7.0, row_weight: torch.Tensor | None = None,
+                row_src: torch.Tensor | None = None, out: torch.Tensor,
+                token_tile: int = 0, split_k: int = 0) -> torch.Tensor:
+    device = _dev(weight, "weight")
+    _bf16_rows(b_src, "activations")
+    _bf16_rows(out, "output")
+    a = _lib.GemmArgs()
+    a.offsets = _ptr(offsets)
+    a.expert_begin = expert_begin
+    a.n_experts = n_experts
+    a.max_rows = max_rows
+    a.token_tile = token_tile
+    a.split_k = split_k
+    a.wfmt = wfmt
+    a.planes = planes
+    a.feat_pad = feat_pad
+    a.n_feat = n_feat
+    a.k_pad = k_pad
+    a.weight = _ptr(weight)
+    if fp8_scale is not None:
+        a.fp8_scale = _ptr(fp8_scale)
+        a.sc_br, a.sc_bc = fp8_block
+        a.sc_nbr, a.sc_nbc = fp8_scale.shape[-2], fp8_scale.shape[-1]
+    a.mx_scale = _ptr(mx_scale)
+    a.b_src = _ptr(b_src)
+    a.ldb = b_src.stride(0)
+    a.k_valid = k_valid
+    a.b_map = _ptr(b_map)
+    a.b_div = b_div
+    a.epilogue = epilogue
+    a.bias = _ptr(bias)
+    a.alpha = alpha
+    a.limit = limit
+    if row_weight is not None:
+        a.row_weight = _ptr(row_weight)
+        a.row_weight_bf16 = int(row_weight.dtype == torch.bfloat16)
+        a.row_src = _ptr(row_src)
+    a.out = _ptr(out)
+    a.ldo = out.stride(0)
+    check(lib.b200moe_expert_gemm(device, _stream(device), ctypes.byref(a)), "expert_gemm")
+    return out
+
+
+# --------------------------------------------------------------------------- combine
+def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *, order: int,
+            experts_per_rank: int = 1, expert_lo: int = 0, expert_hi: int = 1 << 30,
+            weights: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    device = _dev(indices, "indices")
+    T, K = indices.shape
+    H = rows.shape[1]
+    _bf16_rows(rows, "contribution rows")
+    if out is None:
+        out = torch.empty(T, H, device=indices.device, dtype=torch.bfloat16)
+    _bf16_rows(out, "output")
+    wbf16 = int(weights is not None and weights.dtype == torch.bfloat16)
+    check(
+        lib.b200moe_combine(
+            device, _stream(device), _ptr(rows), rows.stride(0), _ptr(inverse), _ptr(indices),
+            T, K, H, order, experts_per_rank, expert_lo, expert_hi, int(weights is not None),
+            _ptr(weights), wbf16, _ptr(out), out.stride(0),
+        ),
+        "combine",
+    )
+    return out
+
+
+def gather_rows(src: torch.Tensor, index_map: torch.Tensor, div: int = 1,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[i] = src[index_map[i] // div] for bf16 rows."""
+    device = _dev(src, "src")
+    _bf16_rows(src, "src")
+    n = index_map.numel()
+    H = src.shape[1]
+    if out is None:
+        out = torch.empty(n, H, device=src.device, dtype=torch.bfloat16)
+    check(
+        lib.b200moe_gather_rows(
+            device, _stream(device), _ptr(src), src.stride(0), _ptr(index_map), div, n, H,
+            _ptr(out), out.stride(0),
+        ),
+        "gather_rows",
+    )
+    return out

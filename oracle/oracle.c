@@ -1,0 +1,230 @@
+/*
+ * CPU oracle — TEST INFRASTRUCTURE ONLY. Only tests/, __graft_entry__.smoke()
+ * and bench.py's CPU-baseline leg may load this library, and only as the
+ * checker; the product path (moe_serving_profile_b200) never does.
+ *
+ * Plain-C restatement of the exact (integer / bit-level) stages of the
+ * reference MoE expert layer (luoshuqing2001/MoE_Serving_Profile):
+ *   - bf16 round-to-nearest-even, e4m3 and e2m1/ue8m0 decoding
+ *   - block-scaled FP8 dequantisation     moe_serving/qwen3_parallel.py:48-53
+ *   - MXFP4 decoding (transformers' _convert_moe_packed_tensors, called at
+ *     moe_serving/gpt_oss_parallel.py:183-193; transformers 5.5.0
+ *     integrations/mxfp4.py:279-330 is the readable proxy)
+ *   - router logits in the library's documented fixed fp32 order, and the
+ *     top-k selection (value descending, ties by ascending expert id)
+ *   - the expert-contiguous permutation in (slot, token) order
+ *     (moe_serving/parallel_numerics.py:21-26)
+ *   - the ordered bf16 combine (parallel_numerics.py:26-35; moe.py:123-136)
+ * Compile with -ffp-contract=off so every float operation rounds as written.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+static float u2f(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+static uint32_t f2u(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+/* float -> bf16 bits, round to nearest even; NaN stays a quiet NaN */
+uint16_t oracle_f32_to_bf16(float f) {
+  uint32_t u = f2u(f);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return (uint16_t)((u >> 16) | 0x40);
+  uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7fffu + lsb;
+  return (uint16_t)(u >> 16);
+}
+float oracle_bf16_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
+static float bf16r(float f) { return oracle_bf16_to_f32(oracle_f32_to_bf16(f)); }
+
+/* e4m3fn: 1 sign, 4 exponent (bias 7), 3 mantissa; 0x7f/0xff are NaN, no inf */
+float oracle_e4m3_to_f32(uint8_t v) {
+  const uint32_t s = v >> 7, e = (v >> 3) & 15u, m = v & 7u;
+  float mag;
+  if (e == 15u && m == 7u) return NAN;
+  if (e == 0u)
+    mag = ldexpf((float)m, -9); /* subnormal: m/8 * 2^-6 */
+  else
+    mag = ldexpf(1.0f + (float)m / 8.0f, (int)e - 7);
+  return s ? -mag : mag;
+}
+
+/* bf16(fp32(w) * scale[r/br][c/bc]) for w e4m3 [rows, cols] */
+void oracle_dequant_fp8(const uint8_t* w, const float* scales, int rows, int cols, int br,
+                        int bc, uint16_t* out) {
+  const int nbc = (cols + bc - 1) / bc;
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < cols; ++c) {
+      const float s = scales[(r / br) * nbc + c / bc];
+      out[(long)r * cols + c] = oracle_f32_to_bf16(oracle_e4m3_to_f32(w[(long)r * cols + c]) * s);
+    }
+}
+
+static const float kE2M1[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,  4.0f,  6.0f,
+                                -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+/* 2^(s - 127) as an fp32 value (s = 0 is the subnormal 2^-127, s = 255 +inf) */
+static float ue8m0(uint8_t s) {
+  if (s == 0) return u2f(0x00400000u);
+  if (s == 255) return u2f(0x7f800000u);
+  return u2f((uint32_t)s << 23);
+}
+
+/* blocks [rows, G, 16] bytes (low nibble = even element), scales [rows, G]
+   -> bf16 [rows, G * 32] (row-major, before the reference's transpose) */
+void oracle_decode_mxfp4(const uint8_t* blocks, const uint8_t* scales, int rows, int G,
+                         uint16_t* out) {
+  for (long r = 0; r < rows; ++r)
+    for (int g = 0; g < G; ++g) {
+      const float sc = ue8m0(scales[r * G + g]);
+      for (int b = 0; b < 16; ++b) {
+        const uint8_t byte = blocks[(r * G + g) * 16 + b];
+        const long o = r * (long)G * 32 + g * 32 + 2 * b;
+        out[o] = oracle_f32_to_bf16(kE2M1[byte & 15] * sc);
+        out[o + 1] = oracle_f32_to_bf16(kE2M1[byte >> 4] * sc);
+      }
+    }
+}
+
+/* Fixed-order fp32 dot product of two bf16 vectors of length H (H % 8 == 0):
+   vector v = h/8 goes to partial v % 32, accumulated in increasing h with
+   fmaf; partials combined pairwise with offsets 16, 8, 4, 2, 1. */
+float oracle_dot_bf16(const uint16_t* x, const uint16_t* w, int H) {
+  float p[32];
+  for (int i = 0; i < 32; ++i) p[i] = 0.0f;
+  for (int v = 0; v < H / 8; ++v)
+    for (int j = 0; j < 8; ++j) {
+      const int h = v * 8 + j;
+      p[v % 32] = fmaf(oracle_bf16_to_f32(x[h]), oracle_bf16_to_f32(w[h]), p[v % 32]);
+    }
+  for (int o = 16; o >= 1; o >>= 1) {
+    float q[32];
+    for (int i = 0; i < 32; ++i) q[i] = p[i] + p[i ^ o];
+    memcpy(p, q, sizeof(p));
+  }
+  return p[0];
+}
+
+/* mode 0: bf16 logits, mode 1: bf16 logits with bias (bf16 [E]), mode 2: fp32.
+   Output as float (holding the bf16 value for modes 0, 1). */
+void oracle_router_logits(const uint16_t* x, long ldx, const uint16_t* w, const uint16_t* bias,
+                          int T, int H, int E, int mode, float* logits) {
+  for (int t = 0; t < T; ++t)
+    for (int e = 0; e < E; ++e) {
+      float acc = oracle_dot_bf16(x + (long)t * ldx, w + (long)e * H, H);
+      if (mode == 2) {
+        logits[(long)t * E + e] = acc;
+      } else {
+        if (mode == 1) acc += oracle_bf16_to_f32(bias[e]);
+        logits[(long)t * E + e] = bf16r(acc);
+      }
+    }
+}
+
+static int greater(float a, int ia, float b, int ib) {
+  /* NaN sorts above every number; equal values by ascending index */
+  const int na = a != a, nb = b != b;
+  if (na || nb) {
+    if (na && nb) return ia < ib;
+    return na;
+  }
+  if (a != b) return a > b;
+  return ia < ib;
+}
+
+/* top-k of each row of values [T, E]: value descending, ties by index */
+void oracle_topk(const float* values, int T, int E, int K, int64_t* indices) {
+  char* taken = (char*)malloc((size_t)E);
+  for (int t = 0; t < T; ++t) {
+    memset(taken, 0, (size_t)E);
+    const float* row = values + (long)t * E;
+    for (int k = 0; k < K; ++k) {
+      int best = -1;
+      for (int e = 0; e < E; ++e) {
+        if (taken[e]) continue;
+        if (best < 0 || greater(row[e], e, row[best], best)) best = e;
+      }
+      taken[best] = 1;
+      indices[(long)t * K + k] = best;
+    }
+  }
+  free(taken);
+}
+
+/* Stable counting sort of the assignments in slot-major order. Ids outside
+   [0, E) are dropped (inverse = -1). Returns the number of placed rows. */
+int oracle_permute(const int64_t* idx, int T, int K, int E, int32_t* counts, int32_t* offsets,
+                   int32_t* perm_src, int32_t* inverse) {
+  memset(counts, 0, sizeof(int32_t) * (size_t)E);
+  for (long j = 0; j < (long)T * K; ++j) {
+    const int64_t e = idx[j];
+    if (e >= 0 && e < E) counts[e]++;
+  }
+  offsets[0] = 0;
+  for (int e = 0; e < E; ++e) offsets[e + 1] = offsets[e] + counts[e];
+  int32_t* run = (int32_t*)malloc(sizeof(int32_t) * (size_t)E);
+  memcpy(run, offsets, sizeof(int32_t) * (size_t)E);
+  for (int k = 0; k < K; ++k)
+    for (int t = 0; t < T; ++t) {
+      const long src = (long)t * K + k;
+      const int64_t e = idx[src];
+      if (e < 0 || e >= E) {
+        inverse[src] = -1;
+        continue;
+      }
+      const int pos = run[e]++;
+      perm_src[pos] = (int32_t)src;
+      inverse[src] = pos;
+    }
+  free(run);
+  return offsets[E];
+}
+
+/* Ordered combine; order 0: ascending expert id, order 1: ascending
+   (expert / epr, slot). scale: contribution = bf16(f32(row) * w). */
+void oracle_combine(const uint16_t* rows, long ld_rows, const int32_t* inverse,
+                    const int64_t* idx, int T, int K, int H, int order, int epr, int64_t lo,
+                    int64_t hi, int scale, const float* weights, uint16_t* out) {
+  int* sel = (int*)malloc(sizeof(int) * (size_t)K);
+  int64_t* key = (int64_t*)malloc(sizeof(int64_t) * (size_t)K);
+  float* acc = (float*)malloc(sizeof(float) * (size_t)H);
+  for (int t = 0; t < T; ++t) {
+    int n = 0;
+    for (int k = 0; k < K; ++k) {
+      const int64_t e = idx[(long)t * K + k];
+      const int r = inverse[(long)t * K + k];
+      if (r < 0 || e < lo || e >= hi) continue;
+      const int64_t kk = order == 0 ? e * 64 + k : (e / epr) * 64 + k;
+      int p = n++;
+      while (p > 0 && key[p - 1] > kk) {
+        key[p] = key[p - 1];
+        sel[p] = sel[p - 1];
+        --p;
+      }
+      key[p] = kk;
+      sel[p] = k;
+    }
+    for (int h = 0; h < H; ++h) acc[h] = 0.0f;
+    for (int i = 0; i < n; ++i) {
+      const int k = sel[i];
+      const int r = inverse[(long)t * K + k];
+      const float wv = scale ? weights[(long)t * K + k] : 1.0f;
+      for (int h = 0; h < H; ++h) {
+        float c = oracle_bf16_to_f32(rows[(long)r * ld_rows + h]);
+        if (scale) c = bf16r(c * wv);
+        acc[h] = bf16r(acc[h] + c);
+      }
+    }
+    for (int h = 0; h < H; ++h) out[(long)t * H + h] = oracle_f32_to_bf16(acc[h]);
+  }
+  free(sel);
+  free(key);
+  free(acc);
+}

@@ -1,0 +1,284 @@
+"""Kernel-level parity on the GPU, called through the C ABI (ops wrappers).
+
+Integer and ordering stages are compared bit-exactly with the C oracle.
+The grouped GEMM is checked bit-exactly on integer-valued data (every fp32
+partial sum is exact, so any summation order gives the same result) across
+token tiles and cluster split-K, and its dequantisers are probed exactly with
+one-hot activations.
+"""
+
+import pytest
+import torch
+
+from moe_serving_profile_b200 import _lib, ops
+from moe_serving_profile_b200 import synthetic as S
+from oracle import oracle
+from tests.conftest import tie_free_rows
+
+pytestmark = pytest.mark.gpu
+
+
+def _status_clean(dev):
+    assert _lib.device_status(dev.index) == 0
+
+
+# ------------------------------------------------------------------ router
+@pytest.mark.parametrize("T,H,E,K", [(1, 2048, 128, 8), (64, 2048, 128, 8), (4096, 2048, 128, 8),
+                                     (64, 256, 8, 2), (13, 4096, 128, 8)])
+def test_qwen_router_bit_exact(cuda, T, H, E, K):
+    g = torch.Generator().manual_seed(T + H)
+    x = torch.randn(T, H, generator=g).bfloat16()
+    w = (torch.randn(E, H, generator=g) * 0.02).bfloat16()
+    out = ops.router(_lib.ROUTER_QWEN3, x.to(cuda), w.to(cuda), None, K, True)
+    ref_logits = oracle.router_logits(x, w, None, 0)
+    assert torch.equal(out.logits.float().cpu(), ref_logits)
+    assert torch.equal(out.indices.cpu(), oracle.topk(ref_logits, K))
+    # probabilities / scores against torch's softmax of the same logits
+    probs = torch.softmax(ref_logits, dim=-1)
+    assert torch.allclose(out.probs.cpu(), probs, rtol=2e-6, atol=1e-9)
+    top = torch.gather(probs, 1, out.indices.cpu())
+    assert torch.allclose(out.scores.cpu(), top / top.sum(-1, keepdim=True), rtol=4e-6, atol=1e-9)
+    assert torch.equal(out.counts.cpu().long(), torch.bincount(out.indices.cpu().flatten(), minlength=E))
+    # the reference's own router (torch GEMM + topk on CUDA): equal on tie-free rows
+    probs_t, scores_t, idx_t, logits_t = oracle.qwen_router(x.to(cuda), w.to(cuda), K, True)
+    same_logits = (logits_t.cpu() == out.logits.cpu()).all(-1)
+    free = tie_free_rows(probs_t, K) & same_logits
+    assert torch.equal(out.indices.cpu()[free], idx_t.cpu()[free])
+    print(f"\nT={T}: {int(free.sum())}/{T} rows tie-free with identical logits")
+    _status_clean(cuda)
+
+
+@pytest.mark.parametrize("T", [1, 16, 64, 2048])
+def test_gpt_oss_router_bit_exact(cuda, T):
+    H, E, K = 2880, 32, 4
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, H, generator=g).bfloat16()
+    w = (torch.randn(E, H, generator=g) * 0.02).bfloat16()
+    b = (torch.randn(E, generator=g) * 0.01).bfloat16()
+    out = ops.router(_lib.ROUTER_GPT_OSS, x.to(cuda), w.to(cuda), b.to(cuda), K, False)
+    ref_logits = oracle.router_logits(x, w, b, 1)
+    assert torch.equal(out.logits.float().cpu(), ref_logits)
+    assert torch.equal(out.indices.cpu(), oracle.topk(ref_logits, K))
+    top = torch.gather(ref_logits, 1, out.indices.cpu())
+    want = torch.softmax(top, dim=1).to(torch.bfloat16)
+    assert (out.scores.cpu().float() - want.float()).abs().max() <= 2 ** -8
+    _status_clean(cuda)
+
+
+def test_native_router_bit_exact(cuda):
+    T, H, E, K = 37, 512, 16, 3
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(T, H, generator=g).bfloat16()
+    w = (torch.randn(E, H, generator=g) * 0.05).bfloat16()
+    out = ops.router(_lib.ROUTER_NATIVE, x.to(cuda), w.to(cuda), None, K, True)
+    ref = oracle.router_logits(x, w, None, 2)
+    assert torch.equal(out.logits.cpu(), ref)
+    assert torch.equal(out.indices.cpu(), oracle.topk(ref, K))
+    p = torch.softmax(ref, -1)
+    top = torch.gather(p, 1, out.indices.cpu())
+    want = (top / top.sum(-1, keepdim=True).clamp_min(1e-20)).to(torch.bfloat16)
+    assert (out.scores.cpu().float() - want.float()).abs().max() <= 2 ** -8
+
+
+def test_router_selection_on_given_logits_and_ties(cuda):
+    """Selection alone on caller logits (the torch GEMM's): bit-exact with the
+    documented rule (value descending, ties by ascending expert id), including
+    rows made of exact ties."""
+    T, E, K = 512, 128, 8
+    g = torch.Generator().manual_seed(3)
+    logits = (torch.randn(T, E, generator=g) * 0.9).bfloat16()
+    logits[:64] = logits[:64, :16].repeat(1, 8)         # each value 8 times
+    logits[64:72] = 0.0                                  # all tied
+    out = ops.router(_lib.ROUTER_QWEN3, None, None, None, K, True, logits=logits.to(cuda))
+    assert torch.equal(out.indices.cpu(), oracle.topk(logits.float(), K))
+    assert torch.equal(out.indices.cpu()[64], torch.arange(K))
+    # record CUDA torch.topk's tie order next to ours (informational)
+    t_idx = torch.topk(torch.softmax(logits.to(cuda), -1, dtype=torch.float), K).indices.cpu()
+    free = tie_free_rows(logits, K)
+    assert torch.equal(t_idx[free], out.indices.cpu()[free])
+    sets_equal = (t_idx.sort(-1).values == out.indices.cpu().sort(-1).values).all(-1)
+    print(f"\ntorch.cuda topk on tie rows: same expert set in {int(sets_equal[~free].sum())}/"
+          f"{int((~free).sum())}; same slot order in "
+          f"{int((t_idx == out.indices.cpu()).all(-1)[~free].sum())}")
+
+
+# ------------------------------------------------------------------ permutation
+@pytest.mark.parametrize("T,K,E", [(1, 8, 128), (13, 2, 4), (64, 8, 128), (1023, 8, 128),
+                                   (4096, 8, 128), (16384, 8, 128), (2048, 4, 32), (8192, 4, 128),
+                                   (3000, 3, 1000)])
+def test_permute_bit_exact(cuda, T, K, E):
+    g = torch.Generator().manual_seed(T * K + E)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).long()
+    p = ops.permute(idx.to(cuda), E)
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    assert torch.equal(p.counts.cpu(), counts) and torch.equal(p.offsets.cpu(), offsets)
+    assert torch.equal(p.perm_src.cpu(), perm) and torch.equal(p.inverse.cpu(), inv)
+    _status_clean(cuda)
+
+
+def test_permute_skewed_and_invalid_ids(cuda):
+    T, K, E = 5000, 8, 64
+    g = torch.Generator().manual_seed(11)
+    idx = torch.randint(0, 4, (T, K), generator=g)       # heavy skew, repeated ids
+    idx[7, 3] = E + 5
+    idx[100, 0] = -1
+    p = ops.permute(idx.to(cuda), E)
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    n = int(offsets[-1])
+    assert torch.equal(p.counts.cpu(), counts) and torch.equal(p.offsets.cpu(), offsets)
+    assert torch.equal(p.perm_src.cpu()[:n], perm[:n]) and torch.equal(p.inverse.cpu(), inv)
+    assert _lib.device_status(cuda.index) & _lib.STATUS_BAD_INDEX
+
+
+def test_permute_empty(cuda):
+    p = ops.permute(torch.empty(0, 8, dtype=torch.int64, device=cuda), 128)
+    assert int(p.offsets[-1]) == 0 and int(p.counts.sum()) == 0
+
+
+# ------------------------------------------------------------------ combine / gather
+@pytest.mark.parametrize("order", [0, 1])
+@pytest.mark.parametrize("scale", [False, True])
+def test_combine_bit_exact(cuda, order, scale):
+    T, K, E, H = 777, 8, 128, 2880
+    g = torch.Generator().manual_seed(5 + order)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).long()
+    rows = torch.randn(T * K, H, generator=g).bfloat16()
+    wts = torch.rand(T, K, generator=g)
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    lo, hi = (16, 80) if scale else (0, E)
+    out = ops.combine(rows.to(cuda), inv.to(cuda), idx.to(cuda), order=order, experts_per_rank=16,
+                      expert_lo=lo, expert_hi=hi, weights=wts.to(cuda) if scale else None)
+    ref = oracle.combine(rows, inv, idx, order=order, experts_per_rank=16, lo=lo, hi=hi,
+                         weights=wts if scale else None)
+    assert torch.equal(out.cpu(), ref)
+
+
+def test_gather_rows_exact(cuda):
+    src = torch.randn(50, 2048).bfloat16()
+    m = torch.randint(0, 400, (333,), dtype=torch.int32)
+    out = ops.gather_rows(src.to(cuda), m.to(cuda), div=8)
+    assert torch.equal(out.cpu(), src[(m // 8).long()])
+
+
+# ------------------------------------------------------------------ grouped GEMM, exact integer data
+def _int_case(fmt, E, feat, K, T, topk, seed):
+    """Integer-valued weights / activations: all fp32 partial sums exact."""
+    g = torch.Generator().manual_seed(seed)
+    if fmt == _lib.W_FP8:
+        wv = torch.randint(-8, 9, (E, feat, K), generator=g).float()
+    elif fmt == _lib.W_MXFP4:
+        codes = torch.randint(0, 16, (E, feat, K), generator=g)
+        lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6])
+        wv = lut[codes] * 2.0                           # scale 2^1 (ue8m0 128)
+    else:
+        wv = torch.randint(-8, 9, (E, feat, K), generator=g).float()
+    x = torch.randint(-3, 4, (T, K), generator=g).float()
+    idx = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).long()
+    return g, wv, x, idx
+
+
+def _pack_weight(fmt, wv):
+    E, feat, K = wv.shape
+    Fp, Kp = -(-feat // 128) * 128, -(-K // 64) * 64
+    if fmt == _lib.W_FP8:
+        w = torch.zeros(E, Fp, Kp, dtype=torch.uint8)
+        w[:, :feat, :K] = wv.to(torch.float8_e4m3fn).view(torch.uint8)
+        scale = torch.ones(E, -(-feat // 128), -(-K // 128))
+        return w, scale, None
+    if fmt == _lib.W_MXFP4:
+        w = torch.zeros(E, Fp, Kp // 2, dtype=torch.uint8)
+        b, s = S.quantize_mxfp4(torch.nn.functional.pad(wv, (0, Kp - K)).reshape(-1, Kp))
+        w[:, :feat] = b.reshape(E, feat, Kp // 2)
+        sc = torch.full((E, Fp, Kp // 32), 127, dtype=torch.uint8)
+        sc[:, :feat] = s.reshape(E, feat, Kp // 32)
+        return w, None, sc
+    w = torch.zeros(E, Fp, Kp, dtype=torch.bfloat16)
+    w[:, :feat, :K] = wv.bfloat16()
+    return w, None, None
+
+
+@pytest.mark.parametrize("fmt", [_lib.W_FP8, _lib.W_MXFP4, _lib.W_BF16])
+@pytest.mark.parametrize("tile,split", [(16, 1), (16, 3), (32, 2), (64, 1), (128, 4), (256, 1), (0, 0)])
+def test_down_gemm_integer_exact(cuda, fmt, tile, split):
+    E, feat, K, T, topk = 6, 300, 448, 150, 3
+    g, wv, x, idx = _int_case(fmt, E, feat, K, T, topk, seed=fmt * 10 + tile + split)
+    w, scale, mx = _pack_weight(fmt, wv)
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    R = T * topk
+    act = torch.zeros(R, -(-K // 64) * 64).bfloat16()
+    act[:, :K] = x[(perm // topk).long()].bfloat16()
+    out = torch.zeros(R, feat, dtype=torch.bfloat16, device=cuda)
+    ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R, wfmt=fmt,
+                    planes=1, feat_pad=w.shape[1], n_feat=feat, k_pad=act.shape[1],
+                    weight=w.to(cuda), fp8_scale=None if scale is None else scale.to(cuda),
+                    mx_scale=None if mx is None else mx.to(cuda), b_src=act.to(cuda), k_valid=K,
+                    epilogue=_lib.EPI_DOWN, out=out, token_tile=tile, split_k=split)
+    # exact result: y[r, f] = sum_k act[r, k] * w[e(r), f, k]
+    e_of_row = torch.repeat_interleave(torch.arange(E), counts.long())
+    ref = torch.einsum("rk,rfk->rf", act[:, :K].double(), wv.double()[e_of_row]).to(torch.bfloat16)
+    assert torch.equal(out.cpu(), ref)
+    _status_clean(cuda)
+
+
+@pytest.mark.parametrize("fmt", [_lib.W_FP8, _lib.W_BF16])
+@pytest.mark.parametrize("tile,split", [(16, 2), (64, 1), (256, 1)])
+def test_gated_gemm_integer_exact(cuda, fmt, tile, split):
+    """Gate/up planes with exact pre-activations; SwiGLU epilogue vs torch."""
+    E, inter, H, T, topk = 5, 200, 320, 97, 2
+    g, wv, x, idx = _int_case(fmt, E, 2 * inter, H, T, topk, seed=99 + tile)
+    w2, sc2, _ = _pack_weight(fmt, wv.reshape(E, 2, inter, H).reshape(E * 2, inter, H))
+    Ip = w2.shape[1]
+    w = w2.reshape(E, 2, Ip, w2.shape[2])
+    scale = None if sc2 is None else sc2.reshape(E, 2, sc2.shape[1], sc2.shape[2])
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    R = T * topk
+    out = torch.zeros(R, Ip, dtype=torch.bfloat16, device=cuda)
+    xb = x.bfloat16()
+    ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R, wfmt=fmt,
+                    planes=2, feat_pad=Ip, n_feat=inter, k_pad=w.shape[3], weight=w.to(cuda),
+                    fp8_scale=None if scale is None else scale.to(cuda), b_src=xb.to(cuda), k_valid=H,
+                    b_map=perm.to(cuda), b_div=topk, epilogue=_lib.EPI_SWIGLU, out=out,
+                    token_tile=tile, split_k=split)
+    e_of_row = torch.repeat_interleave(torch.arange(E), counts.long())
+    xr = x[(perm // topk).long()].double()
+    pre = torch.einsum("rk,rfk->rf", xr, wv.double()[e_of_row])       # [R, 2I] exact
+    gate, up = pre[:, :inter].bfloat16(), pre[:, inter:].bfloat16()
+    ref = (torch.nn.functional.silu(gate) * up)                          # torch bf16 semantics
+    got = out.cpu()[:, :inter]
+    mism = (got != ref)
+    assert float(mism.float().mean()) < 1e-3
+    assert float((got.float() - ref.float()).abs().max()) <= float(ref.float().abs().max()) * 2 ** -7
+    _status_clean(cuda)
+
+
+# ------------------------------------------------------------------ dequantisers, exact
+@pytest.mark.parametrize("storage", ["fp8", "mxfp4"])
+def test_dequant_exact_via_one_hot(cuda, storage):
+    """With one-hot activation rows the down GEMM outputs single dequantised
+    weights, which must equal the oracle's bit for bit."""
+    H, I, E = 256, 192, 2
+    if storage == "fp8":
+        cfg = S.LayerConfig("probe", "qwen3", H, E, 1, I, "fp8", (1,))
+        wq = S.make_qwen(cfg, seed=5)
+        w = oracle.dequant_fp8(wq.down[1], wq.down_scale[1], (128, 128))         # [H, I]
+        from moe_serving_profile_b200.layout import fp8_experts
+        lay = fp8_experts(wq.gate, wq.gate_scale, wq.up, wq.up_scale, wq.down, wq.down_scale, (128, 128))
+        fmt, w2, s2, mx2 = _lib.W_FP8, lay.w2, lay.s2, None
+    else:
+        cfg = S.LayerConfig("probe", "gpt_oss", H, E, 1, I, "mxfp4", (1,))
+        wg = S.make_gpt_oss(cfg, seed=6)
+        w = oracle.decode_mxfp4(wg.dn_blocks[1], wg.dn_scales[1])                 # [H, I]
+        from moe_serving_profile_b200.layout import gpt_oss_mxfp4_experts
+        lay = gpt_oss_mxfp4_experts(wg.gu_blocks, wg.gu_scales, wg.gu_bias, wg.dn_blocks, wg.dn_scales,
+                                    wg.dn_bias, 1.702, 7.0)
+        fmt, w2, s2, mx2 = _lib.W_MXFP4, lay.w2, None, lay.s2
+    R = I                                                  # one row per reduction index, expert 1
+    act = torch.zeros(R, lay.i_pad, dtype=torch.bfloat16)
+    act[torch.arange(I), torch.arange(I)] = 1.0
+    offsets = torch.tensor([0, 0, R], dtype=torch.int32)
+    out = torch.zeros(R, H, dtype=torch.bfloat16, device=cuda)
+    ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R, wfmt=fmt,
+                    planes=1, feat_pad=lay.h_f, n_feat=H, k_pad=lay.i_pad, weight=w2.to(cuda),
+                    fp8_scale=None if s2 is None else s2.to(cuda), mx_scale=None if mx2 is None else mx2.to(cuda),
+                    b_src=act.to(cuda), k_valid=I, epilogue=_lib.EPI_DOWN, out=out)
+    assert torch.equal(out.cpu(), w.T.contiguous())
