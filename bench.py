@@ -71,7 +71,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -145,9 +145,11 @@ def layer_call(cfg, router, packed, x, parallel, rank, ep):
                            numerics="reference")
 
 
-def kernel_launches(T: int, K: int) -> int:
-    """Our kernels per layer call: router (2) + permute (1 or 3) + 2 GEMMs + combine."""
-    return 2 + (1 if T * K <= 8192 else 3) + 2 + 1
+def kernel_launches(T: int, K: int, E: int) -> int:
+    """Our kernels per layer call: router (2) + permute (1 or 3) + row gather
+    (large token tiles only) + 2 GEMMs + combine."""
+    gather = 1 if X.tile_policy(T, K, E) >= 64 else 0
+    return 2 + (1 if T * K <= 8192 else 3) + gather + 2 + 1
 
 
 # --------------------------------------------------------------------------- CPU leg
@@ -225,6 +227,19 @@ def reference_arm(args, cfg):
 
 
 # --------------------------------------------------------------------------- GPU arm
+def profile_calls(args, cfg):
+    """Three eager layer calls per batch size, nothing timed (an ncu target)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    router, packed = build_layer(cfg, dev, 1, 0)
+    for T in (args.tokens or cfg.batches):
+        x = S.make_hidden(T, cfg.hidden, seed=1000 + T, device=dev)
+        for _ in range(3):
+            layer_call(cfg, router, packed, x, None, 0, 1)
+        torch.cuda.synchronize(dev)
+    assert _lib.device_status(0) == 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -233,10 +248,15 @@ def main():
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--workload", default="qwen3-30b-a3b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="eager layer calls only (for ncu): 3 calls per --tokens batch")
+    ap.add_argument("--tokens", type=int, nargs="*", default=None)
     args = ap.parse_args()
     cfg = S.CONFIGS[args.workload]
     if args.impl == "reference":
         return reference_arm(args, cfg)
+    if args.profile:
+        return profile_calls(args, cfg)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -283,14 +303,19 @@ def main():
                 times[T] = (s, e)
         return times
 
-    for _ in range(max(3, args.warmup)):
-        step(False)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
     per_batch_ms = {T: 0.0 for T in batches}
     with ClockSampler(local) as clocks:
+        # warm-up (at least W steps and ~0.5 s, so the clock sampler sees load)
+        t0 = time.perf_counter()
+        n = 0
+        # (ranks > 1 run a fixed count: every rank must replay the same collectives)
+        while n < max(3, args.warmup) or (world == 1 and time.perf_counter() - t0 < 0.5):
+            step(False)
+            torch.cuda.synchronize(dev)
+            n += 1
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
         recs = [step(True) for _ in range(args.steps)]
         torch.cuda.synchronize(dev)
     if world > 1:
@@ -395,7 +420,7 @@ def main():
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
                "kind": "port", "sample": f"reference numerics on host CPU: {sample}"}
 
-    launches = args.steps * sum(kernel_launches(T, cfg.top_k) for T in batches)
+    launches = args.steps * sum(kernel_launches(T, cfg.top_k, cfg.experts) for T in batches)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,

@@ -105,7 +105,9 @@ int b200moe_permute(int device, void* stream, const long long* indices, int T, i
  * n_experts) and every permuted row of that expert, either
  *   gated (planes = 2): act[r, f] = epilogue(x_r . Wgate[e,f], x_r . Wup[e,f])
  *   down  (planes = 1): out[r, f] = epilogue(a_r . Wdown[e,f])
- * on tcgen05 tensor cores (BF16 x BF16 -> FP32 in TMEM). Weights are stored
+ * on tcgen05 tensor cores (BF16 x BF16 -> FP32 in TMEM) by a persistent
+ * kernel (one CTA per SM looping over (expert, token tile, feature tile)
+ * tiles; gated tiles cover 64 features, down tiles 128). Weights are stored
  * per local expert as [n_experts][planes][feat_pad][k_pad] in one of:
  *   B200MOE_W_BF16     bf16
  *   B200MOE_W_FP8      e4m3 with fp32 block scales
@@ -147,7 +149,7 @@ typedef struct b200moe_gemm_args {
   int n_experts;        /* local experts in the weight stack */
   int max_rows;         /* upper bound on rows of these experts (T*K) */
   int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 */
-  int split_k;          /* 0 = choose; else 1..4 (cluster split of K) */
+  int split_k;          /* reserved: must be 0 or 1 */
   /* weights (A operand) */
   int wfmt;             /* B200MOE_W_* */
   int planes;           /* 2 = gated gate/up, 1 = single projection */
@@ -162,6 +164,7 @@ typedef struct b200moe_gemm_args {
      src(r) = b_map ? b_map[r] / b_div : r */
   const void* b_src;
   long long ldb;
+  int b_rows;           /* rows of b_src (tokens T, or T*K permuted rows) */
   int k_valid;
   const int* b_map;
   int b_div;

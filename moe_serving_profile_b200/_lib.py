@@ -61,6 +61,7 @@ class GemmArgs(ctypes.Structure):
         ("mx_scale", c_void_p),
         ("b_src", c_void_p),
         ("ldb", c_longlong),
+        ("b_rows", c_int),
         ("k_valid", c_int),
         ("b_map", c_void_p),
         ("b_div", c_int),

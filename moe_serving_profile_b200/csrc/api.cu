@@ -190,14 +190,18 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   B200_CHECK((a->epilogue == B200MOE_EPI_DOWN) == (a->planes == 1),
              "gated epilogues need planes == 2, the down epilogue planes == 1");
   B200_CHECK(a->n_experts >= 1 && a->expert_begin >= 0, "bad expert range");
+  if (a->n_experts > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "at most 1024 experts per launch");
   B200_CHECK(a->feat_pad >= 128 && a->feat_pad % 128 == 0, "feat_pad must be a positive multiple of 128");
   B200_CHECK(a->n_feat >= 1 && a->n_feat <= a->feat_pad, "n_feat out of range");
   B200_CHECK(a->k_pad >= 64 && a->k_pad % 64 == 0, "k_pad must be a positive multiple of 64");
   B200_CHECK(a->k_valid >= 1 && a->k_valid <= a->k_pad && a->k_valid % 8 == 0,
              "k_valid must be in [1, k_pad] and a multiple of 8");
   B200_CHECK(a->ldb >= a->k_valid && a->ldb % 8 == 0 && aligned16(a->b_src), "B rows must be 16-byte aligned");
+  B200_CHECK(a->b_rows >= 1, "b_rows must be positive");
   B200_CHECK(aligned16(a->weight), "weight must be 16-byte aligned");
   B200_CHECK(a->ldo >= a->n_feat, "ldo too small");
+  B200_CHECK(a->ldo % 8 == 0 && a->n_feat % 8 == 0 && aligned16(a->out),
+             "output rows must be 16-byte aligned (ldo %% 8 == 0, n_feat %% 8 == 0)");
   B200_CHECK(a->b_map == nullptr || a->b_div >= 1, "b_div must be >= 1");
   if (a->wfmt == B200MOE_W_FP8)
     B200_CHECK(a->fp8_scale && a->sc_br >= 1 && a->sc_bc >= 16 && a->sc_bc % 16 == 0 &&
@@ -208,65 +212,64 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   B200_CHECK(a->token_tile == 0 || a->token_tile == 16 || a->token_tile == 32 ||
                  a->token_tile == 64 || a->token_tile == 128 || a->token_tile == 256,
              "token_tile must be 0 or a power of two in [16, 256]");
-  B200_CHECK(a->split_k >= 0 && a->split_k <= 4, "split_k must be 0..4");
+  if (a->split_k > 1) return fail(B200MOE_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
+  B200_CHECK(a->split_k >= 0, "split_k must be 0 or 1");
   if (a->max_rows <= 0) return B200MOE_OK;
   int* sp = nullptr;
   int rc = use_device(device, &sp);
   if (rc) return rc;
 
-  const int nkb = a->k_pad / 64;
+  const bool gated = a->planes == 2;
   int bn = a->token_tile;
   if (bn == 0) {
     const int avg = (a->max_rows + a->n_experts - 1) / a->n_experts;
     bn = std::min(256, std::max(16, pow2_ceil(avg)));
   }
-  B200_CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256, "token_tile must be 16..256, power of 2");
-  B200_CHECK(a->planes * bn <= 512, "planes * token_tile exceeds TMEM columns");
-  const int feat_tiles = a->feat_pad / 128;
-  const int max_tiles = std::min(a->n_experts, a->max_rows) + a->max_rows / bn;
-  int ks = a->split_k;
-  if (ks == 0) {
-    const int items = std::min(a->n_experts, a->max_rows) * feat_tiles;
-    ks = std::max(1, std::min(4, g_sm_count[device] / std::max(1, items)));
-  }
-  ks = std::min(ks, nkb);
-  B200_CHECK(ks >= 1 && ks <= 4, "split_k must be 1..4");
-  B200_CHECK(max_tiles <= 65535, "too many token tiles (%d)", max_tiles);
+  const int feat_tile = gated ? 64 : 128;
+  const int feat_tiles = a->feat_pad / feat_tile;
+  const long long tiles_ub =
+      (long long)(std::min(a->n_experts, a->max_rows) + a->max_rows / bn) * feat_tiles;
 
-  // shared memory plan
+  // shared memory plan: raw weight ring, bf16 A ring, token-row ring, epilogue
+  // exchange buffer, barriers + tile prefix
   const uint32_t rpb = a->wfmt == B200MOE_W_FP8 ? 128u * 64u : (a->wfmt == B200MOE_W_MXFP4 ? 128u * 32u : 0u);
-  const uint32_t a_stage = 128u * 128u * a->planes;
+  const uint32_t a_stage = 128u * 128u;
   const uint32_t b_stage = static_cast<uint32_t>(bn) * 128u;
-  const uint32_t red = ks > 1 ? static_cast<uint32_t>((ks - 1) * a->planes * bn * 512) : 0u;
+  // epilogue: exchange buffer (8 KB), two bf16 staging chunks (8 KB), row weights (1 KB)
+  const uint32_t xbytes = 8192u + 8192u + 1024u;
+  const uint32_t barbytes = (((64u * 8u + 16u + 4u * (a->n_experts + 1)) + 1023u) / 1024u) * 1024u;
   const uint32_t budget = 232448u - 2048u;
-  int nr = rpb ? 4 : 0, na = 3, nb = 4;
-  auto total = [&](int r_, int a_, int b_) {
-    return r_ * rpb * a->planes + a_ * a_stage + b_ * b_stage + red + 1024u;
+  // One ring of na weight stages (raw bytes of quantised formats + the bf16
+  // A tile; stage s is drained by dequantiser warp s, so na <= 8) and a ring
+  // of nb token-row stages.
+  int na = 8, nb = 6;
+  auto total = [&](int a_, int b_) {
+    return a_ * (rpb + a_stage) + b_ * b_stage + xbytes + barbytes;
   };
-  const int steps[][3] = {{0, -1, 0}, {-1, 0, 0}, {0, 0, -1}, {-1, 0, 0}, {0, 0, -1}};
-  for (const auto& s : steps) {
-    if (total(nr, na, nb) <= budget) break;
-    if (rpb == 0 && s[0] != 0) continue;
-    nr += s[0];
-    na += s[1];
-    nb += s[2];
+  while (total(na, nb) > budget) {
+    if (nb > 3) --nb;
+    else if (na > 4) --na;
+    else if (nb > 2) --nb;
+    else if (na > 2) --na;
+    else break;
   }
-  if (total(nr, na, nb) > budget)
-    return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (bn=%d ks=%d)", bn, ks);
+  if (total(na, nb) > budget)
+    return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
+  const int nr = rpb ? na : 0;
 
   b200::GemmParams p{};
   p.offsets = a->offsets;
   p.expert_begin = a->expert_begin;
   p.n_experts = a->n_experts;
   p.bn = bn;
-  p.ks = ks;
-  p.feat_tiles = feat_tiles;
   p.wfmt = a->wfmt;
-  p.planes = a->planes;
+  p.gated = gated ? 1 : 0;
+  p.feat_tile = feat_tile;
+  p.feat_tiles = feat_tiles;
   p.feat_pad = a->feat_pad;
   p.n_feat = a->n_feat;
   p.k_pad = a->k_pad;
-  p.nkb = nkb;
+  p.nkb = a->k_pad / 64;
   p.fp8_scale = a->fp8_scale;
   p.sc_br = a->sc_br;
   p.sc_bc = a->sc_bc;
@@ -274,9 +277,7 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.sc_nbc = a->sc_nbc;
   p.mx_scale = a->mx_scale;
   p.mx_groups = a->k_pad / 32;
-  p.b_src = static_cast<const __nv_bfloat16*>(a->b_src);
-  p.ldb = a->ldb;
-  p.k_valid = a->k_valid;
+  p.b_gather = a->b_map != nullptr ? 1 : 0;
   p.b_map = a->b_map;
   p.b_div = a->b_map ? a->b_div : 1;
   p.epi = a->epilogue;
@@ -294,54 +295,68 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.nb = nb;
   uint32_t off = 0;
   p.raw_off = off;
-  off += nr * rpb * a->planes;
+  off += nr * rpb;
   p.a_off = off;
   off += na * a_stage;
   p.b_off = off;
   off += nb * b_stage;
-  p.red_off = off;
-  off += red;
+  p.x_off = off;
+  off += xbytes;
   p.bar_off = off;
-  off += 1024u;
+  off += barbytes;
   const uint32_t smem = off + 1024u;  // + alignment slack
-  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(a->planes * bn)));
+  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(2 * bn)));
 
-  // weight tensor map
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
   if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  CUtensorMap map;
-  const cuuint64_t rows = static_cast<cuuint64_t>(a->n_experts) * a->planes * a->feat_pad;
-  cuuint64_t dims[2];
-  cuuint64_t strides[1];
-  cuuint32_t box[2];
-  const cuuint32_t estr[2] = {1, 1};
-  CUtensorMapDataType dt;
-  CUtensorMapSwizzle sw;
-  if (a->wfmt == B200MOE_W_BF16) {
-    dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    dims[0] = a->k_pad;
-    strides[0] = static_cast<cuuint64_t>(a->k_pad) * 2;
-    box[0] = 64;
-    sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  } else if (a->wfmt == B200MOE_W_FP8) {
-    dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-    dims[0] = a->k_pad;
-    strides[0] = a->k_pad;
-    box[0] = 64;
-    sw = CU_TENSOR_MAP_SWIZZLE_NONE;
-  } else {
-    dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-    dims[0] = a->k_pad / 2;
-    strides[0] = a->k_pad / 2;
-    box[0] = 32;
-    sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  // weights: [n_experts * planes * feat_pad rows] x [k bytes or elements]
+  CUtensorMap wmap, bmap;
+  {
+    const cuuint64_t rows = static_cast<cuuint64_t>(a->n_experts) * a->planes * a->feat_pad;
+    cuuint64_t dims[2];
+    cuuint64_t strides[1];
+    cuuint32_t box[2];
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMapDataType dt;
+    CUtensorMapSwizzle sw;
+    if (a->wfmt == B200MOE_W_BF16) {
+      dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      dims[0] = a->k_pad;
+      strides[0] = static_cast<cuuint64_t>(a->k_pad) * 2;
+      box[0] = 64;
+      sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    } else if (a->wfmt == B200MOE_W_FP8) {
+      dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      dims[0] = a->k_pad;
+      strides[0] = a->k_pad;
+      box[0] = 64;
+      sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    } else {
+      dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      dims[0] = a->k_pad / 2;
+      strides[0] = a->k_pad / 2;
+      box[0] = 32;
+      sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    }
+    dims[1] = rows;
+    box[1] = gated ? 64 : 128;
+    CUresult cr = enc(&wmap, dt, 2, const_cast<void*>(a->weight), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "weight tensor map failed (%d)", (int)cr);
   }
-  dims[1] = rows;
-  box[1] = 128;
-  CUresult cr = enc(&map, dt, 2, const_cast<void*>(a->weight), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
+  // token rows: [b_rows] x [k_valid] bf16 (columns past k_valid read as zero);
+  // one-row boxes for tile::gather4, token_tile-row boxes for contiguous rows
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->k_valid), static_cast<cuuint64_t>(a->b_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a->ldb) * 2};
+    const cuuint32_t box[2] = {64, a->b_map ? 1u : static_cast<cuuint32_t>(bn)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a->b_src), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "activation tensor map failed (%d)", (int)cr);
+  }
 
   const void* kern = b200::gemm_kernel_ptr();
   {
@@ -351,21 +366,13 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
       g_gemm_attr[device] = true;
     }
   }
+  const int grid = static_cast<int>(std::min<long long>(g_sm_count[device], tiles_ub));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(feat_tiles * ks, max_tiles, 1);
-  cfg.blockDim = dim3(384, 1, 1);
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(512, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  if (ks > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = ks;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
-  void* args[] = {&map, &p};
+  void* args[] = {&wmap, &bmap, &p};
   B200_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
   return B200MOE_OK;
 }

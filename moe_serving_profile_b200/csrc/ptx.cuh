@@ -77,14 +77,18 @@ B200_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Returns false (and
-// records kStatusWaitTimeout) if it does not within kWaitLimitNs.
-B200_DEVI bool wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
+// records kStatusWaitTimeout) if it does not within kWaitLimitNs. Waiters off
+// the critical path pass sleep_ns > 0 to back off between polls and leave
+// issue slots to the warps doing the work.
+B200_DEVI bool wait_bounded(uint64_t* bar, uint32_t parity, int* status, unsigned sleep_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 32; ++i) {
+      if (sleep_ns) __nanosleep(sleep_ns);
       if (mbar_try_wait(bar, parity)) return true;
+    }
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       if (status) atomicOr(status, kStatusWaitTimeout);
       return false;
@@ -107,6 +111,47 @@ B200_DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
+}
+
+// Four rows (arbitrary row coordinates r0..r3, box one row high) of a 2D
+// tensor into four consecutive box rows of shared memory.
+B200_DEVI void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int r0, int r1,
+                           int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2),
+      "r"(r3)
+      : "memory");
+}
+
+// Barrier among `count` threads (a multiple of 32) on hardware barrier `id`.
+B200_DEVI void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier among `count` threads that also ANDs `v` over them (all threads
+// get the same result, so they agree on a decision before more barriers).
+B200_DEVI bool named_bar_and(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "bar.red.and.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
+// (a, b) *= s with one packed fp32 multiply (round to nearest, like two fmul).
+B200_DEVI void mul2_f32(float& a, float& b, float s) {
+  uint64_t x, y, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(y) : "f"(s));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
 }
 
 B200_DEVI void tma_prefetch_desc(const CUtensorMap* map) {
@@ -229,6 +274,14 @@ B200_DEVI void st_cluster_f32x4(uint32_t addr, float a, float b, float c, float 
 // Round-to-nearest-even float -> bf16, returned as a float holding the bf16
 // value (exactly the value torch produces for `x.to(torch.bfloat16)`).
 B200_DEVI float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Round-to-nearest-even float -> bf16 bits with integer ops (keeps the
+// conversion pipe free; identical to cvt.rn for finite values and infinities).
+B200_DEVI uint32_t bf16_rn_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
+}
+B200_DEVI float bf16_rn(float f) { return __uint_as_float(bf16_rn_bits(f) << 16); }
 
 B200_DEVI uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

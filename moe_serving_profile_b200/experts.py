@@ -5,10 +5,11 @@
 permuted row order (expert-major, then slot, then token). The caller combines
 the rows (``ops.combine``) after any expert-parallel exchange.
 
-Launch shapes (token tile, cluster split of K) come from ``tile_policy``,
-which depends only on T, K, the global expert count and the weight shape —
-not on the expert-parallel size — so a token's expert outputs are bitwise the
-same whether its experts run on 1 or 8 GPUs.
+Launch shapes (the token tile) come from ``tile_policy``, which depends only
+on T, K and the global expert count — not on the expert-parallel size. Each
+output element is one fp32 tensor-core accumulation over K in increasing
+order, so a token's expert outputs are bitwise the same whether its experts
+run on 1 or 8 GPUs.
 """
 
 from __future__ import annotations
@@ -27,18 +28,14 @@ def _sm_count(device: int) -> int:
     return torch.cuda.get_device_properties(device).multi_processor_count
 
 
-def tile_policy(T: int, K: int, num_experts: int, feat_tiles: int, k_blocks: int,
-                sm_count: int) -> tuple[int, int]:
-    """(token_tile, split_k) for one grouped GEMM launch."""
-    rows = max(1.0, T * K / num_experts)
+def tile_policy(T: int, K: int, num_experts: int) -> int:
+    """Token tile (the MMA N) for one grouped GEMM launch: the smallest power
+    of two in [16, 256] covering the mean rows per expert."""
+    rows = T * K / num_experts
     bn = 16
     while bn < 256 and bn < rows:
         bn *= 2
-    used = num_experts * (1.0 - (1.0 - K / num_experts) ** T)
-    tiles_per_expert = max(1, math.ceil(rows / bn))
-    items = max(1, round(used)) * tiles_per_expert * feat_tiles
-    ks = max(1, min(4, k_blocks, sm_count // items))
-    return bn, ks
+    return bn
 
 
 def run_experts(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
@@ -66,16 +63,24 @@ def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K:
     T = hidden.shape[0] if tokens is None else tokens
     R = perm.perm_src.numel()
     dev = hidden.device
-    bn, ks = tile_policy(T, K, num_experts, w.i_pad // 128, w.h_k // 64, _sm_count(dev.index))
+    bn = tile_policy(T, K, num_experts)
+    div = K if b_map_div is None else b_map_div
     act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16) if out is None else out
+    if bn >= 64:
+        # large token tiles: gather the routed rows once into permuted order
+        # so the GEMM reads them as plain 2D tiles instead of per-row gathers
+        b_src = ops.gather_rows(hidden, perm.perm_src, div)
+        b_map, b_div = None, 1
+    else:
+        b_src, b_map, b_div = hidden, perm.perm_src, div
     ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
                     max_rows=R, wfmt=w.fmt, planes=2, feat_pad=w.i_pad, n_feat=w.inter,
                     k_pad=w.h_k, weight=w.w1,
                     fp8_scale=w.s1 if w.fmt == _lib.W_FP8 else None, fp8_block=w.block,
-                    mx_scale=w.s1 if w.fmt == _lib.W_MXFP4 else None, b_src=hidden,
-                    k_valid=hidden.shape[1], b_map=perm.perm_src,
-                    b_div=K if b_map_div is None else b_map_div, epilogue=w.gated_epilogue,
-                    bias=w.b1, alpha=w.alpha, limit=w.limit, out=act, token_tile=bn, split_k=ks)
+                    mx_scale=w.s1 if w.fmt == _lib.W_MXFP4 else None, b_src=b_src,
+                    k_valid=hidden.shape[1], b_map=b_map, b_div=b_div,
+                    epilogue=w.gated_epilogue, bias=w.b1, alpha=w.alpha, limit=w.limit, out=act,
+                    token_tile=bn)
     return act
 
 
@@ -85,7 +90,7 @@ def down(w: ExpertWeights, act: torch.Tensor, perm: ops.Permutation,
     """Down projection of the gated rows, scaled by the routing weights."""
     R = perm.perm_src.numel()
     dev = act.device
-    bn, ks = tile_policy(tokens, K, num_experts, w.h_f // 128, w.i_pad // 64, _sm_count(dev.index))
+    bn = tile_policy(tokens, K, num_experts)
     if contrib is None:
         contrib = torch.empty(R, w.hidden, device=dev, dtype=torch.bfloat16)
     ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
@@ -95,7 +100,7 @@ def down(w: ExpertWeights, act: torch.Tensor, perm: ops.Permutation,
                     mx_scale=w.s2 if w.fmt == _lib.W_MXFP4 else None, b_src=act,
                     k_valid=w.inter, epilogue=_lib.EPI_DOWN, bias=w.b2,
                     row_weight=None if weights is None else weights.reshape(-1),
-                    row_src=perm.perm_src, out=contrib, token_tile=bn, split_k=ks)
+                    row_src=perm.perm_src, out=contrib, token_tile=bn)
     return contrib
 
 

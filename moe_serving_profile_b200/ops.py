@@ -131,6 +131,7 @@ def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max
                 weight: torch.Tensor, fp8_scale: torch.Tensor | None = None,
                 fp8_block: tuple[int, int] = (128, 128), mx_scale: torch.Tensor | None = None,
                 b_src: torch.Tensor, k_valid: int, b_map: torch.Tensor | None = None,
+                b_rows: int | None = None,
                 b_div: int = 1, epilogue: int, bias: torch.Tensor | None = None,
                 alpha: float = 1.702, limit: float = 7.0, row_weight: torch.Tensor | None = None,
                 row_src: torch.Tensor | None = None, out: torch.Tensor,
@@ -158,6 +159,7 @@ def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max
     a.mx_scale = _ptr(mx_scale)
     a.b_src = _ptr(b_src)
     a.ldb = b_src.stride(0)
+    a.b_rows = b_src.shape[0] if b_rows is None else b_rows
     a.k_valid = k_valid
     a.b_map = _ptr(b_map)
     a.b_div = b_div
