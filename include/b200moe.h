@@ -100,6 +100,32 @@ int b200moe_permute(int device, void* stream, const long long* indices, int T, i
                     int* counts, int* offsets, int* perm_src, int* inverse, void* workspace,
                     size_t workspace_bytes);
 
+/* Permutation without a caller workspace (no counterpart in the reference,
+ * whose bookkeeping runs on the host). Same arguments, outputs, ordering and
+ * errors as b200moe_permute; the per-chunk histograms live in one fixed
+ * device array of B200MOE_PERMUTE_SCRATCH_BYTES per device instead of the
+ * workspace, so the call makes no allocation (no cudaMalloc/cudaFree, no
+ * allocating library call). It is for callers that cannot allocate: a host
+ * binding that owns only buffers pre-sized by its engine's memory planner,
+ * and a serving step that must not call cudaMalloc/cudaFree because those
+ * can synchronise the whole device and stall its other streams.
+ *
+ * Limit: b200moe_permute_workspace(T, K, E) must be at most
+ * B200MOE_PERMUTE_SCRATCH_BYTES (1 MiB: e.g. T*K up to 2,097,152 at E = 128);
+ * larger problems return B200MOE_ERR_UNSUPPORTED.
+ * Setup: the first call on a device looks up the array's address on that
+ * device; make that first call before any stream capture.
+ * Zeroing: none needed; every scratch word a call reads was written earlier
+ * in the same call.
+ * Races: calls on one device share the array, so calls that overlap in time
+ * (different streams without an ordering between them, or different host
+ * threads) race; order them on one stream or with events.
+ */
+#define B200MOE_PERMUTE_SCRATCH_BYTES (1u << 20)
+
+int b200moe_permute_noalloc(int device, void* stream, const long long* indices, int T, int K,
+                            int E, int* counts, int* offsets, int* perm_src, int* inverse);
+
 /* ------------------------------------------------------------ grouped GEMM
  * One launch computes, for every expert in [expert_begin, expert_begin +
  * n_experts) and every permuted row of that expert, either

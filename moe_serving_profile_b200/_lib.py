@@ -22,6 +22,7 @@ ROUTER_QWEN3, ROUTER_GPT_OSS, ROUTER_NATIVE = 0, 1, 2
 W_BF16, W_FP8, W_MXFP4 = 0, 1, 2
 EPI_SWIGLU, EPI_CLAMP_SWIGLU, EPI_DOWN = 0, 1, 2
 ORDER_EXPERT, ORDER_RANK_SLOT = 0, 1
+PERMUTE_SCRATCH_BYTES = 1 << 20
 
 EXPORTED = (
     "b200moe_last_error",
@@ -30,6 +31,7 @@ EXPORTED = (
     "b200moe_router",
     "b200moe_permute_workspace",
     "b200moe_permute",
+    "b200moe_permute_noalloc",
     "b200moe_expert_gemm",
     "b200moe_combine",
     "b200moe_gather_rows",
@@ -100,6 +102,10 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_permute.argtypes = [
         c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
         c_void_p, c_size_t,
+    ]
+    lib.b200moe_permute_noalloc.restype = c_int
+    lib.b200moe_permute_noalloc.argtypes = [
+        c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
     ]
     lib.b200moe_expert_gemm.restype = c_int
     lib.b200moe_expert_gemm.argtypes = [c_int, c_void_p, POINTER(GemmArgs)]

@@ -49,6 +49,7 @@ std::mutex g_mu;
 int* g_status_ptr[kMaxDevices] = {};
 int g_sm_count[kMaxDevices] = {};
 bool g_gemm_attr[kMaxDevices] = {};
+void* g_permute_scratch_ptr[kMaxDevices] = {};
 
 int use_device(int device, int** status) {
   B200_CHECK(device >= 0 && device < kMaxDevices, "device %d out of range", device);
@@ -178,6 +179,44 @@ int b200moe_permute(int device, void* stream, const long long* indices, int T, i
   }
   B200_CUDA(b200::launch_permute(st, indices, T, K, E, counts, offsets, perm_src, inverse,
                                  workspace, sp));
+  return B200MOE_OK;
+}
+
+int b200moe_permute_noalloc(int device, void* stream, const long long* indices, int T, int K,
+                            int E, int* counts, int* offsets, int* perm_src, int* inverse) {
+  B200_CHECK(T >= 0 && K >= 1 && E >= 1, "bad sizes T=%d K=%d E=%d", T, K, E);
+  if (E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "permute supports E <= 1024 (E=%d)", E);
+  B200_CHECK((long long)T * K < (1ll << 30), "T*K too large");
+  B200_CHECK(counts && offsets, "counts and offsets are required");
+  const bool empty = (long long)T * K == 0;
+  if (!empty) B200_CHECK(indices && perm_src && inverse, "indices, perm_src and inverse are required");
+  const size_t need = b200::permute_workspace_bytes(T, K, E);
+  if (need > B200MOE_PERMUTE_SCRATCH_BYTES)
+    return fail(B200MOE_ERR_UNSUPPORTED,
+                "permute_noalloc needs %zu scratch bytes, more than its fixed %u (T=%d K=%d E=%d)",
+                need, B200MOE_PERMUTE_SCRATCH_BYTES, T, K, E);
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+  void* scratch = nullptr;
+  {
+    // first call on this device: look up the array's address with the device current
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_permute_scratch_ptr[device] == nullptr) {
+      void* p = nullptr;
+      B200_CUDA(b200::permute_static_scratch(&p));
+      g_permute_scratch_ptr[device] = p;
+    }
+    scratch = g_permute_scratch_ptr[device];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (empty) {
+    B200_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * E, st));
+    B200_CUDA(cudaMemsetAsync(offsets, 0, sizeof(int) * (E + 1), st));
+    return B200MOE_OK;
+  }
+  B200_CUDA(b200::launch_permute(st, indices, T, K, E, counts, offsets, perm_src, inverse,
+                                 scratch, sp));
   return B200MOE_OK;
 }
 

@@ -19,6 +19,9 @@ size_t permute_workspace_bytes(int T, int K, int E);
 cudaError_t launch_permute(cudaStream_t st, const long long* indices, int T, int K, int E,
                            int* counts, int* offsets, int* perm_src, int* inverse,
                            void* workspace, int* status);
+// Address, on the current device, of the fixed permutation scratch array
+// (B200MOE_PERMUTE_SCRATCH_BYTES).
+cudaError_t permute_static_scratch(void** ptr);
 
 cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            const int* inverse, const long long* indices, int T, int K, int H,

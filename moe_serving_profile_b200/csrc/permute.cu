@@ -8,8 +8,14 @@
 // of 1024 assignments: a per-chunk histogram kernel, a single-CTA scan, and a
 // placement kernel that ranks equal experts inside a chunk with
 // __match_any_sync plus a per-warp prefix in shared memory.
+#include "b200moe.h"
 #include "internal.h"
 #include "ptx.cuh"
+
+// Chunk-histogram scratch of b200moe_permute_noalloc: one fixed array per
+// device, written by the histogram kernel before the scan and placement
+// kernels read it, so it never needs clearing.
+static __device__ __align__(256) int g_permute_scratch[B200MOE_PERMUTE_SCRATCH_BYTES / sizeof(int)];
 
 namespace b200 {
 namespace {
@@ -210,6 +216,10 @@ size_t permute_workspace_bytes(int T, int K, int E) {
   if (R <= kSmallMax) return 0;
   const long long nchunks = (R + kChunk - 1) / kChunk;
   return static_cast<size_t>(nchunks * E * sizeof(int));
+}
+
+cudaError_t permute_static_scratch(void** ptr) {
+  return cudaGetSymbolAddress(ptr, g_permute_scratch);
 }
 
 cudaError_t launch_permute(cudaStream_t st, const long long* indices, int T, int K, int E,

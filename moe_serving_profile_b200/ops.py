@@ -125,6 +125,30 @@ def permute(indices: torch.Tensor, num_experts: int) -> Permutation:
     return Permutation(counts, offsets, perm_src, inverse)
 
 
+def permute_noalloc(indices: torch.Tensor, num_experts: int, out: Permutation) -> Permutation:
+    """``permute`` into caller-owned buffers, with no allocation in the call:
+    the chunk histograms use the library's fixed per-device scratch
+    (``_lib.PERMUTE_SCRATCH_BYTES``). Calls on one device must not overlap in
+    time; shapes needing more scratch raise NotImplementedError."""
+    device = _dev(indices, "indices")
+    if indices.dtype != torch.int64 or indices.dim() != 2 or not indices.is_contiguous():
+        raise ValueError("indices must be a contiguous int64 [T, K] tensor")
+    T, K = indices.shape
+    want = {"counts": num_experts, "offsets": num_experts + 1, "perm_src": T * K, "inverse": T * K}
+    for name, n in want.items():
+        t = getattr(out, name)
+        if t.dtype != torch.int32 or not t.is_contiguous() or t.numel() != n or t.device != indices.device:
+            raise ValueError(f"out.{name} must be a contiguous int32 tensor of {n} elements on {indices.device}")
+    check(
+        lib.b200moe_permute_noalloc(
+            device, _stream(device), _ptr(indices), T, K, num_experts, _ptr(out.counts),
+            _ptr(out.offsets), _ptr(out.perm_src), _ptr(out.inverse),
+        ),
+        "permute_noalloc",
+    )
+    return out
+
+
 # --------------------------------------------------------------------------- grouped GEMM
 def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max_rows: int,
                 wfmt: int, planes: int, feat_pad: int, n_feat: int, k_pad: int,
