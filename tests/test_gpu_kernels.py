@@ -3,7 +3,7 @@
 Integer and ordering stages are compared bit-exactly with the C oracle.
 The grouped GEMM is checked bit-exactly on integer-valued data (every fp32
 partial sum is exact, so any summation order gives the same result) across
-token tiles and cluster split-K, and its dequantisers are probed exactly with
+token tiles and weight formats, and its dequantisers are probed exactly with
 one-hot activations.
 """
 

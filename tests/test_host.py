@@ -1,0 +1,146 @@
+"""Host-side checks that need no GPU.
+
+* the C-ABI library loads and exports every function ``include/b200moe.h``
+  declares, and the ctypes binding registers each of them;
+* arguments the C ABI rejects on the host (before any CUDA call) give the
+  documented status codes;
+* the torch wrappers refuse CPU tensors (there is no CPU path);
+* the load-time weight layouts (padding, GPT-OSS gate/up de-interleave,
+  MXFP4 scale padding) and the token-tile policy.
+"""
+
+import ctypes
+import re
+
+import pytest
+import torch
+
+from moe_serving_profile_b200 import _lib, layout, ops
+from moe_serving_profile_b200.experts import tile_policy
+from tests.conftest import ROOT
+
+HEADER = ROOT / "include" / "b200moe.h"
+
+
+def _declared() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(b200moe_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = _declared()
+    assert len(names) >= 11
+    for n in names:
+        assert hasattr(_lib.lib, n), f"{n} declared in the header but not exported"
+    assert sorted(_lib.EXPORTED) == names
+    assert _lib.version().startswith("b200moe")
+    assert _lib.lib.b200moe_gemm_args_size() == ctypes.sizeof(_lib.GemmArgs)
+
+
+def test_permute_workspace_is_host_arithmetic():
+    n = ctypes.c_size_t(0)
+    assert _lib.lib.b200moe_permute_workspace(64, 8, 128, ctypes.byref(n)) == _lib.OK
+    assert n.value == 0                                  # single-CTA path, no workspace
+    assert _lib.lib.b200moe_permute_workspace(4096, 8, 128, ctypes.byref(n)) == _lib.OK
+    assert n.value == 32 * 128 * 4                       # 32 chunks of 1024 assignments
+    assert _lib.lib.b200moe_permute_workspace(-1, 8, 128, ctypes.byref(n)) == _lib.ERR_INVALID
+
+
+FAKE = 0x10000   # a 16-byte aligned non-NULL address; never dereferenced by a rejected call
+
+
+def test_c_abi_rejections_before_any_cuda_call():
+    L = _lib.lib
+    assert L.b200moe_permute(0, None, FAKE, 4, 2, 2000, FAKE, FAKE, FAKE, FAKE, None, 0) == _lib.ERR_UNSUPPORTED
+    assert L.b200moe_permute(0, None, FAKE, 4, 0, 8, FAKE, FAKE, FAKE, FAKE, None, 0) == _lib.ERR_INVALID
+    # 1 MiB of fixed scratch: 2049 chunks at E = 128 is one chunk too many
+    assert L.b200moe_permute_noalloc(0, None, FAKE, 2049 * 128, 8, 128, FAKE, FAKE, FAKE, FAKE) == _lib.ERR_UNSUPPORTED
+    assert "scratch" in L.b200moe_last_error().decode()
+    assert L.b200moe_router(0, None, 7, FAKE, 64, FAKE, None, 4, 64, 8, 2, 1, FAKE, FAKE, FAKE, FAKE, None, 0) == _lib.ERR_INVALID
+    assert L.b200moe_router(0, None, 0, FAKE, 64, FAKE, None, 4, 64, 600, 2, 1, FAKE, FAKE, FAKE, FAKE, None, 0) == _lib.ERR_UNSUPPORTED
+    assert L.b200moe_expert_gemm(0, None, None) == _lib.ERR_INVALID
+
+
+def _gemm_args(**over):
+    a = _lib.GemmArgs(offsets=FAKE, expert_begin=0, n_experts=8, max_rows=64, token_tile=0,
+                      split_k=0, wfmt=_lib.W_BF16, planes=1, feat_pad=256, n_feat=256, k_pad=128,
+                      weight=FAKE, b_src=FAKE, ldb=128, b_rows=64, k_valid=128, b_div=1,
+                      epilogue=_lib.EPI_DOWN, out=FAKE, ldo=256)
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("over,code", [
+    ({"split_k": 2}, _lib.ERR_UNSUPPORTED),
+    ({"n_experts": 2000}, _lib.ERR_UNSUPPORTED),
+    ({"feat_pad": 200}, _lib.ERR_INVALID),
+    ({"k_valid": 130}, _lib.ERR_INVALID),
+    ({"ldo": 250, "n_feat": 250}, _lib.ERR_INVALID),
+    ({"out": FAKE + 8}, _lib.ERR_INVALID),
+    ({"planes": 2}, _lib.ERR_INVALID),                   # down epilogue with two planes
+    ({"wfmt": _lib.W_FP8}, _lib.ERR_INVALID),             # fp8 without scales
+    ({"token_tile": 48}, _lib.ERR_INVALID),
+])
+def test_gemm_argument_rejections(over, code):
+    a = _gemm_args(**over)
+    assert _lib.lib.b200moe_expert_gemm(0, None, ctypes.byref(a)) == code
+
+
+def test_check_maps_status_codes_to_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_INVALID, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.ERR_UNSUPPORTED, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.ERR_CUDA, "x")
+
+
+def test_wrappers_refuse_cpu_tensors():
+    idx = torch.zeros(4, 2, dtype=torch.int64)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.permute(idx, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gather_rows(torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(4, dtype=torch.int32), 1)
+
+
+@pytest.mark.parametrize("T,K,E,bn", [(1, 8, 128, 16), (64, 8, 128, 16), (512, 8, 128, 32),
+                                      (4096, 8, 128, 256), (2048, 4, 32, 256), (16, 4, 32, 16),
+                                      (64, 4, 32, 16), (256, 8, 128, 16)])
+def test_tile_policy(T, K, E, bn):
+    assert tile_policy(T, K, E) == bn
+
+
+def test_fp8_layout_pads_with_zeros():
+    E, I, H = 2, 136, 200
+    g = torch.Generator().manual_seed(0)
+    mk = lambda *s: torch.randint(0, 255, s, generator=g, dtype=torch.uint8).view(torch.float8_e4m3fn)
+    gate, up, down = mk(E, I, H), mk(E, I, H), mk(E, H, I)
+    sc = lambda r, c: torch.rand(E, (r + 127) // 128, (c + 127) // 128, generator=g)
+    w = layout.fp8_experts(gate, sc(I, H), up, sc(I, H), down, sc(H, I), (128, 128))
+    assert w.w1.shape == (E, 2, 256, 256) and w.w2.shape == (E, 256, 256)
+    assert torch.equal(w.w1[:, 0, :I, :H], gate.view(torch.uint8))
+    assert torch.equal(w.w1[:, 1, :I, :H], up.view(torch.uint8))
+    assert int(w.w1[:, :, I:].sum()) == 0 and int(w.w1[:, :, :, H:].sum()) == 0
+    assert torch.equal(w.w2[:, :H, :I], down.view(torch.uint8)) and int(w.w2[:, H:].sum()) == 0
+    assert w.s1.shape == (E, 2, 2, 2) and w.s1.dtype == torch.float32
+
+
+def test_gpt_oss_mxfp4_layout_deinterleaves_gate_up():
+    E, I, H = 2, 64, 96
+    g = torch.Generator().manual_seed(1)
+    gu_b = torch.randint(0, 255, (E, 2 * I, H // 32, 16), generator=g, dtype=torch.uint8)
+    gu_s = torch.randint(100, 140, (E, 2 * I, H // 32), generator=g, dtype=torch.uint8)
+    gu_bias = torch.randn(E, 2 * I, generator=g)
+    dn_b = torch.randint(0, 255, (E, H, I // 32, 16), generator=g, dtype=torch.uint8)
+    dn_s = torch.randint(100, 140, (E, H, I // 32), generator=g, dtype=torch.uint8)
+    dn_bias = torch.randn(E, H, generator=g)
+    w = layout.gpt_oss_mxfp4_experts(gu_b, gu_s, gu_bias, dn_b, dn_s, dn_bias, 1.702, 7.0)
+    assert w.i_pad == 128 and w.h_k == 128 and w.h_f == 128
+    assert torch.equal(w.w1[:, 0, :I, : H // 2], gu_b[:, 0::2].reshape(E, I, H // 2))
+    assert torch.equal(w.w1[:, 1, :I, : H // 2], gu_b[:, 1::2].reshape(E, I, H // 2))
+    assert torch.equal(w.s1[:, 1, :I, : H // 32], gu_s[:, 1::2])
+    assert bool((w.s1[:, :, I:] == 127).all()) and bool((w.s1[:, :, :, H // 32:] == 127).all())
+    assert bool((w.s2[:, :, I // 32:] == 127).all())
+    assert torch.equal(w.b1[:, 0, :I], gu_bias[:, 0::2].bfloat16())
+    assert w.gated_epilogue == _lib.EPI_CLAMP_SWIGLU
