@@ -234,12 +234,30 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
                     long long ld_out);
 
 /* ------------------------------------------------------------ row gather
- * dst[i, :H] = src[map[i] / div, :H] for i < n (bf16 rows). The dispatch
+ * dst[i, :H] = src[map[i] / div, :H] for i < n (bf16 rows; a negative
+ * map[i], a dropped assignment, gives a zero row). The dispatch
  * packing of moe_serving/moe.py:127 (hidden[token_index[order]]) and the
  * un-permute of received rows.
  */
 int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_src,
                         const int* map, int div, int n, int H, void* dst, long long ld_dst);
+
+/* ------------------------------------------------------------ token all-to-all
+ * Receive-side plan of the dispatch exchange of moe_serving/moe.py:123-131
+ * (collective.exchange of rows grouped by destination rank). After the
+ * exchange a rank holds rows grouped by source rank and, inside a source, by
+ * local expert. counts: int32 [ep * experts_per_rank], counts[s * el + e] =
+ * rows source s sent for local expert e. Outputs (int32):
+ *   offsets [el + 1]  expert-major segment starts (sources ascending inside
+ *                     an expert, each source's rows in arrival order)
+ *   map_in  [rows]    expert-major position -> arrival row
+ *   map_back[rows]    arrival row -> expert-major position
+ * rows must equal the sum of counts (else B200MOE_STATUS_BAD_TILE is raised
+ * in the device status). ep * experts_per_rank <= 1024.
+ */
+int b200moe_a2a_recv_plan(int device, void* stream, const int* counts, int ep,
+                          int experts_per_rank, int rows, int* offsets, int* map_in,
+                          int* map_back);
 
 #ifdef __cplusplus
 }

@@ -35,6 +35,7 @@ EXPORTED = (
     "b200moe_expert_gemm",
     "b200moe_combine",
     "b200moe_gather_rows",
+    "b200moe_a2a_recv_plan",
     "b200moe_gemm_args_size",
 )
 
@@ -122,6 +123,10 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_gather_rows.argtypes = [
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int, c_int, c_void_p,
         c_longlong,
+    ]
+    lib.b200moe_a2a_recv_plan.restype = c_int
+    lib.b200moe_a2a_recv_plan.argtypes = [
+        c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
     ]
     return lib
 

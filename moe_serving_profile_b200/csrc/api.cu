@@ -123,7 +123,7 @@ int b200moe_router(int device, void* stream, int mode, const void* hidden, long 
   B200_CHECK(T >= 0 && E >= 1 && K >= 1, "bad sizes T=%d E=%d K=%d", T, E, K);
   if (E > 512 || K > 32 || K > E)
     return fail(B200MOE_ERR_UNSUPPORTED, "router supports E <= 512 and K <= min(32, E) (E=%d K=%d)", E, K);
-  B200_CHECK(logits && scores && indices, "logits, scores and indices are required");
+  B200_CHECK(T == 0 || (logits && scores && indices), "logits, scores and indices are required");
   if (mode == B200MOE_ROUTER_GPT_OSS) B200_CHECK(bias != nullptr, "GPT-OSS router needs a bias");
   if (!logits_given && T > 0) {
     B200_CHECK(hidden && weight, "hidden and weight are required");
@@ -222,6 +222,7 @@ int b200moe_permute_noalloc(int device, void* stream, const long long* indices, 
 
 int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   B200_CHECK(a != nullptr, "args is NULL");
+  if (a->max_rows <= 0) return B200MOE_OK;
   B200_CHECK(a->offsets && a->weight && a->b_src && a->out, "offsets, weight, b_src, out are required");
   B200_CHECK(a->wfmt >= B200MOE_W_BF16 && a->wfmt <= B200MOE_W_MXFP4, "bad weight format %d", a->wfmt);
   B200_CHECK(a->planes == 1 || a->planes == 2, "planes must be 1 or 2");
@@ -253,7 +254,6 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
              "token_tile must be 0 or a power of two in [16, 256]");
   if (a->split_k > 1) return fail(B200MOE_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
   B200_CHECK(a->split_k >= 0, "split_k must be 0 or 1");
-  if (a->max_rows <= 0) return B200MOE_OK;
   int* sp = nullptr;
   int rc = use_device(device, &sp);
   if (rc) return rc;
@@ -424,8 +424,8 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
   if (K > 32 || H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "combine needs K <= 32 and H %% 8 == 0");
   B200_CHECK(order == B200MOE_ORDER_EXPERT || order == B200MOE_ORDER_RANK_SLOT, "bad order");
   B200_CHECK(order == B200MOE_ORDER_EXPERT || experts_per_rank >= 1, "experts_per_rank must be >= 1");
-  B200_CHECK(out && inverse && indices, "out, inverse and indices are required");
-  B200_CHECK(rows || T == 0, "rows is required");
+  if (T == 0) return B200MOE_OK;
+  B200_CHECK(out && inverse && indices && rows, "rows, out, inverse and indices are required");
   B200_CHECK(!scale_rows || weights, "scale_rows needs weights");
   B200_CHECK(aligned16(rows) && aligned16(out) && ld_rows % 8 == 0 && ld_out % 8 == 0,
              "rows/out must be 16-byte aligned with ld %% 8 == 0");
@@ -441,13 +441,32 @@ int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_
                         const int* map, int div, int n, int H, void* dst, long long ld_dst) {
   B200_CHECK(n >= 0 && H >= 8 && div >= 1, "bad sizes");
   if (H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "gather_rows needs H %% 8 == 0");
-  B200_CHECK(n == 0 || (src && map && dst), "src, map and dst are required");
+  if (n == 0) return B200MOE_OK;
+  B200_CHECK(src && map && dst, "src, map and dst are required");
   B200_CHECK(aligned16(src) && aligned16(dst) && ld_src % 8 == 0 && ld_dst % 8 == 0,
              "rows must be 16-byte aligned with ld %% 8 == 0");
   int rc = use_device(device, nullptr);
   if (rc) return rc;
   B200_CUDA(b200::launch_gather_rows(static_cast<cudaStream_t>(stream), src, ld_src, map, div, n, H,
                                      dst, ld_dst));
+  return B200MOE_OK;
+}
+
+int b200moe_a2a_recv_plan(int device, void* stream, const int* counts, int ep,
+                          int experts_per_rank, int rows, int* offsets, int* map_in,
+                          int* map_back) {
+  B200_CHECK(ep >= 1 && experts_per_rank >= 1 && rows >= 0, "bad sizes ep=%d el=%d rows=%d", ep,
+             experts_per_rank, rows);
+  if ((long long)ep * experts_per_rank > 1024)
+    return fail(B200MOE_ERR_UNSUPPORTED, "a2a_recv_plan supports ep * experts_per_rank <= 1024");
+  B200_CHECK(counts && offsets, "counts and offsets are required");
+  B200_CHECK(rows == 0 || (map_in && map_back), "map_in and map_back are required");
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_a2a_recv_plan(static_cast<cudaStream_t>(stream), counts, ep,
+                                       experts_per_rank, rows, offsets, map_in, map_back,
+                                       g_sm_count[device], sp));
   return B200MOE_OK;
 }
 

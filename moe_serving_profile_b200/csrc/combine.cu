@@ -81,10 +81,15 @@ __global__ void __launch_bounds__(128) gather_rows_kernel(const __nv_bfloat16* _
                                                            long long ld_dst) {
   const int i = blockIdx.x;
   if (i >= n) return;
-  const long long s = map[i] / div;
+  const int m = map[i];
   const int nvec = H >> 3;
-  const uint4* a = reinterpret_cast<const uint4*>(src + s * ld_src);
   uint4* b = reinterpret_cast<uint4*>(dst + i * ld_dst);
+  if (m < 0) {  // a dropped assignment (inverse entry -1): zero row
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) b[v] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const long long s = m / div;
+  const uint4* a = reinterpret_cast<const uint4*>(src + s * ld_src);
   for (int v = threadIdx.x; v < nvec; v += blockDim.x) b[v] = __ldg(a + v);
 }
 

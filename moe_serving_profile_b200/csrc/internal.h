@@ -23,6 +23,11 @@ cudaError_t launch_permute(cudaStream_t st, const long long* indices, int T, int
 // (B200MOE_PERMUTE_SCRATCH_BYTES).
 cudaError_t permute_static_scratch(void** ptr);
 
+// Receive-side plan of the token all-to-all (a2a.cu).
+cudaError_t launch_a2a_recv_plan(cudaStream_t st, const int* counts, int ep, int el, int rows,
+                                 int* offsets, int* map_in, int* map_back, int sm_count,
+                                 int* status);
+
 cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            const int* inverse, const long long* indices, int T, int K, int H,
                            int order, int experts_per_rank, int expert_lo, int expert_hi,

@@ -9,6 +9,7 @@
 // placement kernel that ranks equal experts inside a chunk with
 // __match_any_sync plus a per-warp prefix in shared memory.
 #include "b200moe.h"
+#include "block_scan.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -37,38 +38,6 @@ __device__ __forceinline__ int load_expert(const long long* __restrict__ idx, in
     return -1;
   }
   return static_cast<int>(v);
-}
-
-// Exclusive scan of vals[0..n) (n <= 1024) held one per thread; returns the
-// exclusive prefix for this thread, total in *total. Uses scratch[32].
-__device__ int block_exclusive_scan(int v, int n, int* scratch, int* total) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid >= n) v = 0;
-  int incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int u = __shfl_up_sync(kFull, incl, o);
-    if (lane >= o) incl += u;
-  }
-  if (lane == 31) scratch[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    const int nw = (blockDim.x + 31) >> 5;
-    int s = lane < nw ? scratch[lane] : 0;
-    int si = s;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(kFull, si, o);
-      if (lane >= o) si += u;
-    }
-    scratch[lane] = si - s;  // exclusive warp offsets
-    if (lane == 31) scratch[32] = si;
-  }
-  __syncthreads();
-  const int res = scratch[warp] + incl - v;
-  *total = scratch[32];
-  __syncthreads();
-  return res;
 }
 
 // Place the assignments j in [c0, c0 + 1024) given base[e] = first position

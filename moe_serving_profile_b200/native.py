@@ -1,0 +1,312 @@
+"""Token all-to-all expert parallelism: the native runtime's MoE block.
+
+Same names, arguments and results as moe_serving/moe.py (ExpertPlan,
+RoutingStats, LocalSwiGLUExperts, route, routed_forward, MoELayer,
+simulate_ranks) and moe_serving/distributed.py (Collective, SingleRank,
+ProcessGroupCollective, exchange_inplace, collective_for), computed by the
+b200moe kernels:
+
+* dispatch: one expert-major permutation of the T*K assignments. A rank's
+  experts are a contiguous id range, so expert-major order is already grouped
+  by destination rank; one row gather packs the send buffer
+  (hidden[token_index[order]] of moe.py:127).
+* one count exchange of the [ep][experts_per_rank] per-expert counts and a
+  single host read of the split sizes (the reference reads counts on the host
+  once per exchange, three times per layer, distributed.py:37-45);
+* receive side: ``a2a_recv_plan`` transposes the [source][expert] segments
+  into expert-major order and the grouped GEMMs read the rows through that
+  map, then one gather restores the arrival order for the return exchange;
+* combine: ``index_add_`` of moe.py:134-136 — per token, contributions
+  bf16(y * w) added in (destination rank, slot) order starting from bf16 zero.
+
+Expert arithmetic is LocalSwiGLUExperts.forward (moe.py:73-81): bf16 gate/up
+projection, bf16(bf16(silu(gate)) * up), bf16 down projection.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from moe_serving_profile_b200 import _lib, ops
+from moe_serving_profile_b200.experts import check_inputs, run_experts
+from moe_serving_profile_b200.layout import bf16_experts
+from moe_serving_profile_b200.router import native_route
+
+
+# --------------------------------------------------------------------------- collectives
+class Collective:
+    """Moves a row tensor that is grouped by destination rank
+    (moe_serving/distributed.py:14-18)."""
+
+    world_size: int
+
+    def exchange(self, rows: torch.Tensor, send_counts, recv_counts=None):
+        raise NotImplementedError
+
+
+class SingleRank(Collective):
+    world_size = 1
+
+    def exchange(self, rows: torch.Tensor, send_counts, recv_counts=None):
+        return rows, send_counts
+
+
+class ProcessGroupCollective(Collective):
+    """NCCL (or gloo) all_to_all_single over ``group``. ``exchange(rows,
+    send_counts)`` matches moe_serving/distributed.py:27-46; given the receive
+    split sizes as a host list it skips the count exchange."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world_size = dist.get_world_size(group)
+
+    def exchange(self, rows: torch.Tensor, send_counts, recv_counts=None):
+        device = rows.device
+        if recv_counts is None:
+            send = torch.as_tensor(send_counts).to(device=device, dtype=torch.int64)
+            recv = torch.empty(self.world_size, device=device, dtype=torch.int64)
+            dist.all_to_all_single(recv, send, group=self.group)
+            both = torch.cat([send, recv]).tolist()
+            send_list, recv_list = both[: self.world_size], both[self.world_size:]
+            recv_out = recv
+        else:
+            send_list = [int(c) for c in send_counts]
+            recv_list = [int(c) for c in recv_counts]
+            recv_out = recv_list
+        out = rows.new_empty(sum(recv_list), *rows.shape[1:])
+        dist.all_to_all_single(out, rows.contiguous(), output_split_sizes=recv_list,
+                               input_split_sizes=send_list, group=self.group)
+        return out, recv_out
+
+
+def exchange_inplace(payloads: list[torch.Tensor], splits: list) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """One-process stand-in for the all-to-all (moe_serving/distributed.py:49-67):
+    ``payloads[r]`` is grouped by destination; each result is grouped by source."""
+    world = len(payloads)
+    starts = [[0] * (world + 1) for _ in range(world)]
+    for s in range(world):
+        for d in range(world):
+            starts[s][d + 1] = starts[s][d] + int(splits[s][d])
+    received = []
+    for d in range(world):
+        chunks = [payloads[s][starts[s][d]:starts[s][d + 1]] for s in range(world)]
+        counts = torch.tensor([int(splits[s][d]) for s in range(world)], dtype=torch.int64)
+        received.append((torch.cat(chunks, dim=0), counts))
+    return received
+
+
+def collective_for(world_size: int) -> Collective:
+    if world_size == 1 or not dist.is_initialized():
+        return SingleRank()
+    return ProcessGroupCollective()
+
+
+# --------------------------------------------------------------------------- plan / stats
+@dataclass
+class ExpertPlan:
+    """Contiguous expert ranges per rank (moe_serving/moe.py:19-37)."""
+
+    num_experts: int
+    ep_size: int
+    rank: int
+
+    def __post_init__(self) -> None:
+        if self.num_experts % self.ep_size:
+            raise ValueError(f"{self.num_experts} experts do not divide across {self.ep_size} ranks")
+        self.experts_per_rank = self.num_experts // self.ep_size
+        self.expert_start = self.rank * self.experts_per_rank
+        self.expert_end = self.expert_start + self.experts_per_rank
+
+    def owner(self, expert_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        dest = torch.div(expert_ids, self.experts_per_rank, rounding_mode="floor")
+        return dest, expert_ids - dest * self.experts_per_rank
+
+
+@dataclass
+class RoutingStats:
+    """Per-layer routing counts (moe_serving/moe.py:40-55)."""
+
+    counts: torch.Tensor
+    layer: int = 0
+    moe_seconds: float = 0.0
+    engram_seconds: float = 0.0
+
+    @property
+    def expert_load_cv(self) -> float:
+        mean = self.counts.float().mean()
+        if float(mean) == 0:
+            return 0.0
+        return float(self.counts.float().std(unbiased=False) / mean)
+
+    @property
+    def expert_dead_fraction(self) -> float:
+        return float((self.counts == 0).float().mean())
+
+
+# --------------------------------------------------------------------------- experts
+class LocalSwiGLUExperts(torch.nn.Module):
+    """The experts one rank owns (moe_serving/moe.py:58-81): ``gate_up``
+    [local_experts, 2 * intermediate, hidden] bf16 with the gate half first,
+    ``down`` [local_experts, hidden, intermediate]. The weights are packed
+    once into the grouped GEMM's K-major layout."""
+
+    def __init__(self, gate_up: torch.Tensor, down: torch.Tensor):
+        super().__init__()
+        if gate_up.dtype != torch.bfloat16 or down.dtype != torch.bfloat16:
+            raise ValueError("LocalSwiGLUExperts weights must be bfloat16")
+        self.hidden = down.shape[1]
+        self.intermediate = down.shape[2]
+        self.num_experts = gate_up.shape[0]
+        inter = self.intermediate
+        self.weights = bf16_experts(gate_up[:, :inter], gate_up[:, inter:], down)
+
+    def forward(self, hidden: torch.Tensor, local_expert_ids: torch.Tensor) -> torch.Tensor:
+        """Row i of the result is expert local_expert_ids[i] applied to row i."""
+        if hidden.shape[0] == 0:
+            return hidden.new_empty(0, self.hidden)
+        ids = local_expert_ids.reshape(-1, 1).to(torch.int64).contiguous()
+        hidden = hidden.contiguous()
+        perm = ops.permute(ids, self.num_experts)
+        y = run_experts(self.weights, hidden, perm, None, K=1, num_experts=self.num_experts,
+                        expert_begin=0)
+        return ops.gather_rows(y, perm.inverse, 1)
+
+
+def route(hidden: torch.Tensor, gate_weight: torch.Tensor, top_k: int,
+          renormalize: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """moe_serving/moe.py:97-107: (index int64 [T,K], weight [T,K] in hidden's dtype)."""
+    return native_route(hidden, gate_weight, top_k, renormalize)
+
+
+# --------------------------------------------------------------------------- dispatch / combine
+@dataclass
+class _Send:
+    hidden: torch.Tensor
+    index: torch.Tensor
+    weight: torch.Tensor       # bf16 [T, K]
+    perm: ops.Permutation
+    rows: torch.Tensor         # [T*K, H] grouped by destination rank
+
+
+def _prepare(hidden, expert_index, expert_weight, num_experts) -> _Send:
+    hidden, index, weight = check_inputs(hidden, expert_index, expert_weight)
+    perm = ops.permute(index, num_experts)
+    rows = ops.gather_rows(hidden, perm.perm_src, index.shape[1])
+    # the reference scales by weight.to(rows.dtype) (moe.py:136)
+    return _Send(hidden, index, weight.to(hidden.dtype).contiguous(), perm, rows)
+
+
+def _compute(experts: LocalSwiGLUExperts, recv_rows: torch.Tensor, recv_counts: torch.Tensor,
+             ep: int) -> torch.Tensor:
+    """Expert outputs for the received rows, in arrival order."""
+    R = recv_rows.shape[0]
+    if R == 0:
+        return recv_rows.new_empty(0, experts.hidden)
+    el = experts.num_experts
+    plan = ops.a2a_recv_plan(recv_counts.to(torch.int32).contiguous(), ep, el, R)
+    rperm = ops.Permutation(None, plan.offsets, plan.map_in, plan.map_back)
+    y = run_experts(experts.weights, recv_rows, rperm, None, K=1, num_experts=el, expert_begin=0,
+                    b_map_div=1)
+    return ops.gather_rows(y, plan.map_back, 1)
+
+
+def _combine(send: _Send, returned: torch.Tensor, experts_per_rank: int) -> torch.Tensor:
+    return ops.combine(returned, send.perm.inverse, send.index, order=_lib.ORDER_RANK_SLOT,
+                       experts_per_rank=experts_per_rank, weights=send.weight)
+
+
+def routed_forward(hidden: torch.Tensor, expert_index: torch.Tensor, expert_weight: torch.Tensor,
+                   experts: LocalSwiGLUExperts, plan: ExpertPlan, collective: Collective) -> torch.Tensor:
+    """Dispatch local tokens, run the owned experts, combine (moe_serving/moe.py:110-137)."""
+    if plan.ep_size > 1 and isinstance(collective, SingleRank):
+        raise RuntimeError("expert parallel needs a process group; launch with torchrun")
+    if experts.num_experts != plan.experts_per_rank:
+        raise ValueError(f"rank holds {experts.num_experts} experts, plan expects {plan.experts_per_rank}")
+    ep, el = plan.ep_size, plan.experts_per_rank
+    send = _prepare(hidden, expert_index, expert_weight, plan.num_experts)
+    if ep == 1:
+        # no exchange: the experts read the tokens through the permutation
+        returned = run_experts(experts.weights, send.hidden, send.perm, None, K=send.index.shape[1],
+                               num_experts=el, expert_begin=0)
+        return _combine(send, returned, el)
+    ours = isinstance(collective, ProcessGroupCollective)
+    # per-expert counts, experts_per_rank of them to every destination
+    count_rows = send.perm.counts.view(-1, 1)
+    if ours:
+        recv_counts, _ = collective.exchange(count_rows, [el] * ep, [el] * ep)
+    else:
+        recv_counts, _ = collective.exchange(
+            count_rows, torch.full((ep,), el, dtype=torch.int64, device=hidden.device))
+    recv_counts = recv_counts.reshape(-1)
+    splits = torch.stack([send.perm.counts.view(ep, el).sum(1),
+                          recv_counts.view(ep, el).sum(1).to(torch.int32)]).tolist()
+    send_list, recv_list = splits
+    if ours:
+        recv_rows, _ = collective.exchange(send.rows, send_list, recv_list)
+    else:
+        recv_rows, _ = collective.exchange(send.rows, torch.tensor(send_list, device=hidden.device))
+    computed = _compute(experts, recv_rows, recv_counts, ep)
+    if ours:
+        returned, _ = collective.exchange(computed, recv_list, send_list)
+    else:
+        returned, _ = collective.exchange(computed, torch.tensor(recv_list, device=hidden.device))
+    return _combine(send, returned, el)
+
+
+class MoELayer(torch.nn.Module):
+    """Router + token all-to-all experts (moe_serving/moe.py:140-168). The
+    shared expert is not implemented on this path."""
+
+    def __init__(self, gate_weight: torch.Tensor, experts: LocalSwiGLUExperts, plan: ExpertPlan,
+                 top_k: int, renormalize: bool = True, shared=None,
+                 collective: Collective | None = None, layer_id: int = 0):
+        super().__init__()
+        if shared is not None:
+            raise NotImplementedError("the shared expert is not implemented on the b200 path")
+        self.gate_weight = torch.nn.Parameter(gate_weight, requires_grad=False)
+        self.experts = experts
+        self.shared = None
+        self.plan = plan
+        self.top_k = top_k
+        self.renormalize = renormalize
+        self.collective = collective or SingleRank()
+        self.layer_id = layer_id
+
+    def forward(self, hidden: torch.Tensor) -> tuple[torch.Tensor, RoutingStats]:
+        out = ops.router(_lib.ROUTER_NATIVE, hidden, self.gate_weight, None, self.top_k,
+                         self.renormalize)
+        output = routed_forward(hidden, out.indices, out.scores, self.experts, self.plan,
+                                self.collective)
+        return output, RoutingStats(counts=out.counts.to(torch.int64).cpu(), layer=self.layer_id)
+
+
+def simulate_routed(hiddens: list[torch.Tensor], indices: list[torch.Tensor],
+                    weights: list[torch.Tensor], expert_banks: list[LocalSwiGLUExperts],
+                    num_experts: int) -> list[torch.Tensor]:
+    """The lockstep all-to-all of ``simulate_ranks`` for given per-rank routing."""
+    ep = len(hiddens)
+    el = ExpertPlan(num_experts, ep, 0).experts_per_rank
+    sends = [_prepare(h, i, w, num_experts) for h, i, w in zip(hiddens, indices, weights)]
+    counts = exchange_inplace([s.perm.counts.view(-1, 1) for s in sends], [[el] * ep] * ep)
+    recv_counts = [c.reshape(-1) for c, _ in counts]
+    send_splits = [s.perm.counts.view(ep, el).sum(1).tolist() for s in sends]
+    recv = exchange_inplace([s.rows for s in sends], send_splits)
+    computed = [_compute(expert_banks[r], recv[r][0], recv_counts[r], ep) for r in range(ep)]
+    returned = exchange_inplace(computed, [recv[r][1].tolist() for r in range(ep)])
+    return [_combine(sends[r], returned[r][0], el) for r in range(ep)]
+
+
+def simulate_ranks(hiddens: list[torch.Tensor], gates: torch.Tensor,
+                   expert_banks: list[LocalSwiGLUExperts], top_k: int, renormalize: bool = True,
+                   shared=None) -> list[torch.Tensor]:
+    """Every rank inside one process (moe_serving/moe.py:171-224): the same
+    kernels as ``routed_forward`` with ``exchange_inplace`` standing in for
+    the all-to-all. Used to check the all-to-all math on one GPU."""
+    if shared is not None:
+        raise NotImplementedError("the shared expert is not implemented on the b200 path")
+    routes = [route(h, gates, top_k, renormalize) for h in hiddens]
+    return simulate_routed(hiddens, [r[0] for r in routes], [r[1] for r in routes], expert_banks,
+                           gates.shape[0])

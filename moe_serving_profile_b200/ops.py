@@ -241,3 +241,31 @@ def gather_rows(src: torch.Tensor, index_map: torch.Tensor, div: int = 1,
         "gather_rows",
     )
     return out
+
+
+# --------------------------------------------------------------------------- token all-to-all
+@dataclass
+class RecvPlan:
+    offsets: torch.Tensor    # int32 [el+1]: expert-major segment starts
+    map_in: torch.Tensor     # int32 [rows]: expert-major position -> arrival row
+    map_back: torch.Tensor   # int32 [rows]: arrival row -> expert-major position
+
+
+def a2a_recv_plan(counts: torch.Tensor, ep: int, experts_per_rank: int, rows: int) -> RecvPlan:
+    """Transposition of received [source][expert] row segments into expert-major
+    order; ``counts`` is int32 [ep * experts_per_rank] (source-major)."""
+    device = _dev(counts, "counts")
+    if counts.dtype != torch.int32 or not counts.is_contiguous() or counts.numel() != ep * experts_per_rank:
+        raise ValueError("counts must be a contiguous int32 tensor of ep * experts_per_rank elements")
+    dev = counts.device
+    offsets = torch.empty(experts_per_rank + 1, device=dev, dtype=torch.int32)
+    map_in = torch.empty(rows, device=dev, dtype=torch.int32)
+    map_back = torch.empty(rows, device=dev, dtype=torch.int32)
+    check(
+        lib.b200moe_a2a_recv_plan(
+            device, _stream(device), _ptr(counts), ep, experts_per_rank, rows, _ptr(offsets),
+            _ptr(map_in), _ptr(map_back),
+        ),
+        "a2a_recv_plan",
+    )
+    return RecvPlan(offsets, map_in, map_back)

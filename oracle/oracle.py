@@ -259,17 +259,22 @@ def gpt_oss_layer(hidden, indices, weights, gu_blocks, gu_scales, gu_bias, dn_bl
     return ordered_expert_merge(hidden, indices, weights, project)
 
 
-def routed_forward_ranks(hiddens, gate_weight, gate_up, down, top_k, renormalize=True):
+def routed_forward_ranks(hiddens, gate_weight, gate_up, down, top_k, renormalize=True,
+                         routes=None):
     """moe_serving/moe.py:171-224 (simulate_ranks) with the exchange of
     moe_serving/distributed.py:49-67: token all-to-all EP over len(hiddens)
     in-process ranks, SwiGLU experts gate_up [E, 2I, H], down [E, H, I] run
-    per expert on the owning rank (moe.py:73-81); returns per-rank outputs."""
+    per expert on the owning rank (moe.py:73-81); returns per-rank outputs.
+    ``routes`` (a list of per-rank (index, weight)) replaces the router."""
     ep = len(hiddens)
     E = gate_weight.shape[0]
     epr = E // ep
     packed = []
-    for hidden in hiddens:
-        index, weight, _ = native_route(hidden, gate_weight, top_k, renormalize)
+    for r, hidden in enumerate(hiddens):
+        if routes is None:
+            index, weight, _ = native_route(hidden, gate_weight, top_k, renormalize)
+        else:
+            index, weight = routes[r]
         flat_index = index.reshape(-1)
         token_index = torch.arange(hidden.shape[0]).repeat_interleave(top_k)
         dest = torch.div(flat_index, epr, rounding_mode="floor")

@@ -1,0 +1,129 @@
+"""Token all-to-all expert parallelism (moe_serving/moe.py) on the GPU.
+
+The ranks run in one process (``simulate_ranks`` / ``simulate_routed``, the
+reference's own one-process stand-in for the all-to-all), so every kernel of
+the a2a path — permutation, dispatch gather, receive plan, grouped GEMMs
+through the receive map, return gather, (rank, slot)-ordered combine — runs
+on one GPU. Routing must match the reference bit for bit where its top-k has
+no tie; outputs are compared with the oracle on identical routing within the
+BF16 layer tolerance (relative L2 <= 1e-2, max |error| <= 2^-5 max |ref|).
+"""
+
+import pytest
+import torch
+
+from moe_serving_profile_b200 import _lib, native, ops
+from moe_serving_profile_b200 import synthetic as S
+from oracle import oracle
+from tests.conftest import load_golden, max_abs, rel_l2, tie_free_rows
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-2
+MAX_ABS_FRAC = 2 ** -5
+
+
+def _close(out, ref, what=""):
+    r, m = rel_l2(out, ref), max_abs(out, ref)
+    bound = MAX_ABS_FRAC * float(ref.float().abs().max())
+    assert r <= REL_L2 and m <= bound, f"{what}: rel_l2 {r:.2e} max_abs {m:.3e} (bound {bound:.3e})"
+
+
+def _banks(gate_up, down, ep, dev):
+    el = gate_up.shape[0] // ep
+    return [native.LocalSwiGLUExperts(gate_up[r * el:(r + 1) * el].to(dev),
+                                      down[r * el:(r + 1) * el].to(dev)) for r in range(ep)]
+
+
+def test_native_golden_two_ranks(cuda):
+    g = load_golden("native_a2a")
+    tokens = g["tokens"].to(cuda)
+    idx, w = native.route(tokens, g["gate"].to(cuda), g["top_k"], True)
+    assert torch.equal(idx.cpu(), g["index"])
+    outs = native.simulate_ranks([tokens[:3], tokens[3:]], g["gate"].to(cuda),
+                                 _banks(g["gate_up"], g["down"], 2, cuda), g["top_k"])
+    for o, ref in zip(outs, g["rank_outputs"]):
+        _close(o, ref, "golden rank")
+    assert _lib.device_status(cuda.index) == 0
+
+
+def _case(E, H, I, K, tokens_per_rank, seed):
+    g = torch.Generator().manual_seed(seed)
+    gate_up = (torch.randn(E, 2 * I, H, generator=g) * 0.02).bfloat16()
+    down = (torch.randn(E, H, I, generator=g) * 0.02).bfloat16()
+    gate = (torch.randn(E, H, generator=g) * 0.02).bfloat16()
+    hiddens = [torch.randn(t, H, generator=g).bfloat16() for t in tokens_per_rank]
+    return gate_up, down, gate, hiddens
+
+
+@pytest.mark.parametrize("ep,tokens", [(1, [64]), (2, [64, 48]), (4, [16, 0, 64, 33]),
+                                       (8, [8] * 8)])
+def test_a2a_matches_oracle(cuda, ep, tokens):
+    E, H, I, K = 128, 2048, 768, 8
+    gate_up, down, gate, hiddens = _case(E, H, I, K, tokens, seed=ep)
+    banks = _banks(gate_up, down, ep, cuda)
+    hd = [h.to(cuda) for h in hiddens]
+    routes = [native.route(h, gate.to(cuda), K, True) if h.shape[0] else
+              (torch.empty(0, K, dtype=torch.int64, device=cuda),
+               torch.empty(0, K, dtype=torch.bfloat16, device=cuda)) for h in hd]
+    outs = native.simulate_routed(hd, [r[0] for r in routes], [r[1] for r in routes], banks, E)
+    refs = oracle.routed_forward_ranks(hiddens, gate, gate_up, down, K,
+                                       routes=[(r[0].cpu(), r[1].cpu()) for r in routes])
+    for rank, (o, ref) in enumerate(zip(outs, refs)):
+        assert o.shape == ref.shape
+        if ref.numel():
+            _close(o, ref, f"rank {rank}")
+    # routing agrees with the reference's router wherever its top-k has no tie
+    for h, (idx, _) in zip(hiddens, routes):
+        if h.shape[0] == 0:
+            continue
+        ridx, _, scores = oracle.native_route(h, gate, K, True)
+        ok = tie_free_rows(scores, K)
+        assert torch.equal(idx.cpu()[ok], ridx[ok])
+    assert _lib.device_status(cuda.index) == 0
+
+
+def test_routed_forward_single_rank(cuda):
+    E, H, I, K = 32, 512, 256, 4
+    gate_up, down, gate, (h,) = _case(E, H, I, K, [100], seed=7)
+    experts = native.LocalSwiGLUExperts(gate_up.to(cuda), down.to(cuda))
+    plan = native.ExpertPlan(E, 1, 0)
+    idx, w = native.route(h.to(cuda), gate.to(cuda), K, True)
+    out = native.routed_forward(h.to(cuda), idx, w, experts, plan, native.SingleRank())
+    (ref,) = oracle.routed_forward_ranks([h], gate, gate_up, down, K, routes=[(idx.cpu(), w.cpu())])
+    _close(out, ref, "ep1")
+    layer = native.MoELayer(gate.to(cuda), experts, plan, K)
+    out2, stats = layer(h.to(cuda))
+    assert torch.equal(out2, out)
+    assert int(stats.counts.sum()) == 100 * K and stats.counts.shape == (E,)
+
+
+def test_local_experts_forward(cuda):
+    E, H, I = 8, 256, 128
+    gate_up, down, _, (h,) = _case(E, H, I, 1, [77], seed=3)
+    ids = torch.randint(0, E, (77,), generator=torch.Generator().manual_seed(1))
+    experts = native.LocalSwiGLUExperts(gate_up.to(cuda), down.to(cuda))
+    out = experts(h.to(cuda), ids.to(cuda))
+    ref = torch.empty(77, H, dtype=torch.bfloat16)
+    for e in ids.unique().tolist():
+        m = ids == e
+        gg, uu = torch.nn.functional.linear(h[m], gate_up[e]).chunk(2, dim=-1)
+        ref[m] = torch.nn.functional.linear(torch.nn.functional.silu(gg) * uu, down[e])
+    _close(out, ref, "LocalSwiGLUExperts")
+
+
+def test_recv_plan_transposes_segments(cuda):
+    ep, el = 3, 4
+    counts = torch.tensor([[2, 0, 1, 3], [0, 0, 2, 1], [1, 4, 0, 0]], dtype=torch.int32)
+    rows = int(counts.sum())
+    plan = ops.a2a_recv_plan(counts.flatten().to(cuda), ep, el, rows)
+    # arrival row j -> (source, expert); expert-major order sorts by (expert, source, arrival)
+    src_e = [(s, e) for s in range(ep) for e in range(el) for _ in range(int(counts[s, e]))]
+    order = sorted(range(rows), key=lambda j: (src_e[j][1], src_e[j][0], j))
+    assert plan.map_in.cpu().tolist() == order
+    back = [0] * rows
+    for p, j in enumerate(order):
+        back[j] = p
+    assert plan.map_back.cpu().tolist() == back
+    assert plan.offsets.cpu().tolist() == [0] + torch.cumsum(counts.sum(0), 0).tolist()
+    assert _lib.device_status(cuda.index) == 0

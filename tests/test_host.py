@@ -144,3 +144,37 @@ def test_gpt_oss_mxfp4_layout_deinterleaves_gate_up():
     assert bool((w.s2[:, :, I // 32:] == 127).all())
     assert torch.equal(w.b1[:, 0, :I], gu_bias[:, 0::2].bfloat16())
     assert w.gated_epilogue == _lib.EPI_CLAMP_SWIGLU
+
+
+# ------------------------------------------------------------------ native runtime host logic
+def test_expert_plan_and_stats():
+    from moe_serving_profile_b200 import native
+
+    p = native.ExpertPlan(128, 8, 3)
+    assert (p.experts_per_rank, p.expert_start, p.expert_end) == (16, 48, 64)
+    dest, local = p.owner(torch.tensor([0, 17, 127]))
+    assert dest.tolist() == [0, 1, 7] and local.tolist() == [0, 1, 15]
+    with pytest.raises(ValueError):
+        native.ExpertPlan(10, 4, 0)
+    st = native.RoutingStats(counts=torch.tensor([2, 2, 0, 4]))
+    assert st.expert_dead_fraction == 0.25
+    assert abs(st.expert_load_cv - float(torch.tensor([2., 2., 0., 4.]).std(unbiased=False) / 2)) < 1e-7
+
+
+def test_exchange_inplace_groups_by_source():
+    from moe_serving_profile_b200 import native
+
+    p0 = torch.tensor([[0], [1], [2]])          # rank 0 sends 1 row to 0, 2 rows to 1
+    p1 = torch.tensor([[10], [11], [12]])       # rank 1 sends 2 rows to 0, 1 row to 1
+    (r0, c0), (r1, c1) = native.exchange_inplace([p0, p1], [[1, 2], [2, 1]])
+    assert r0.flatten().tolist() == [0, 10, 11] and c0.tolist() == [1, 2]
+    assert r1.flatten().tolist() == [1, 2, 12] and c1.tolist() == [2, 1]
+
+
+def test_empty_problems_return_ok_without_device_work():
+    L = _lib.lib
+    # T = 0 / n = 0 / no rows: nothing to enqueue, so no pointer is needed and no CUDA call runs
+    assert L.b200moe_combine(0, None, None, 8, None, None, 0, 8, 64, 1, 16, 0, 128, 1, None, 1, None, 64) == _lib.OK
+    assert L.b200moe_gather_rows(0, None, None, 64, None, 1, 0, 64, None, 64) == _lib.OK
+    a = _lib.GemmArgs(max_rows=0)
+    assert L.b200moe_expert_gemm(0, None, ctypes.byref(a)) == _lib.OK

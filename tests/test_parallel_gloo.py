@@ -80,3 +80,45 @@ def test_parallel_group_rejects_bad_size():
     with pytest.raises(ValueError):
         ParallelGroup(0)
     assert ParallelGroup(1).size == 1
+
+
+def _exchange_worker(rank: int, world: int, port: int, q):
+    try:
+        from datetime import timedelta
+
+        from moe_serving_profile_b200 import native
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        coll = native.ProcessGroupCollective()
+        assert native.collective_for(world) is not None and coll.world_size == world
+        send = [rank + d + 1 for d in range(world)]            # rows to destination d
+        rows = torch.cat([torch.full((n, 3), float(10 * rank + d)) for d, n in enumerate(send)])
+        got, recv = coll.exchange(rows, torch.tensor(send))    # reference path (count exchange)
+        expect_counts = [s + rank + 1 for s in range(world)]
+        assert recv.tolist() == expect_counts
+        ref = torch.cat([torch.full((n, 3), float(10 * s + rank)) for s, n in enumerate(expect_counts)])
+        assert torch.equal(got, ref)
+        got2, recv2 = coll.exchange(rows, send, expect_counts)  # known splits: no count exchange
+        assert torch.equal(got2, ref) and recv2 == expect_counts
+        back, _ = coll.exchange(got2, expect_counts, send)      # return trip restores the rows
+        assert torch.equal(back, rows)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as exc:
+        q.put((rank, repr(exc)))
+
+
+def test_process_group_collective_exchange():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: "ok", 1: "ok"}, results
