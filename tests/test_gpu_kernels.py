@@ -298,3 +298,10 @@ def test_dequant_exact_via_one_hot(cuda, storage):
                     fp8_scale=None if s2 is None else s2.to(cuda), mx_scale=None if mx2 is None else mx2.to(cuda),
                     b_src=act.to(cuda), k_valid=I, epilogue=_lib.EPI_DOWN, out=out)
     assert torch.equal(out.cpu(), w.T.contiguous())
+
+
+def test_backend_check_runtime_accepts_this_device(cuda):
+    from moe_serving_profile_b200 import backend
+
+    backend.check_runtime("qwen3", cuda, torch.bfloat16, "fp8")
+    backend.check_runtime("gpt_oss", cuda, torch.bfloat16, "mxfp4")

@@ -178,3 +178,21 @@ def test_empty_problems_return_ok_without_device_work():
     assert L.b200moe_gather_rows(0, None, None, 64, None, 1, 0, 64, None, 64) == _lib.OK
     a = _lib.GemmArgs(max_rows=0)
     assert L.b200moe_expert_gemm(0, None, ctypes.byref(a)) == _lib.OK
+
+
+def test_backend_checks_and_metadata():
+    from moe_serving_profile_b200 import backend
+
+    with pytest.raises(ValueError, match="CUDA"):
+        backend.check_runtime("qwen3", "cpu", torch.bfloat16, "fp8")
+    with pytest.raises(ValueError):
+        backend.check_runtime("qwen3", "cuda", torch.float16, "fp8")
+    with pytest.raises(ValueError):
+        backend.check_runtime("gpt_oss", "cuda", torch.bfloat16, "fp8")
+    with pytest.raises(ValueError):
+        backend.check_runtime("llama", "cuda", torch.bfloat16, "fp8")
+    m = backend.backend_metadata("gpt_oss", "reference")
+    assert "mxfp4" in m["experts"] and "ordered" in m["expert_parallel"]
+    assert "fp8" in backend.backend_metadata("qwen3", "fast")["experts"]
+    with pytest.raises(ValueError):
+        backend.backend_metadata("qwen3", "efficient")
