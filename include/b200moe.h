@@ -133,19 +133,30 @@ int b200moe_permute_noalloc(int device, void* stream, const long long* indices, 
  *   down  (planes = 1): out[r, f] = epilogue(a_r . Wdown[e,f])
  * on tcgen05 tensor cores (BF16 x BF16 -> FP32 in TMEM) by a persistent
  * kernel (one CTA per SM looping over (expert, token tile, feature tile)
- * tiles; gated tiles cover 64 features, down tiles 128). Weights are stored
- * per local expert as [n_experts][planes][feat_pad][k_pad] in one of:
- *   B200MOE_W_BF16     bf16
- *   B200MOE_W_FP8      e4m3 with fp32 block scales
- *                      scale[n_experts][planes][sc_nbr][sc_nbc], block
- *                      sc_br x sc_bc; dequantised in shared memory to
- *                      bf16(fp32(w) * scale), the arithmetic of
- *                      moe_serving/qwen3_parallel.py:48-53
- *   B200MOE_W_MXFP4    e2m1 pairs (low nibble first), 16 bytes per 32
- *                      values, ue8m0 scales [n_experts][planes][feat_pad]
- *                      [k_pad/32]; decoded exactly to bf16 as
- *                      transformers' _convert_moe_packed_tensors does
- *                      (called at moe_serving/gpt_oss_parallel.py:183-193)
+ * tiles; gated tiles cover 64 features, down tiles 128). Weights, logically
+ * [n_experts][planes][feat_pad][k_pad], are passed as
+ *   B200MOE_W_BF16     bf16 in that layout (K contiguous)
+ *   B200MOE_W_FP8      e4m3 with fp32 block scales (block sc_br x sc_bc),
+ *                      converted on chip to bf16(fp32(w) * scale), the
+ *                      arithmetic of moe_serving/qwen3_parallel.py:48-53
+ *   B200MOE_W_MXFP4    e2m1 pairs (low nibble first) with ue8m0 scales per
+ *                      32 values, decoded exactly to bf16 as transformers'
+ *                      _convert_moe_packed_tensors does (called at
+ *                      moe_serving/gpt_oss_parallel.py:183-193)
+ * Quantised weights are packed once at load time into blobs, one per
+ * (expert, feature tile, 64-column k-block), stored
+ * [n_experts][feat_pad / tile_rows_per_plane][k_pad / 64][blob_bytes]:
+ *   rows: a feature tile is 64 features of both planes (rows 0-63 gate,
+ *     64-127 up) when planes = 2, or 128 features when planes = 1;
+ *   data: 128 rows of 64 bytes (FP8) or 32 bytes (MXFP4), the 16-byte chunk
+ *     c of row r stored at chunk position c ^ ((r >> 1) & 3) (FP8) or
+ *     c ^ ((r >> 2) & 1) (MXFP4);
+ *   scales after the data: FP8 with sc_br and sc_bc multiples of 64, the
+ *     fp32 scales of rows 0-63 and 64-127 then 8 zero bytes (blob 8208 B);
+ *     other FP8 blocks, fp32 [128 rows][4 chunks of 16 columns] (blob
+ *     10240 B); MXFP4, ue8m0 [128 rows][2 groups of 32 columns] (blob 4352 B).
+ * Quantised weights are converted by the CTA into tensor memory, which
+ * limits token_tile to 128 for them (B200MOE_ERR_UNSUPPORTED above).
  * Epilogues:
  *   B200MOE_EPI_SWIGLU     bf16(bf16(silu(bf16 g)) * bf16 u)
  *                          (moe_serving/qwen3_parallel.py:84-94)
@@ -174,7 +185,7 @@ typedef struct b200moe_gemm_args {
   int expert_begin;     /* first global expert id handled by this launch */
   int n_experts;        /* local experts in the weight stack */
   int max_rows;         /* upper bound on rows of these experts (T*K) */
-  int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 */
+  int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 (BF16 only) */
   int split_k;          /* reserved: must be 0 or 1 */
   /* weights (A operand) */
   int wfmt;             /* B200MOE_W_* */
@@ -182,10 +193,8 @@ typedef struct b200moe_gemm_args {
   int feat_pad;         /* padded features per plane, multiple of 128 */
   int n_feat;           /* valid features per plane */
   int k_pad;            /* padded reduction length, multiple of 64 */
-  const void* weight;   /* device */
-  const float* fp8_scale;
-  int sc_br, sc_bc, sc_nbr, sc_nbc;
-  const unsigned char* mx_scale;
+  const void* weight;   /* device: bf16 tiles or packed blobs (above) */
+  int sc_br, sc_bc;     /* FP8 scale block, selects the blob's scale form */
   /* activations (B operand): row r reads b_src[src(r) * ldb + k], k < k_valid,
      src(r) = b_map ? b_map[r] / b_div : r */
   const void* b_src;

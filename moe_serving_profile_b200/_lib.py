@@ -56,12 +56,8 @@ class GemmArgs(ctypes.Structure):
         ("n_feat", c_int),
         ("k_pad", c_int),
         ("weight", c_void_p),
-        ("fp8_scale", c_void_p),
         ("sc_br", c_int),
         ("sc_bc", c_int),
-        ("sc_nbr", c_int),
-        ("sc_nbc", c_int),
-        ("mx_scale", c_void_p),
         ("b_src", c_void_p),
         ("ldb", c_longlong),
         ("b_rows", c_int),

@@ -244,10 +244,8 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
              "output rows must be 16-byte aligned (ldo %% 8 == 0, n_feat %% 8 == 0)");
   B200_CHECK(a->b_map == nullptr || a->b_div >= 1, "b_div must be >= 1");
   if (a->wfmt == B200MOE_W_FP8)
-    B200_CHECK(a->fp8_scale && a->sc_br >= 1 && a->sc_bc >= 16 && a->sc_bc % 16 == 0 &&
-                   a->sc_nbr >= 1 && a->sc_nbc >= 1,
-               "fp8 weights need scales with block cols a multiple of 16");
-  if (a->wfmt == B200MOE_W_MXFP4) B200_CHECK(a->mx_scale != nullptr, "mxfp4 weights need scales");
+    B200_CHECK(a->sc_br >= 1 && a->sc_bc >= 16 && a->sc_bc % 16 == 0,
+               "fp8 weights need a scale block with columns a multiple of 16");
   if (a->row_weight) B200_CHECK(a->row_src != nullptr, "row_weight needs row_src");
   B200_CHECK(a->token_tile == 0 || a->token_tile == 16 || a->token_tile == 32 ||
                  a->token_tile == 64 || a->token_tile == 128 || a->token_tile == 256,
@@ -259,10 +257,16 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   if (rc) return rc;
 
   const bool gated = a->planes == 2;
+  // quantised weights keep their converted A tiles in tensor memory next to
+  // the accumulators, which caps the token tile at 128 columns
+  const int max_bn = a->wfmt == B200MOE_W_BF16 ? 256 : 128;
+  if (a->token_tile > max_bn)
+    return fail(B200MOE_ERR_UNSUPPORTED, "token_tile %d exceeds %d for this weight format",
+                a->token_tile, max_bn);
   int bn = a->token_tile;
   if (bn == 0) {
     const int avg = (a->max_rows + a->n_experts - 1) / a->n_experts;
-    bn = std::min(256, std::max(16, pow2_ceil(avg)));
+    bn = std::min(max_bn, std::max(16, pow2_ceil(avg)));
   }
   const int feat_tile = gated ? 64 : 128;
   const int feat_tiles = a->feat_pad / feat_tile;
@@ -271,30 +275,45 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
 
   // shared memory plan: raw weight ring, bf16 A ring, token-row ring, epilogue
   // exchange buffer, barriers + tile prefix
-  const uint32_t rpb = a->wfmt == B200MOE_W_FP8 ? 128u * 64u : (a->wfmt == B200MOE_W_MXFP4 ? 128u * 32u : 0u);
+  // quantised weights: one blob per (expert, feature tile, k-block), staged
+  // on 1024-byte boundaries
+  const bool fp8_half = a->sc_br % 64 == 0 && a->sc_bc % 64 == 0;
+  const uint32_t blob_bytes = a->wfmt == B200MOE_W_FP8 ? 8192u + (fp8_half ? 16u : 2048u)
+                              : (a->wfmt == B200MOE_W_MXFP4 ? 4096u + 256u : 0u);
+  const uint32_t rpb = (blob_bytes + 1023u) & ~1023u;
   const uint32_t a_stage = 128u * 128u;
   const uint32_t b_stage = static_cast<uint32_t>(bn) * 128u;
   // epilogue: exchange buffer (8 KB), two bf16 staging chunks (8 KB), row weights (1 KB)
   const uint32_t xbytes = 8192u + 8192u + 1024u;
-  const uint32_t barbytes = (((64u * 8u + 16u + 4u * (a->n_experts + 1)) + 1023u) / 1024u) * 1024u;
+  const uint32_t barbytes = (((96u * 8u + 16u + 4u * (a->n_experts + 1)) + 1023u) / 1024u) * 1024u;
   const uint32_t budget = 232448u - 2048u;
-  // One ring of na weight stages (raw bytes of quantised formats + the bf16
-  // A tile; stage s is drained by dequantiser warp s, so na <= 8) and a ring
-  // of nb token-row stages.
-  int na = 8, nb = 6;
-  auto total = [&](int a_, int b_) {
-    return a_ * (rpb + a_stage) + b_ * b_stage + xbytes + barbytes;
-  };
-  while (total(na, nb) > budget) {
-    if (nb > 3) --nb;
-    else if (na > 4) --na;
-    else if (nb > 2) --nb;
-    else if (na > 2) --na;
-    else break;
+  // BF16 weights: a ring of na shared-memory A stages filled by TMA and nb
+  // token-row stages. Quantised weights: na = 8 tensor-memory A stages (TMEM
+  // columns 256..511, beside the two accumulator slots of at most 128 columns
+  // each), nb token-row stages and as many raw stages as fit (even, <= 24).
+  int na = 0, nb = 0, nr = 0;
+  if (rpb == 0) {
+    na = 8;
+    nb = 6;
+    auto total = [&](int a_, int b_) { return a_ * a_stage + b_ * b_stage + xbytes + barbytes; };
+    while (total(na, nb) > budget) {
+      if (nb > 3) --nb;
+      else if (na > 4) --na;
+      else if (nb > 2) --nb;
+      else if (na > 2) --na;
+      else break;
+    }
+    if (total(na, nb) > budget)
+      return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
+  } else {
+    na = 8;
+    nb = b_stage <= 4096u ? 8 : 4;
+    const uint32_t fixed = nb * b_stage + xbytes + barbytes;
+    nr = fixed < budget ? static_cast<int>((budget - fixed) / rpb) : 0;
+    nr = std::min(24, nr) & ~1;
+    if (nr < 4)
+      return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
   }
-  if (total(na, nb) > budget)
-    return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
-  const int nr = rpb ? na : 0;
 
   b200::GemmParams p{};
   p.offsets = a->offsets;
@@ -309,13 +328,10 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.n_feat = a->n_feat;
   p.k_pad = a->k_pad;
   p.nkb = a->k_pad / 64;
-  p.fp8_scale = a->fp8_scale;
-  p.sc_br = a->sc_br;
-  p.sc_bc = a->sc_bc;
-  p.sc_nbr = a->sc_nbr;
-  p.sc_nbc = a->sc_nbc;
-  p.mx_scale = a->mx_scale;
-  p.mx_groups = a->k_pad / 32;
+  p.wblob = static_cast<const uint8_t*>(a->weight);
+  p.blob_bytes = blob_bytes;
+  p.stage_bytes = rpb;
+  p.scale_form = a->wfmt == B200MOE_W_MXFP4 ? 2 : (fp8_half ? 0 : 1);
   p.b_gather = a->b_map != nullptr ? 1 : 0;
   p.b_map = a->b_map;
   p.b_div = a->b_map ? a->b_div : 1;
@@ -336,7 +352,7 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.raw_off = off;
   off += nr * rpb;
   p.a_off = off;
-  off += na * a_stage;
+  if (rpb == 0) off += na * a_stage;
   p.b_off = off;
   off += nb * b_stage;
   p.x_off = off;
@@ -344,41 +360,29 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.bar_off = off;
   off += barbytes;
   const uint32_t smem = off + 1024u;  // + alignment slack
-  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(2 * bn)));
+  // independent accumulator chains for short token tiles: 2 slots x nacc
+  // banks x bn columns stay within the 256 columns below the A stages
+  p.nacc = std::max(1, std::min(4, 128 / bn));
+  p.nbanks = std::min(p.nacc, p.nkb);
+  // two MMA issuers when there are banks for both and the A / B rings split
+  // evenly between them
+  p.n_issuers = (p.nacc % 2 == 0 && na % 2 == 0 && nb % 2 == 0) ? 2 : 1;
+  p.tmem_cols = rpb ? 512u : static_cast<uint32_t>(std::max(32, pow2_ceil(2 * p.nacc * bn)));
+  p.a_col0 = 256u;
 
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
   if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  // weights: [n_experts * planes * feat_pad rows] x [k bytes or elements]
+  // BF16 weights: [n_experts * planes * feat_pad rows] x [k_pad] tiles
   CUtensorMap wmap, bmap;
-  {
+  std::memset(&wmap, 0, sizeof(wmap));
+  if (a->wfmt == B200MOE_W_BF16) {
     const cuuint64_t rows = static_cast<cuuint64_t>(a->n_experts) * a->planes * a->feat_pad;
-    cuuint64_t dims[2];
-    cuuint64_t strides[1];
-    cuuint32_t box[2];
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->k_pad), rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a->k_pad) * 2};
+    const cuuint32_t box[2] = {64, gated ? 64u : 128u};
     const cuuint32_t estr[2] = {1, 1};
-    CUtensorMapDataType dt;
-    CUtensorMapSwizzle sw;
-    if (a->wfmt == B200MOE_W_BF16) {
-      dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-      dims[0] = a->k_pad;
-      strides[0] = static_cast<cuuint64_t>(a->k_pad) * 2;
-      box[0] = 64;
-      sw = CU_TENSOR_MAP_SWIZZLE_128B;
-    } else if (a->wfmt == B200MOE_W_FP8) {
-      dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      dims[0] = a->k_pad;
-      strides[0] = a->k_pad;
-      box[0] = 64;
-      sw = CU_TENSOR_MAP_SWIZZLE_NONE;
-    } else {
-      dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-      dims[0] = a->k_pad / 2;
-      strides[0] = a->k_pad / 2;
-      box[0] = 32;
-      sw = CU_TENSOR_MAP_SWIZZLE_NONE;
-    }
-    dims[1] = rows;
-    box[1] = gated ? 64 : 128;
+    const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
     CUresult cr = enc(&wmap, dt, 2, const_cast<void*>(a->weight), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

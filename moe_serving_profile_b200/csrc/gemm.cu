@@ -13,8 +13,10 @@
 // One CTA per SM loops over tiles t = blockIdx.x, blockIdx.x + gridDim.x, ...
 // (tile = (expert, token tile, feature tile), feature tile fastest so that
 // concurrently running CTAs share token rows in L2). 16 warps:
-//   warp 0      TMA: raw weight tiles (e4m3 / e2m1 bytes) into a ring of raw
-//               stages, or bf16 weights straight into the A stages
+//   warp 0      TMA: one bulk copy per k-block of the packed weight blob
+//               (e4m3 / e2m1 rows + scales) into a ring of shared-memory
+//               stages, or 2D tiles of bf16 weights straight into
+//               shared-memory A stages
 //   warp 1      TMEM allocator and tcgen05.mma issuer (one thread); two
 //               accumulator slots so a tile's epilogue overlaps the next
 //               tile's main loop
@@ -22,12 +24,13 @@
 //               rows (gate/up) or a 2D tile of contiguous rows (down)
 //   warps 4-7   epilogue (TMEM lane quarters 0-3): activation / bias /
 //               routing weight, bf16 stores
-//   warps 8-15  dequantisers: raw stage -> bf16 A stage in the 128-byte
-//               swizzled K-major layout tcgen05 reads; warp w owns A stage w
-//               and converts every na-th k-block by itself
+//   warps 8-15  converters (quantised weights): two groups of four warps;
+//               group g converts the CTA's k-blocks g, g + 2, g + 4, ...,
+//               each lane one weight row, and writes the bf16 tile into a
+//               tensor-memory A stage (warp w owns TMEM lanes 32 (w % 4) ..
+//               + 31) that tcgen05.mma reads as its A operand. Four A stages
+//               per group let a group run ahead of the MMA's consumption.
 // All rings are phase-tracked mbarriers; every wait is bounded (see ptx.cuh).
-#include <cuda_fp8.h>
-
 #include "gemm_params.h"
 #include "ptx.cuh"
 
@@ -39,14 +42,15 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kThreads = 512;
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
+constexpr int kWarpMma2 = 3;     // second MMA issuer (two-issuer tiles)
 constexpr int kWarpB = 2;
 constexpr int kWarpEpi = 4;      // warps 4..7
 constexpr int kWarpConv = 8;     // warps 8..15
-constexpr int kConvWarps = 8;
-constexpr int kConvThreads = kConvWarps * 32;
 constexpr uint32_t kATile = 128u * 128u;    // 128 rows x 64 bf16
 constexpr uint32_t kRawFp8 = 128u * 64u;    // 128 rows x 64 e4m3
 constexpr uint32_t kRawMx = 128u * 32u;     // 128 rows x 64 e2m1
+constexpr uint32_t kAStageCols = 32;        // TMEM columns per A stage (64 bf16 / lane)
+enum { kScaleHalf = 0, kScaleChunk = 1, kScaleMx = 2 };
 
 enum { kWBf16 = 0, kWFp8 = 1, kWMx = 2 };
 enum { kEpiSwiglu = 0, kEpiClamp = 1, kEpiDown = 2 };
@@ -91,26 +95,6 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const Gemm
   return r;
 }
 
-// 16 e4m3 -> 16 bf16 holding bf16(fp32(w) * scale), the reference's dequant.
-__device__ __forceinline__ void fp8x16_to_bf16(const uint4& q, float scale, uint32_t (&o)[8]) {
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(
-        static_cast<__nv_fp8x2_storage_t>(w[i] & 0xffffu), __NV_E4M3);
-    const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(
-        static_cast<__nv_fp8x2_storage_t>(w[i] >> 16), __NV_E4M3);
-    float a0 = __half2float(__ushort_as_half(lo.x));
-    float a1 = __half2float(__ushort_as_half(lo.y));
-    float a2 = __half2float(__ushort_as_half(hi.x));
-    float a3 = __half2float(__ushort_as_half(hi.y));
-    mul2_f32(a0, a1, scale);
-    mul2_f32(a2, a3, scale);
-    o[2 * i] = pack_bf16x2(a0, a1);
-    o[2 * i + 1] = pack_bf16x2(a2, a3);
-  }
-}
-
 // 2^(s-127) as the fp32 value torch's ldexp multiplies by (exact, including
 // the subnormal s = 0 and the overflow s = 255).
 __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
@@ -119,62 +103,73 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
   return __uint_as_float(s << 23);
 }
 
-// 16 bytes of e2m1 pairs (low nibble first) -> 32 bf16 (exact).
-__device__ __forceinline__ void mx32_to_bf16(const uint4& q, float scale, const float* lut,
-                                             uint32_t (&o)[16]) {
+// Two f16 (one word, element 0 low) -> two fp32 (exact).
+__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& x, float& y) {
+  asm("{\n\t.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+      : "=f"(x), "=f"(y) : "r"(h));
+}
+
+// 16 e4m3 -> 16 bf16 = bf16(fp32(w) * scale) through the hardware e4m3 -> f16
+// conversion (exact), an exact f16 -> fp32 widening, one fp32 multiply and
+// one round to bf16: the reference's arithmetic for every scale.
+__device__ __forceinline__ void fp8x16_cvt(const uint4& q, float scale, uint32_t (&o)[8]) {
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
+    uint32_t h01, h23;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+        : "=r"(h01), "=r"(h23) : "r"(w[i]));
+    float a0, a1, a2, a3;
+    f16x2_to_f32(h01, a0, a1);
+    f16x2_to_f32(h23, a2, a3);
+    mul2_f32(a0, a1, scale);
+    mul2_f32(a2, a3, scale);
+    o[2 * i] = pack_bf16x2(a0, a1);
+    o[2 * i + 1] = pack_bf16x2(a2, a3);
+  }
+}
+
+// 32 e2m1 (16 bytes, element 0 in the low nibble) -> 32 bf16 =
+// e2m1 * 2^(S-127) through the hardware e2m1 -> f16 conversion (exact); the
+// power-of-two scale and the bf16 rounding are exact too.
+__device__ __forceinline__ void mx32_cvt(const uint4& q, uint32_t sexp, uint32_t (&o)[16]) {
+  const float s = ue8m0_to_f32(sexp);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t h[4];
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3]) : "r"(w[i]));
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const uint32_t byte = (w[i] >> (8 * b)) & 0xffu;
-      float lo = lut[byte & 15u];
-      float hi = lut[byte >> 4];
-      mul2_f32(lo, hi, scale);
+      float lo, hi;
+      f16x2_to_f32(h[b], lo, hi);
+      mul2_f32(lo, hi, s);
       o[4 * i + b] = pack_bf16x2(lo, hi);
     }
   }
 }
 
-// Four e4m3 codes (one word) -> four bf16 holding bf16(fp32(w) * scale).
-// The fp32 bit pattern (c & 0x7f) << 20 | sign << 31 has the value
-// e4m3(c) * 2^-120 for every code (normal codes give normal fp32, subnormal
-// codes subnormal fp32), so multiplying it by s120 = scale * 2^120 yields the
-// same real product as fp32(w) * scale and rounds once, exactly as the
-// reference does; only the final bf16 pack uses the conversion pipe.
-// Requires scale < 2^8 (s120 finite); the 0x7f / 0xff NaN codes are not
-// propagated as NaN.
-__device__ __forceinline__ void fp8x4_scaled(uint32_t w, float s120, uint32_t& o01,
-                                             uint32_t& o23) {
-  float f0 = __uint_as_float(((w << 20) & 0x07f00000u) | ((w << 24) & 0x80000000u));
-  float f1 = __uint_as_float(((w << 12) & 0x07f00000u) | ((w << 16) & 0x80000000u));
-  float f2 = __uint_as_float(((w << 4) & 0x07f00000u) | ((w << 8) & 0x80000000u));
-  float f3 = __uint_as_float(((w >> 4) & 0x07f00000u) | (w & 0x80000000u));
-  mul2_f32(f0, f1, s120);
-  mul2_f32(f2, f3, s120);
-  o01 = pack_bf16x2(f0, f1);
-  o23 = pack_bf16x2(f2, f3);
-}
-
-// Eight e2m1 codes (one word, element 0 in the low nibble) -> eight bf16.
-// The fp32 pattern (n & 7) << 22 | sign << 31 has the value e2m1(n) * 2^-126
-// for every code; times s = 2^(S-1) it is e2m1(n) * 2^(S-127) exactly, a value
-// bf16 represents, so the bf16 is the high half of the fp32 bits (no
-// rounding, no conversion instruction). Requires S <= 128.
-__device__ __forceinline__ void mx8_scaled(uint32_t w, float s, uint32_t (&o)[4]) {
-  float f[8];
-  f[0] = __uint_as_float(((w << 22) & 0x01c00000u) | ((w << 28) & 0x80000000u));
-  f[1] = __uint_as_float(((w << 18) & 0x01c00000u) | ((w << 24) & 0x80000000u));
-  f[2] = __uint_as_float(((w << 14) & 0x01c00000u) | ((w << 20) & 0x80000000u));
-  f[3] = __uint_as_float(((w << 10) & 0x01c00000u) | ((w << 16) & 0x80000000u));
-  f[4] = __uint_as_float(((w << 6) & 0x01c00000u) | ((w << 12) & 0x80000000u));
-  f[5] = __uint_as_float(((w << 2) & 0x01c00000u) | ((w << 8) & 0x80000000u));
-  f[6] = __uint_as_float(((w >> 2) & 0x01c00000u) | ((w << 4) & 0x80000000u));
-  f[7] = __uint_as_float(((w >> 6) & 0x01c00000u) | (w & 0x80000000u));
+// 16 accumulator columns of this thread's TMEM lane summed over the banks
+// the tile wrote (bank b at column offset b * stride): bank0, bank0 + 1, ...
+// (mod nacc), nbanks of them, in that order.
+__device__ __forceinline__ void load_acc(uint32_t taddr, int stride, int bank0, int nacc, int nbanks,
+                                         float (&acc)[16]) {
+  uint32_t r[16];
+  tmem_ld16(taddr + static_cast<uint32_t>(bank0 * stride), r);
+  tmem_ld_wait();
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    mul2_f32(f[2 * i], f[2 * i + 1], s);
-    o[i] = __byte_perm(__float_as_uint(f[2 * i]), __float_as_uint(f[2 * i + 1]), 0x7632);
+  for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(r[j]);
+  for (int k = 1; k < nbanks; ++k) {
+    const int b = (bank0 + k) & (nacc - 1);
+    tmem_ld16(taddr + static_cast<uint32_t>(b * stride), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(r[j]);
   }
 }
 
@@ -202,7 +197,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ float s_lut[16];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t* sbase = smem_raw + (base_u32 - raw_u32);
@@ -247,19 +241,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) *s_total = acc * p.feat_tiles;
   }
-  if (threadIdx.x < 16) {
-    const int m = threadIdx.x & 7;
-    const float v = (m == 0) ? 0.f : (m == 1) ? 0.5f : (m == 2) ? 1.f : (m == 3) ? 1.5f
-                  : (m == 4) ? 2.f : (m == 5) ? 3.f : (m == 6) ? 4.f : 6.f;
-    s_lut[threadIdx.x] = (threadIdx.x & 8) ? -v : v;
-  }
   if (threadIdx.x == 32 * kWarpTma) {
+    // quantised weights: a raw stage is drained, and an A stage filled, by
+    // the four warps of one converter group
+    const uint32_t group = p.wfmt == kWBf16 ? 1u : 4u;
     for (int i = 0; i < p.nr; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 1);
+      mbar_init(&raw_empty[i], group);
     }
     for (int i = 0; i < p.na; ++i) {
-      mbar_init(&a_full[i], 1);
+      mbar_init(&a_full[i], group);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < p.nb; ++i) {
@@ -267,12 +258,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], static_cast<uint32_t>(p.n_issuers));
       mbar_init(&acc_empty[i], 4);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, static_cast<uint32_t>(p.n_issuers));
     fence_mbar_init();
-    tma_prefetch_desc(&wmap);
+    if (p.wfmt == kWBf16) tma_prefetch_desc(&wmap);   // quantised weights use bulk copies
     tma_prefetch_desc(&bmap);
   }
   if (warp == kWarpMma) {
@@ -290,16 +281,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ weight TMA producer
     if (lane == 0) {
       bool ok = true;
-      const uint32_t rowbytes = p.wfmt == kWFp8 ? 64u : 32u;
-      const uint32_t rpb = 128u * rowbytes;
-      // raw stage s feeds A stage s (one ring): each raw stage is drained by
-      // exactly one dequantiser warp, which steps through its phases in order
-      Ring ring(p.na);
+      // k-block i of this CTA goes to raw stage i % nr (nr even), drained by
+      // converter group i % 2, whose warps step through its phases in order.
+      // BF16 tiles go straight to shared-memory A stages.
+      Ring ring(p.wfmt == kWBf16 ? p.na : p.nr);
       uint64_t* full = p.wfmt == kWBf16 ? a_full : raw_full;
       uint64_t* empty = p.wfmt == kWBf16 ? a_empty : raw_empty;
       int issued = 0;
+      Tile tl2{0, 0, 0, 0};
+      if (blockIdx.x < total) tl2 = decode_tile(blockIdx.x, prefix, p);
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        const Tile tl = decode_tile(t, prefix, p);
+        const Tile tl = tl2;   // decoded one tile ahead
+        if (t + gridDim.x < total) tl2 = decode_tile(t + gridDim.x, prefix, p);
         const int wrow = tl.e * planes * p.feat_pad + tl.ft * p.feat_tile;
         for (int kb = 0; kb < p.nkb; ++kb, ring.next(), ++issued) {
           const int s = ring.idx;
@@ -313,11 +306,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(dst, &wmap, &full[s], kb * 64, wrow);
             if (p.gated) tma_load_2d(dst + 64 * 128, &wmap, &full[s], kb * 64, wrow + p.feat_pad);
           } else {
-            mbar_arrive_expect_tx(&full[s], rpb);
-            uint8_t* dst = sbase + p.raw_off + s * rpb;
-            const int c0 = kb * static_cast<int>(rowbytes);
-            tma_load_2d(dst, &wmap, &full[s], c0, wrow);
-            if (p.gated) tma_load_2d(dst + 64 * rowbytes, &wmap, &full[s], c0, wrow + p.feat_pad);
+            const long long blob = (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb + kb;
+            mbar_arrive_expect_tx(&full[s], p.blob_bytes);
+            bulk_load(sbase + p.raw_off + s * p.stage_bytes, p.wblob + blob * p.blob_bytes,
+                      p.blob_bytes, &full[s]);
           }
         }
       }
@@ -325,33 +317,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = max(0, issued - ring.n); i < issued; ++i)
         wait_bounded(&full[i % ring.n], (i / ring.n) & 1, p.status, 32);
     }
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------ MMA issuer
+  } else if (warp == kWarpMma || (warp == kWarpMma2 && p.n_issuers == 2)) {
+    // ------------------------------------------------ MMA issuers
+    // With two issuers, issuer j (warp 1 or 3) takes the CTA's k-blocks
+    // i = j, j + 2, ... (the A stages converter group j fills) and
+    // accumulates k-block i into bank i % nacc (nacc even), so the two never
+    // share an accumulator; each one alone costs about 75 cycles per MMA of
+    // issue time, two overlap. Both commit to acc_full.
     if (lane == 0) {
+      const int step = p.n_issuers;
+      const int j = warp == kWarpMma ? 0 : 1;
       const uint32_t idesc = idesc_bf16_f32(128, p.bn);
-      Ring ra(p.na), rb(p.nb);
+      Ring ra(p.na / step), rb(p.nb / step);
       int tc = 0;
+      int i0 = 0;   // CTA-wide index of the tile's first k-block
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc) {
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc, i0 += p.nkb) {
         const int slot = tc & 1;
         if (!wait_bounded(&acc_empty[slot], ((tc >> 1) & 1) ^ 1, p.status)) break;
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(slot * p.bn);
-        for (int kb = 0; kb < p.nkb; ++kb, ra.next(), rb.next()) {
-          if (!wait_bounded(&a_full[ra.idx], ra.phase, p.status) ||
-              !wait_bounded(&b_full[rb.idx], rb.phase, p.status)) {
+        // tile slot `slot` owns accumulator banks slot * nacc .. + nacc - 1.
+        // Stages are released two of this issuer's k-blocks at a time: a
+        // commit costs about as much as an MMA, back-to-back commits about one.
+        const uint32_t d0 = tmem + static_cast<uint32_t>(slot * p.nacc * p.bn);
+        int pa0 = 0, pa1 = 0, pb0 = 0, pb1 = 0, npend = 0;
+        const int kb0 = (j - i0) & (step - 1);   // step is 1 or 2
+        for (int kb = kb0; kb < p.nkb; kb += step) {
+          const int bank = (i0 + kb) & (p.nacc - 1);   // nacc is 1, 2 or 4
+          const bool first = kb < p.nacc;   // this bank's first k-block of the tile
+          const uint32_t d = d0 + static_cast<uint32_t>(bank * p.bn);
+          const int sa = j + step * ra.idx, sb = j + step * rb.idx;
+          if (!wait_spin(&a_full[sa], ra.phase, p.status) ||
+              !wait_spin(&b_full[sb], rb.phase, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = sdesc_k_sw128(base_u32 + p.a_off + ra.idx * kATile);
-          const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + rb.idx * p.bn * 128);
+          const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + sb * p.bn * 128);
+          if (p.wfmt == kWBf16) {
+            const uint64_t adesc = sdesc_k_sw128(base_u32 + p.a_off + sa * kATile);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&a_empty[ra.idx]);
-          umma_commit(&b_empty[rb.idx]);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
+          } else {
+            const uint32_t at = tmem + p.a_col0 + static_cast<uint32_t>(sa) * kAStageCols;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_tmem_a(d, at + 8 * kk, bdesc + 2 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
+          }
+          if (npend == 0) {
+            pa0 = sa;
+            pb0 = sb;
+          } else {
+            pa1 = sa;
+            pb1 = sb;
+          }
+          ++npend;
+          ra.next();
+          rb.next();
+          if (npend == 2 || kb + step >= p.nkb) {
+            umma_commit(&a_empty[pa0]);
+            if (npend == 2) umma_commit(&a_empty[pa1]);
+            umma_commit(&b_empty[pb0]);
+            if (npend == 2) umma_commit(&b_empty[pb1]);
+            npend = 0;
+          }
         }
+        if (!ok) break;
         umma_commit(&acc_full[slot]);
       }
       // all issued MMAs have finished before TMEM is released
@@ -360,20 +392,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpB) {
     // ------------------------------------------------ token-row TMA producer
+    // The gathered rows' token ids of the next tile are loaded while this
+    // tile's k-blocks are issued.
     Ring ring(p.nb);
     int issued = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-      const Tile tl = decode_tile(t, prefix, p);
-      int tok[2][4];
+    int tok[2][4], nxt[2][4];
+    auto load_tok = [&](const Tile& tl_, int (&d)[2][4]) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int q4 = (lane + 32 * j) * 4;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int r = (q4 + i < tl.nrows) ? q4 + i : 0;   // padding rows repeat row 0
-          tok[j][i] = (p.b_gather && q4 < p.bn) ? p.b_map[tl.row0 + r] / p.b_div : 0;
+          const int r = (q4 + i < tl_.nrows) ? q4 + i : 0;   // padding rows repeat row 0
+          d[j][i] = (p.b_gather && q4 < p.bn) ? p.b_map[tl_.row0 + r] / p.b_div : 0;
         }
+      }
+    };
+    int t = blockIdx.x;
+    Tile tl{0, 0, 0, 0};
+    if (t < total) {
+      tl = decode_tile(t, prefix, p);
+      load_tok(tl, tok);
+    }
+    for (; ok && t < total; t += gridDim.x) {
+      const int t2 = t + gridDim.x;
+      Tile tl2 = tl;
+      if (t2 < total) {
+        tl2 = decode_tile(t2, prefix, p);
+        load_tok(tl2, nxt);
       }
       for (int kb = 0; kb < p.nkb; ++kb, ring.next(), ++issued) {
         const int s = ring.idx;
@@ -396,6 +443,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(dst, &bmap, &b_full[s], kb * 64, tl.row0);
         }
       }
+      tl = tl2;
+      if (t2 < total) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) tok[j][i] = nxt[j][i];
+      }
     }
     if (lane == 0)
       for (int i = max(0, issued - p.nb); i < issued; ++i)
@@ -414,8 +468,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* rowv = reinterpret_cast<float*>(sbase + p.x_off + 16384);             // [256] f32
     int tc = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
+      // tile bookkeeping and bias first: their loads overlap the accumulator wait
       const Tile tl = decode_tile(t, prefix, p);
       const int slot = tc & 1;
+      const int fl = p.gated ? (q & 1) * 32 + lane : q * 32 + lane;
+      const int f = tl.ft * (p.gated ? 64 : 128) + fl;
+      const bool fvalid = f < p.n_feat;
+      float b0 = 0.f, b1 = 0.f;
+      if (p.bias != nullptr && fvalid) {
+        if (p.gated) {
+          b0 = __bfloat162float(p.bias[(long long)(tl.e * 2) * p.feat_pad + f]);
+          b1 = __bfloat162float(p.bias[(long long)(tl.e * 2 + 1) * p.feat_pad + f]);
+        } else {
+          b0 = __bfloat162float(p.bias[(long long)tl.e * p.feat_pad + f]);
+        }
+      }
+      const int bank0 = (tc * p.nkb) & (p.nacc - 1);
       // the four epilogue warps agree on success before using their barrier
       const bool ok =
           named_bar_and(1, 128, wait_bounded(&acc_full[slot], (tc >> 1) & 1, p.status, 128));
@@ -423,21 +491,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int ncols = (tl.nrows + 15) & ~15;
       if (p.gated) {
-        const int fl = (q & 1) * 32 + lane;
-        const int f = tl.ft * 64 + fl;
-        const bool fvalid = f < p.n_feat;
-        float bg = 0.f, bu = 0.f;
-        if (p.bias != nullptr && fvalid) {
-          bg = __bfloat162float(p.bias[(long long)(tl.e * 2) * p.feat_pad + f]);
-          bu = __bfloat162float(p.bias[(long long)(tl.e * 2 + 1) * p.feat_pad + f]);
-        }
+        const float bg = b0, bu = b1;
         const int jb = (q >> 1) * 8;
         for (int c0 = 0, ci = 0; c0 < ncols; c0 += 16, ++ci) {
-          uint32_t r[16];
-          tmem_ld16(tq + slot * p.bn + c0, r);
-          tmem_ld_wait();
+          float acc[16];
+          load_acc(tq + slot * p.nacc * p.bn + c0, p.bn, bank0, p.nacc, p.nbanks, acc);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xbuf[(q * 16 + j) * 32 + lane] = __uint_as_float(r[j]);
+          for (int j = 0; j < 16; ++j) xbuf[(q * 16 + j) * 32 + lane] = acc[j];
           named_bar_sync(1, 128);
           uint16_t* st = stage + (ci & 1) * 16 * 64;     // [16][64]
 #pragma unroll
@@ -456,11 +516,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<const uint4*>(st + j * 64 + c8);
         }
       } else {
-        const int fl = q * 32 + lane;
-        const int f = tl.ft * 128 + fl;
-        const bool fvalid = f < p.n_feat;
-        float b0 = 0.f;
-        if (p.bias != nullptr && fvalid) b0 = __bfloat162float(p.bias[(long long)tl.e * p.feat_pad + f]);
         const bool scaled = p.row_w != nullptr;
         if (scaled) {
           for (int i = te; i < tl.nrows; i += 128) {
@@ -472,13 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_bar_sync(1, 128);
         }
         for (int c0 = 0, ci = 0; c0 < ncols; c0 += 16, ++ci) {
-          uint32_t r[16];
-          tmem_ld16(tq + slot * p.bn + c0, r);
-          tmem_ld_wait();
+          float acc[16];
+          load_acc(tq + slot * p.nacc * p.bn + c0, p.bn, bank0, p.nacc, p.nbanks, acc);
           uint16_t* st = stage + (ci & 1) * 16 * 128;    // [16][128]
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            float y = bf16_rn(__uint_as_float(r[j]));
+            float y = bf16_rn(acc[j]);
             if (p.bias != nullptr) y = bf16_rn(y + b0);
             if (scaled) y = bf16_rn(y * rowv[c0 + j]);
             st[j * 128 + fl] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
@@ -499,118 +553,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[slot]);
     }
-  } else if (warp >= kWarpConv && warp < kWarpConv + p.na && p.wfmt != kWBf16) {
-    // ------------------------------------------------ dequantisers
-    // Warp w owns A stage w and converts this CTA's k-blocks w, w + na,
-    // w + 2 na, ... on its own (16 fp8 chunks or 8 mxfp4 groups per lane),
-    // so na k-blocks are converted concurrently with no cross-warp barrier.
-    const int w = warp - kWarpConv;
-    const int kb_per_sc = (p.wfmt == kWFp8 && p.sc_bc % 64 == 0) ? p.sc_bc / 64 : 0;
-    int t = blockIdx.x, kb = w, it = w, uses = 0, cur_t = -1;
-    Tile tl{0, 0, 0, 0};
-    const float* srow[2] = {nullptr, nullptr};   // gate/first-half and up/second-half scale rows
-    const uint8_t* mscale = nullptr;
-    while (true) {
+  } else if (warp >= kWarpConv && p.wfmt != kWBf16) {
+    // ------------------------------------------------ converters
+    // Group g = (warp - 8) / 4 converts the CTA's k-blocks g, g + 2, ...;
+    // within a k-block, lane i of warp w converts weight row 32 (w % 4) + i
+    // (64 values) and stores it to TMEM lane 32 (w % 4) + i of A stage
+    // g + 2 j. Raw stages g + 2 j are read back conflict-free through the
+    // packing's chunk permutation.
+    const int g = (warp - kWarpConv) >> 2;
+    const int qw = warp & 3;
+    const int row = qw * 32 + lane;
+    const int half = row >> 6;                           // gate/up plane or down half
+    const uint32_t tq = tmem + (static_cast<uint32_t>(qw * 32) << 16) + p.a_col0;
+    int t = blockIdx.x, kb = g;
+    while (kb >= p.nkb) {
+      kb -= p.nkb;
+      t += gridDim.x;
+    }
+    Ring rr(p.nr / 2), ar(p.na / 2);
+    while (t < total) {
+      const int rs = g + 2 * rr.idx;
+      const int as = g + 2 * ar.idx;
+      // polls with a short sleep: prompt when the converters run level with
+      // the MMA (prefill), few issue slots taken from the MMA warps otherwise
+      if (!wait_spin(&raw_full[rs], rr.phase, p.status, 32) ||
+          !wait_spin(&a_empty[as], ar.phase ^ 1u, p.status, 32)) break;
+      tc_fence_after();
+      const uint8_t* stage = sbase + p.raw_off + rs * p.stage_bytes;
+      uint32_t o[32];
+      if (p.wfmt == kWFp8) {
+        const uint8_t* raw = stage + row * 64;
+        const float* sc = reinterpret_cast<const float*>(stage + kRawFp8);
+        const int sw = (row >> 1) & 3;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
+          const float scale = p.scale_form == kScaleHalf ? sc[half] : sc[row * 4 + c];
+          fp8x16_cvt(qv, scale, *reinterpret_cast<uint32_t(*)[8]>(o + 8 * c));
+        }
+      } else {
+        const uint8_t* raw = stage + row * 32;
+        const int sw = (row >> 2) & 1;
+        const uint32_t sx = *reinterpret_cast<const unsigned short*>(stage + kRawMx + row * 2);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
+          mx32_cvt(qv, (sx >> (8 * c)) & 0xffu, *reinterpret_cast<uint32_t(*)[16]>(o + 16 * c));
+        }
+      }
+      // the raw bytes and scales are in registers: release the stage to the TMA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      tmem_st32(tq + static_cast<uint32_t>(as) * kAStageCols, o);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[as]);
+      rr.next();
+      ar.next();
+      kb += 2;
       while (kb >= p.nkb) {
         kb -= p.nkb;
         t += gridDim.x;
       }
-      if (t >= total) break;
-      if (t != cur_t) {
-        cur_t = t;
-        tl = decode_tile(t, prefix, p);
-        if (p.wfmt == kWFp8) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            // rows 64h..64h+63: a plane of the gated tile, or half the down tile
-            const int pl = p.gated ? h : 0;
-            const int f = tl.ft * p.feat_tile + (p.gated ? 0 : 64 * h);
-            const int sri = min(min(f, p.n_feat - 1) / p.sc_br, p.sc_nbr - 1);
-            srow[h] = p.fp8_scale + ((long long)(tl.e * planes + pl) * p.sc_nbr + sri) * p.sc_nbc;
-          }
-        } else {
-          mscale = p.mx_scale + (long long)(tl.e * planes) * p.feat_pad * p.mx_groups;
-        }
-      }
-      // raw stage w and A stage w are used only by this warp, once per `uses`,
-      // so the phase this warp waits for is never more than one ahead
-      const int sr = w;
-      if (!wait_bounded(&raw_full[sr], uses & 1, p.status) ||
-          !wait_bounded(&a_empty[w], (uses & 1) ^ 1, p.status)) break;
-      uint8_t* astage = sbase + p.a_off + w * kATile;
-      if (p.wfmt == kWFp8) {
-        const uint8_t* raw = sbase + p.raw_off + sr * kRawFp8;
-        // uniform scale per half-tile when the scale block covers it
-        const bool uni = kb_per_sc != 0 && p.sc_br % 64 == 0;
-        float sh[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) sh[h] = uni ? __ldg(srow[h] + min(kb / kb_per_sc, p.sc_nbc - 1)) : 0.f;
-#pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
-          const int item = lane + 32 * j;
-          const int row = item >> 2;
-          const int v = item & 3;
-          const uint4 qv = *reinterpret_cast<const uint4*>(raw + row * 64 + v * 16);
-          float scale;
-          if (uni) {
-            scale = (j >> 3) ? sh[1] : sh[0];
-          } else {
-            const int pl = p.gated ? (row >> 6) : 0;
-            const int f = tl.ft * p.feat_tile + (p.gated ? (row & 63) : row);
-            const int sri = min(min(f, p.n_feat - 1) / p.sc_br, p.sc_nbr - 1);
-            const int sci = min((kb * 64 + v * 16) / p.sc_bc, p.sc_nbc - 1);
-            scale = __ldg(p.fp8_scale + ((long long)(tl.e * planes + pl) * p.sc_nbr + sri) * p.sc_nbc + sci);
-          }
-          uint32_t o[8];
-          if (scale < 256.f) {
-            const float s120 = scale * 0x1p120f;
-            fp8x4_scaled(qv.x, s120, o[0], o[1]);
-            fp8x4_scaled(qv.y, s120, o[2], o[3]);
-            fp8x4_scaled(qv.z, s120, o[4], o[5]);
-            fp8x4_scaled(qv.w, s120, o[6], o[7]);
-          } else {
-            fp8x16_to_bf16(qv, scale, o);
-          }
-          *reinterpret_cast<uint4*>(astage + swz(row, 2 * v)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(astage + swz(row, 2 * v + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-        }
-      } else {
-        const uint8_t* raw = sbase + p.raw_off + sr * kRawMx;
-#pragma unroll 4
-        for (int j = 0; j < 8; ++j) {
-          const int item = lane + 32 * j;
-          const int row = item >> 1;
-          const int g = item & 1;
-          const uint4 qv = *reinterpret_cast<const uint4*>(raw + row * 32 + g * 16);
-          const int pl = p.gated ? (row >> 6) : 0;
-          const int f = tl.ft * p.feat_tile + (p.gated ? (row & 63) : row);
-          const uint32_t sexp =
-              __ldg(mscale + ((long long)pl * p.feat_pad + f) * p.mx_groups + kb * 2 + g);
-          uint32_t o[16];
-          if (sexp <= 128u) {
-            const float s = __uint_as_float((sexp + 126u) << 23);
-            mx8_scaled(qv.x, s, *reinterpret_cast<uint32_t(*)[4]>(o));
-            mx8_scaled(qv.y, s, *reinterpret_cast<uint32_t(*)[4]>(o + 4));
-            mx8_scaled(qv.z, s, *reinterpret_cast<uint32_t(*)[4]>(o + 8));
-            mx8_scaled(qv.w, s, *reinterpret_cast<uint32_t(*)[4]>(o + 12));
-          } else {
-            mx32_to_bf16(qv, ue8m0_to_f32(sexp), s_lut, o);
-          }
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            *reinterpret_cast<uint4*>(astage + swz(row, 4 * g + q4)) =
-                make_uint4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&raw_empty[sr]);
-        mbar_arrive(&a_full[w]);
-      }
-      it += p.na;
-      kb += p.na;
-      ++uses;
     }
   }
   tc_fence_before();

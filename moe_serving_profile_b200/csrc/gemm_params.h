@@ -14,10 +14,14 @@ struct GemmParams {
   // weights (MMA A): 128 rows per tile. Gated: 64 gate + 64 up rows of the
   // same 64 features; down: 128 features.
   int wfmt, gated, feat_tile, feat_tiles, feat_pad, n_feat, k_pad, nkb;
-  const float* fp8_scale;
-  int sc_br, sc_bc, sc_nbr, sc_nbc;
-  const uint8_t* mx_scale;
-  int mx_groups;
+  // quantised weights: one blob per (expert, feature tile, k-block) of
+  // blob_bytes (128 rows of e4m3 / e2m1 bytes, then the k-block's scales in
+  // form scale_form: 0 FP8 one fp32 per 64-row half, 1 FP8 fp32 per (row,
+  // 16-column chunk), 2 MXFP4 two ue8m0 bytes per row), staged in shared
+  // memory every stage_bytes
+  const uint8_t* wblob;
+  uint32_t blob_bytes, stage_bytes;
+  int scale_form;
   // activations (MMA B): rows gathered by token (b_map / b_div) or contiguous
   int b_gather;
   const int* b_map;
@@ -32,9 +36,17 @@ struct GemmParams {
   __nv_bfloat16* out;
   long long ldo;
   int* status;
-  // shared-memory plan
+  // pipeline plan: nr raw weight stages in shared memory (quantised
+  // weights), na A stages (BF16 weights: shared memory; quantised weights:
+  // tensor memory at column a_col0, 32 columns each), nb token-row stages
   int nr, na, nb;
-  uint32_t raw_off, a_off, b_off, x_off, bar_off, tmem_cols;
+  // accumulator banks per tile: CTA-wide k-block i accumulates into bank
+  // i % nacc (independent MMA chains; the epilogue adds the banks in order);
+  // banks used per tile = min(nacc, nkb)
+  int nacc, nbanks;
+  // MMA issuer threads (2 when nacc is even: k-block i goes to issuer i % 2)
+  int n_issuers;
+  uint32_t raw_off, a_off, b_off, x_off, bar_off, tmem_cols, a_col0;
 };
 
 // Address of the grouped GEMM kernel (for cudaLaunchKernelExC).

@@ -96,6 +96,39 @@ B200_DEVI bool wait_bounded(uint64_t* bar, uint32_t parity, int* status, unsigne
   }
 }
 
+B200_DEVI bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// wait_bounded for waiters on the critical path: polls with the non-blocking
+// test_wait, so the thread sees the phase complete within one short sleep
+// instead of after a suspended try_wait resumes; the sleep between polls
+// leaves the scheduler's issue slots to the warps being waited for. Same
+// limit and status on timeout.
+B200_DEVI bool wait_spin(uint64_t* bar, uint32_t parity, int* status, unsigned sleep_ns = 20) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      __nanosleep(sleep_ns);
+      if (mbar_test_wait(bar, parity)) return true;
+    }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicOr(status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (TMA, tcgen05.mma) before signalling a barrier.
 B200_DEVI void fence_proxy_async_smem() {
@@ -110,6 +143,16 @@ B200_DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Contiguous global -> shared copy by the TMA engine (both addresses 16-byte
+// aligned, bytes a multiple of 16), completing on `bar`'s transaction count.
+B200_DEVI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -224,6 +267,18 @@ B200_DEVI void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32
       : "memory");
 }
 
+// As umma_bf16 with the A operand (128 rows x 16 k, row r in TMEM lane r,
+// two bf16 per 32-bit column) read from tensor memory at tmem_a.
+B200_DEVI void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread
 // has completed.
 B200_DEVI void umma_commit(uint64_t* bar) {
@@ -246,6 +301,22 @@ B200_DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 B200_DEVI void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane (32x32b shape:
+// warp w writes lanes 32 * (w % 4) .. + 31, thread i lane 32 * (w % 4) + i).
+B200_DEVI void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+B200_DEVI void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- cluster
 B200_DEVI uint32_t cluster_ctarank() {

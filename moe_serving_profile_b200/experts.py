@@ -28,14 +28,20 @@ def _sm_count(device: int) -> int:
     return torch.cuda.get_device_properties(device).multi_processor_count
 
 
-def tile_policy(T: int, K: int, num_experts: int) -> int:
+def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256) -> int:
     """Token tile (the MMA N) for one grouped GEMM launch: the smallest power
-    of two in [16, 256] covering the mean rows per expert."""
+    of two in [16, max_tile] covering the mean rows per expert. Quantised
+    weights pass max_tile = 128 (their A tiles share tensor memory with the
+    accumulators)."""
     rows = T * K / num_experts
     bn = 16
-    while bn < 256 and bn < rows:
+    while bn < max_tile and bn < rows:
         bn *= 2
     return bn
+
+
+def _max_tile(w: ExpertWeights) -> int:
+    return 256 if w.fmt == _lib.W_BF16 else 128
 
 
 def run_experts(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
@@ -63,7 +69,7 @@ def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K:
     T = hidden.shape[0] if tokens is None else tokens
     R = perm.perm_src.numel()
     dev = hidden.device
-    bn = tile_policy(T, K, num_experts)
+    bn = tile_policy(T, K, num_experts, _max_tile(w))
     div = K if b_map_div is None else b_map_div
     act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16) if out is None else out
     if bn >= 64:
@@ -75,9 +81,7 @@ def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K:
         b_src, b_map, b_div = hidden, perm.perm_src, div
     ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
                     max_rows=R, wfmt=w.fmt, planes=2, feat_pad=w.i_pad, n_feat=w.inter,
-                    k_pad=w.h_k, weight=w.w1,
-                    fp8_scale=w.s1 if w.fmt == _lib.W_FP8 else None, fp8_block=w.block,
-                    mx_scale=w.s1 if w.fmt == _lib.W_MXFP4 else None, b_src=b_src,
+                    k_pad=w.h_k, weight=w.w1, fp8_block=w.block, b_src=b_src,
                     k_valid=hidden.shape[1], b_map=b_map, b_div=b_div,
                     epilogue=w.gated_epilogue, bias=w.b1, alpha=w.alpha, limit=w.limit, out=act,
                     token_tile=bn)
@@ -90,14 +94,12 @@ def down(w: ExpertWeights, act: torch.Tensor, perm: ops.Permutation,
     """Down projection of the gated rows, scaled by the routing weights."""
     R = perm.perm_src.numel()
     dev = act.device
-    bn = tile_policy(tokens, K, num_experts)
+    bn = tile_policy(tokens, K, num_experts, _max_tile(w))
     if contrib is None:
         contrib = torch.empty(R, w.hidden, device=dev, dtype=torch.bfloat16)
     ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
                     max_rows=R, wfmt=w.fmt, planes=1, feat_pad=w.h_f, n_feat=w.hidden,
-                    k_pad=w.i_pad, weight=w.w2,
-                    fp8_scale=w.s2 if w.fmt == _lib.W_FP8 else None, fp8_block=w.block,
-                    mx_scale=w.s2 if w.fmt == _lib.W_MXFP4 else None, b_src=act,
+                    k_pad=w.i_pad, weight=w.w2, fp8_block=w.block, b_src=act,
                     k_valid=w.inter, epilogue=_lib.EPI_DOWN, bias=w.b2,
                     row_weight=None if weights is None else weights.reshape(-1),
                     row_src=perm.perm_src, out=contrib, token_tile=bn)

@@ -152,8 +152,7 @@ def permute_noalloc(indices: torch.Tensor, num_experts: int, out: Permutation) -
 # --------------------------------------------------------------------------- grouped GEMM
 def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max_rows: int,
                 wfmt: int, planes: int, feat_pad: int, n_feat: int, k_pad: int,
-                weight: torch.Tensor, fp8_scale: torch.Tensor | None = None,
-                fp8_block: tuple[int, int] = (128, 128), mx_scale: torch.Tensor | None = None,
+                weight: torch.Tensor, fp8_block: tuple[int, int] = (128, 128),
                 b_src: torch.Tensor, k_valid: int, b_map: torch.Tensor | None = None,
                 b_rows: int | None = None,
                 b_div: int = 1, epilogue: int, bias: torch.Tensor | None = None,
@@ -176,11 +175,7 @@ def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max
     a.n_feat = n_feat
     a.k_pad = k_pad
     a.weight = _ptr(weight)
-    if fp8_scale is not None:
-        a.fp8_scale = _ptr(fp8_scale)
-        a.sc_br, a.sc_bc = fp8_block
-        a.sc_nbr, a.sc_nbc = fp8_scale.shape[-2], fp8_scale.shape[-1]
-    a.mx_scale = _ptr(mx_scale)
+    a.sc_br, a.sc_bc = fp8_block
     a.b_src = _ptr(b_src)
     a.ldb = b_src.stride(0)
     a.b_rows = b_src.shape[0] if b_rows is None else b_rows

@@ -118,12 +118,14 @@ def test_fp8_layout_pads_with_zeros():
     gate, up, down = mk(E, I, H), mk(E, I, H), mk(E, H, I)
     sc = lambda r, c: torch.rand(E, (r + 127) // 128, (c + 127) // 128, generator=g)
     w = layout.fp8_experts(gate, sc(I, H), up, sc(I, H), down, sc(H, I), (128, 128))
-    assert w.w1.shape == (E, 2, 256, 256) and w.w2.shape == (E, 256, 256)
-    assert torch.equal(w.w1[:, 0, :I, :H], gate.view(torch.uint8))
-    assert torch.equal(w.w1[:, 1, :I, :H], up.view(torch.uint8))
-    assert int(w.w1[:, :, I:].sum()) == 0 and int(w.w1[:, :, :, H:].sum()) == 0
-    assert torch.equal(w.w2[:, :H, :I], down.view(torch.uint8)) and int(w.w2[:, H:].sum()) == 0
-    assert w.s1.shape == (E, 2, 2, 2) and w.s1.dtype == torch.float32
+    # blobs: [E, feature tiles, k-blocks, 128 rows x 64 B + 16 B of scales]
+    assert w.w1.shape == (E, 256 // 64, 256 // 64, 8208) and w.w2.shape == (E, 256 // 128, 256 // 64, 8208)
+    w1 = layout.unpack_blob_rows(w.w1, 64, 2)
+    w2 = layout.unpack_blob_rows(w.w2, 64, 1)[:, 0]
+    assert torch.equal(w1[:, 0, :I, :H], gate.view(torch.uint8))
+    assert torch.equal(w1[:, 1, :I, :H], up.view(torch.uint8))
+    assert int(w1[:, :, I:].sum()) == 0 and int(w1[:, :, :, H:].sum()) == 0
+    assert torch.equal(w2[:, :H, :I], down.view(torch.uint8)) and int(w2[:, H:].sum()) == 0
 
 
 def test_gpt_oss_mxfp4_layout_deinterleaves_gate_up():
@@ -137,11 +139,15 @@ def test_gpt_oss_mxfp4_layout_deinterleaves_gate_up():
     dn_bias = torch.randn(E, H, generator=g)
     w = layout.gpt_oss_mxfp4_experts(gu_b, gu_s, gu_bias, dn_b, dn_s, dn_bias, 1.702, 7.0)
     assert w.i_pad == 128 and w.h_k == 128 and w.h_f == 128
-    assert torch.equal(w.w1[:, 0, :I, : H // 2], gu_b[:, 0::2].reshape(E, I, H // 2))
-    assert torch.equal(w.w1[:, 1, :I, : H // 2], gu_b[:, 1::2].reshape(E, I, H // 2))
-    assert torch.equal(w.s1[:, 1, :I, : H // 32], gu_s[:, 1::2])
-    assert bool((w.s1[:, :, I:] == 127).all()) and bool((w.s1[:, :, :, H // 32:] == 127).all())
-    assert bool((w.s2[:, :, I // 32:] == 127).all())
+    assert w.w1.shape == (E, 2, 2, 4352) and w.w2.shape == (E, 1, 2, 4352)
+    w1 = layout.unpack_blob_rows(w.w1, 32, 2)
+    assert torch.equal(w1[:, 0, :I, : H // 2], gu_b[:, 0::2].reshape(E, I, H // 2))
+    assert torch.equal(w1[:, 1, :I, : H // 2], gu_b[:, 1::2].reshape(E, I, H // 2))
+    # scales after the data: [128 rows][2 groups] per (tile, k-block)
+    s1 = w.w1[..., 4096:].reshape(E, 2, 2, 2, 64, 2)        # [E, ft, kb, plane, row, group]
+    s1 = s1.permute(0, 3, 1, 4, 2, 5).reshape(E, 2, 128, 4)  # [E, plane, feature, group]
+    assert torch.equal(s1[:, 1, :I, : H // 32], gu_s[:, 1::2])
+    assert bool((s1[:, :, I:] == 127).all()) and bool((s1[:, :, :, H // 32:] == 127).all())
     assert torch.equal(w.b1[:, 0, :I], gu_bias[:, 0::2].bfloat16())
     assert w.gated_epilogue == _lib.EPI_CLAMP_SWIGLU
 
