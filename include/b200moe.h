@@ -155,8 +155,9 @@ int b200moe_permute_noalloc(int device, void* stream, const long long* indices, 
  *     fp32 scales of rows 0-63 and 64-127 then 8 zero bytes (blob 8208 B);
  *     other FP8 blocks, fp32 [128 rows][4 chunks of 16 columns] (blob
  *     10240 B); MXFP4, ue8m0 [128 rows][2 groups of 32 columns] (blob 4352 B).
- * Quantised weights are converted by the CTA into tensor memory, which
- * limits token_tile to 128 for them (B200MOE_ERR_UNSUPPORTED above).
+ * Quantised weights are converted by the CTA into tensor memory; with a
+ * 256-token tile the accumulator then has one slot (the epilogue of a tile
+ * does not overlap the next tile's main loop).
  * Epilogues:
  *   B200MOE_EPI_SWIGLU     bf16(bf16(silu(bf16 g)) * bf16 u)
  *                          (moe_serving/qwen3_parallel.py:84-94)
@@ -185,7 +186,7 @@ typedef struct b200moe_gemm_args {
   int expert_begin;     /* first global expert id handled by this launch */
   int n_experts;        /* local experts in the weight stack */
   int max_rows;         /* upper bound on rows of these experts (T*K) */
-  int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 (BF16 only) */
+  int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 */
   int split_k;          /* reserved: must be 0 or 1 */
   /* weights (A operand) */
   int wfmt;             /* B200MOE_W_* */

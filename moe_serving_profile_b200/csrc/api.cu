@@ -257,16 +257,14 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   if (rc) return rc;
 
   const bool gated = a->planes == 2;
-  // quantised weights keep their converted A tiles in tensor memory next to
-  // the accumulators, which caps the token tile at 128 columns
-  const int max_bn = a->wfmt == B200MOE_W_BF16 ? 256 : 128;
-  if (a->token_tile > max_bn)
-    return fail(B200MOE_ERR_UNSUPPORTED, "token_tile %d exceeds %d for this weight format",
-                a->token_tile, max_bn);
   int bn = a->token_tile;
   if (bn == 0) {
+    // quantised weights: 256-token tiles would leave a single accumulator
+    // slot (their A stages hold the other half of tensor memory), which
+    // measured slower than two 128-token tiles
+    const int max_auto = a->wfmt == B200MOE_W_BF16 ? 256 : 128;
     const int avg = (a->max_rows + a->n_experts - 1) / a->n_experts;
-    bn = std::min(max_bn, std::max(16, pow2_ceil(avg)));
+    bn = std::min(max_auto, std::max(16, pow2_ceil(avg)));
   }
   const int feat_tile = gated ? 64 : 128;
   const int feat_tiles = a->feat_pad / feat_tile;
@@ -364,10 +362,13 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   // banks x bn columns stay within the 256 columns below the A stages
   p.nacc = std::max(1, std::min(4, 128 / bn));
   p.nbanks = std::min(p.nacc, p.nkb);
+  // quantised weights keep their A stages in TMEM columns 256..511, so a
+  // 256-token tile gets a single accumulator slot
+  p.acc_slots = (rpb && bn > 128) ? 1 : 2;
   // two MMA issuers when there are banks for both and the A / B rings split
   // evenly between them
   p.n_issuers = (p.nacc % 2 == 0 && na % 2 == 0 && nb % 2 == 0) ? 2 : 1;
-  p.tmem_cols = rpb ? 512u : static_cast<uint32_t>(std::max(32, pow2_ceil(2 * p.nacc * bn)));
+  p.tmem_cols = rpb ? 512u : static_cast<uint32_t>(std::max(32, pow2_ceil(p.acc_slots * p.nacc * bn)));
   p.a_col0 = 256u;
 
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();

@@ -333,8 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int i0 = 0;   // CTA-wide index of the tile's first k-block
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc, i0 += p.nkb) {
-        const int slot = tc & 1;
-        if (!wait_bounded(&acc_empty[slot], ((tc >> 1) & 1) ^ 1, p.status)) break;
+        // accumulator slots: two (the epilogue of tile t overlaps the main
+        // loop of tile t + 1) or one when a 256-token tile fills them both
+        const int slot = p.acc_slots == 2 ? (tc & 1) : 0;
+        const uint32_t use = p.acc_slots == 2 ? static_cast<uint32_t>(tc >> 1) : static_cast<uint32_t>(tc);
+        if (!wait_bounded(&acc_empty[slot], (use & 1u) ^ 1u, p.status)) break;
         tc_fence_after();
         // tile slot `slot` owns accumulator banks slot * nacc .. + nacc - 1.
         // Stages are released two of this issuer's k-blocks at a time: a
@@ -470,7 +473,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
       // tile bookkeeping and bias first: their loads overlap the accumulator wait
       const Tile tl = decode_tile(t, prefix, p);
-      const int slot = tc & 1;
+      const int slot = p.acc_slots == 2 ? (tc & 1) : 0;
+      const uint32_t use = p.acc_slots == 2 ? static_cast<uint32_t>(tc >> 1) : static_cast<uint32_t>(tc);
       const int fl = p.gated ? (q & 1) * 32 + lane : q * 32 + lane;
       const int f = tl.ft * (p.gated ? 64 : 128) + fl;
       const bool fvalid = f < p.n_feat;
@@ -486,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int bank0 = (tc * p.nkb) & (p.nacc - 1);
       // the four epilogue warps agree on success before using their barrier
       const bool ok =
-          named_bar_and(1, 128, wait_bounded(&acc_full[slot], (tc >> 1) & 1, p.status, 128));
+          named_bar_and(1, 128, wait_bounded(&acc_full[slot], use & 1u, p.status, 128));
       if (!ok) break;
       tc_fence_after();
       const int ncols = (tl.nrows + 15) & ~15;

@@ -46,6 +46,10 @@ struct GemmParams {
   int nacc, nbanks;
   // MMA issuer threads (2 when nacc is even: k-block i goes to issuer i % 2)
   int n_issuers;
+  // accumulator slots (2: tile t + 1 accumulates while tile t's epilogue
+  // drains; 1: 256-token tiles of quantised weights, whose A stages take the
+  // other half of tensor memory)
+  int acc_slots;
   uint32_t raw_off, a_off, b_off, x_off, bar_off, tmem_cols, a_col0;
 };
 

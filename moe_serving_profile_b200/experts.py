@@ -30,9 +30,7 @@ def _sm_count(device: int) -> int:
 
 def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256) -> int:
     """Token tile (the MMA N) for one grouped GEMM launch: the smallest power
-    of two in [16, max_tile] covering the mean rows per expert. Quantised
-    weights pass max_tile = 128 (their A tiles share tensor memory with the
-    accumulators)."""
+    of two in [16, max_tile] covering the mean rows per expert."""
     rows = T * K / num_experts
     bn = 16
     while bn < max_tile and bn < rows:
@@ -41,6 +39,9 @@ def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256) -> int:
 
 
 def _max_tile(w: ExpertWeights) -> int:
+    # quantised weights: two 128-token tiles beat one 256-token tile, whose
+    # accumulator would have a single slot (the A stages hold the other half
+    # of tensor memory)
     return 256 if w.fmt == _lib.W_BF16 else 128
 
 
