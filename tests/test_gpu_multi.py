@@ -1,0 +1,120 @@
+"""Expert parallelism over NCCL on two GPUs (skipped with fewer than two).
+
+* replicated-token EP (qwen3.ParallelExperts with ParallelGroup(2), the
+  reference's --ep-size layout): with numerics="reference" the output on
+  every rank equals the one-GPU layer bit for bit; numerics="fast" stays
+  within the BF16 layer tolerance;
+* token all-to-all (native.routed_forward with ProcessGroupCollective): each
+  rank's output equals native.simulate_routed (all ranks in one process, the
+  same kernels) bit for bit.
+
+Ranks are spawned processes, one per GPU, with a 60 s process-group timeout;
+the parent gives them a bounded time to report.
+"""
+
+import os
+import socket
+from types import SimpleNamespace
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _qwen_module(cfg, w, dev, parallel, numerics):
+    from moe_serving_profile_b200 import qwen3
+
+    conf = SimpleNamespace(num_experts=cfg.experts, hidden_act="silu")
+    m = qwen3.ParallelExperts(conf, parallel, numerics)
+    for i, mods in enumerate(m.local):
+        e = m.start + i
+        mods["gate_proj"] = qwen3.ExpertProjection(w.gate[e].to(dev), w.gate_scale[e].to(dev), cfg.block)
+        mods["up_proj"] = qwen3.ExpertProjection(w.up[e].to(dev), w.up_scale[e].to(dev), cfg.block)
+        mods["down_proj"] = qwen3.ExpertProjection(w.down[e].to(dev), w.down_scale[e].to(dev), cfg.block)
+    return m
+
+
+def _worker(rank: int, port: int, q):
+    try:
+        from datetime import timedelta
+
+        import torch.distributed as dist
+
+        from moe_serving_profile_b200 import native
+        from moe_serving_profile_b200 import synthetic as S
+        from moe_serving_profile_b200.parallel import ParallelGroup
+        from oracle import oracle
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=dev,
+                                timeout=timedelta(seconds=60))
+        res = {}
+        # ---- replicated-token EP
+        cfg = S.CONFIGS["qwen3-30b-a3b"]
+        w = S.make_qwen(cfg, seed=4, device=dev)   # same seed, same values on every GPU
+        T = 64
+        x = S.make_hidden(T, cfg.hidden, seed=5, device=dev)
+        _, scores, idx, _ = oracle.qwen_router(x.cpu(), w.router.cpu(), cfg.top_k, True)
+        scores, idx = scores.to(dev), idx.to(dev)
+        one = _qwen_module(cfg, w, dev, ParallelGroup(1), "reference")(x, idx, scores)
+        pg = ParallelGroup(WORLD)
+        ref_ep = _qwen_module(cfg, w, dev, pg, "reference")(x, idx, scores)
+        fast_ep = _qwen_module(cfg, w, dev, pg, "fast")(x, idx, scores)
+        res["reference_equal"] = bool(torch.equal(ref_ep, one))
+        diff = (fast_ep.float() - one.float())
+        res["fast_rel_l2"] = float(diff.norm() / one.float().norm())
+        # ---- token all-to-all
+        E, H, I, K = 128, 2048, 768, 8
+        g = torch.Generator().manual_seed(7)
+        gate_up = (torch.randn(E, 2 * I, H, generator=g) * 0.02).bfloat16()
+        down = (torch.randn(E, H, I, generator=g) * 0.02).bfloat16()
+        gate = (torch.randn(E, H, generator=g) * 0.02).bfloat16()
+        tokens = [48, 33]
+        hiddens = [torch.randn(t, H, generator=g).bfloat16().to(dev) for t in tokens]
+        el = E // WORLD
+        banks = [native.LocalSwiGLUExperts(gate_up[r * el:(r + 1) * el].to(dev),
+                                           down[r * el:(r + 1) * el].to(dev)) for r in range(WORLD)]
+        routes = [native.route(h, gate.to(dev), K, True) for h in hiddens]
+        sim = native.simulate_routed(hiddens, [r_[0] for r_ in routes], [r_[1] for r_ in routes], banks, E)
+        plan = native.ExpertPlan(E, WORLD, rank)
+        out = native.routed_forward(hiddens[rank], routes[rank][0], routes[rank][1], banks[rank], plan,
+                                    native.ProcessGroupCollective())
+        res["a2a_equal"] = bool(torch.equal(out, sim[rank]))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as exc:  # report instead of leaving the parent waiting
+        q.put((rank, repr(exc)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_expert_parallel_over_nccl():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(WORLD):
+        res = results[r]
+        assert isinstance(res, dict), res
+        assert res["reference_equal"], f"rank {r}: replicated-token EP differs from one GPU"
+        assert res["fast_rel_l2"] < 1e-2, res
+        assert res["a2a_equal"], f"rank {r}: all-to-all differs from the one-process run"
