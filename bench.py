@@ -13,9 +13,10 @@ public modules (router + ParallelExperts forward, eager) with the tokens
 copied from pinned host memory and the outputs copied back every batch.
 
 N > 1 (torchrun, one rank per GPU): replicated-token expert parallelism, the
-reference's record_* layout: every rank routes all tokens and runs its
-E/N experts; contributions are exchanged with one NCCL all-reduce and combined
-in global expert order. Work per step is fixed (strong scaling).
+reference's record_* layout: every rank routes all tokens and runs its E/N
+experts, combines its own experts' contributions and the [T, H] partial sums
+are all-reduced over NCCL ("fast" numerics, the reference's efficient EP
+exchange). Work per step is fixed (strong scaling).
 
 ``--impl reference`` times the reference algorithm on the host CPU (the
 torch restatement in oracle/, reference numerics), rank 0 only.
@@ -138,11 +139,19 @@ def build_layer(cfg, dev, ep: int, rank: int, seed: int = 1):
     return router, packed
 
 
+def numerics_for(ep: int) -> str:
+    """One GPU: the reference's ordered combine. Several: each rank combines
+    its own experts and the [T, H] partial sums are all-reduced (the
+    reference's fast / efficient EP exchange; the exact ordered combine would
+    move every [T*K, H] contribution row to every rank)."""
+    return "reference" if ep == 1 else "fast"
+
+
 def layer_call(cfg, router, packed, x, parallel, rank, ep):
     _, scores, idx = router(x)
     return X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts,
                            expert_begin=rank * (cfg.experts // ep), parallel=parallel,
-                           numerics="reference")
+                           numerics=numerics_for(ep))
 
 
 def kernel_launches(T: int, K: int, E: int) -> int:
@@ -433,6 +442,7 @@ def main():
             "config": {"workload": cfg.name, "batches": batches, "hidden": cfg.hidden,
                        "experts": cfg.experts, "top_k": cfg.top_k, "intermediate": cfg.inter,
                        "weights": cfg.storage, "parallelism": f"ep{world} replicated-token",
+                       "numerics": numerics_for(world),
                        "l2": "flushed (256 MiB write) before every batch", "timing": "CUDA graph "
                        "replay per batch, CUDA events"},
             "per_batch": per_batch, "roofline": roofline,
