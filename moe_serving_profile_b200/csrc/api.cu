@@ -304,8 +304,11 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
     if (total(na, nb) > budget)
       return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
   } else {
+    // token-row stages: 8, matching the A stages (one commit releases both),
+    // while at least 8 raw stages still fit; else 4
     na = 8;
-    nb = b_stage <= 4096u ? 8 : 4;
+    nb = 8;
+    if (nb * b_stage + xbytes + barbytes + 8 * rpb > budget) nb = 4;
     const uint32_t fixed = nb * b_stage + xbytes + barbytes;
     nr = fixed < budget ? static_cast<int>((budget - fixed) / rpb) : 0;
     nr = std::min(24, nr) & ~1;
@@ -365,6 +368,7 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   // quantised weights keep their A stages in TMEM columns 256..511, so a
   // 256-token tile gets a single accumulator slot
   p.acc_slots = (rpb && bn > 128) ? 1 : 2;
+  p.joint_ab = na == nb ? 1 : 0;
   // two MMA issuers when there are banks for both and the A / B rings split
   // evenly between them
   p.n_issuers = (p.nacc % 2 == 0 && na % 2 == 0 && nb % 2 == 0) ? 2 : 1;

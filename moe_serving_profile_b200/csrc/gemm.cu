@@ -345,28 +345,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d0 = tmem + static_cast<uint32_t>(slot * p.nacc * p.bn);
         int pa0 = 0, pa1 = 0, pb0 = 0, pb1 = 0, npend = 0;
         const int kb0 = (j - i0) & (step - 1);   // step is 1 or 2
+        // readiness of the next k-block's A and B is probed before this
+        // k-block's MMAs are issued, so the barrier read's latency overlaps
+        // the MMA issue; the blocking wait runs only if the probe said no
+        bool ready = false;
         for (int kb = kb0; kb < p.nkb; kb += step) {
           const int bank = (i0 + kb) & (p.nacc - 1);   // nacc is 1, 2 or 4
           const bool first = kb < p.nacc;   // this bank's first k-block of the tile
           const uint32_t d = d0 + static_cast<uint32_t>(bank * p.bn);
           const int sa = j + step * ra.idx, sb = j + step * rb.idx;
-          if (!wait_spin(&a_full[sa], ra.phase, p.status) ||
-              !wait_spin(&b_full[sb], rb.phase, p.status)) {
+          if (!ready && (!wait_spin(&a_full[sa], ra.phase, p.status) ||
+                         !wait_spin(&b_full[sb], rb.phase, p.status))) {
             ok = false;
             break;
           }
           tc_fence_after();
+          Ring na_ = ra, nb_ = rb;   // the next k-block's stages, probed during this one's MMAs
+          na_.next();
+          nb_.next();
+          const bool more = kb + step < p.nkb;
           const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + sb * p.bn * 128);
           if (p.wfmt == kWBf16) {
+            ready = more && mbar_test_wait(&a_full[j + step * na_.idx], na_.phase) &&
+                    mbar_test_wait(&b_full[j + step * nb_.idx], nb_.phase);
             const uint64_t adesc = sdesc_k_sw128(base_u32 + p.a_off + sa * kATile);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               umma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
           } else {
             const uint32_t at = tmem + p.a_col0 + static_cast<uint32_t>(sa) * kAStageCols;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_tmem_a(d, at + 8 * kk, bdesc + 2 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
+            // without a next k-block in this tile the probe reads the current,
+            // completed barriers and its answer is discarded
+            const bool probe = umma_k64_tmem_a_probe(
+                d, at, bdesc, idesc, first ? 0u : 1u,
+                more ? &a_full[j + step * na_.idx] : &a_full[sa], more ? na_.phase : ra.phase,
+                more ? &b_full[j + step * nb_.idx] : &b_full[sb], more ? nb_.phase : rb.phase);
+            ready = more && probe;
           }
           if (npend == 0) {
             pa0 = sa;
@@ -381,8 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (npend == 2 || kb + step >= p.nkb) {
             umma_commit(&a_empty[pa0]);
             if (npend == 2) umma_commit(&a_empty[pa1]);
-            umma_commit(&b_empty[pb0]);
-            if (npend == 2) umma_commit(&b_empty[pb1]);
+            if (!p.joint_ab) {
+              umma_commit(&b_empty[pb0]);
+              if (npend == 2) umma_commit(&b_empty[pb1]);
+            }
             npend = 0;
           }
         }
@@ -427,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int kb = 0; kb < p.nkb; ++kb, ring.next(), ++issued) {
         const int s = ring.idx;
-        if (!wait_bounded(&b_empty[s], ring.phase ^ 1u, p.status, 32)) {
+        if (!wait_bounded(p.joint_ab ? &a_empty[s] : &b_empty[s], ring.phase ^ 1u, p.status, 32)) {
           ok = false;
           break;
         }

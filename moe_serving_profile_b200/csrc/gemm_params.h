@@ -50,6 +50,10 @@ struct GemmParams {
   // drains; 1: 256-token tiles of quantised weights, whose A stages take the
   // other half of tensor memory)
   int acc_slots;
+  // joint_ab: A and B rings have the same number of stages and k-block i
+  // uses stage i % na of both, so one commit to a_empty releases both (the
+  // token-row producer waits on a_empty; b_empty is unused)
+  int joint_ab;
   uint32_t raw_off, a_off, b_off, x_off, bar_off, tmem_cols, a_col0;
 };
 

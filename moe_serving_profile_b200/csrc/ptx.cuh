@@ -279,6 +279,40 @@ B200_DEVI void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc
       : "memory");
 }
 
+// Four umma_bf16_tmem_a of one 64-column k-block (A columns a, a+8, a+16,
+// a+24; B descriptor advanced by 32 bytes per MMA; the first accumulates
+// only if acc0 != 0), with the test_waits of two mbarriers issued ahead of
+// them: returns whether both phases had completed. The barrier reads are in
+// flight while the MMAs issue instead of stalling the thread before them.
+B200_DEVI bool umma_k64_tmem_a_probe(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t acc0, uint64_t* bar_a, uint32_t pa, uint64_t* bar_b,
+                                     uint32_t pb) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred qa, qb, q0, qt;\n\t.reg .b64 bd;\n\t.reg .b32 ta;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 qa, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 qb, [%3], %4;\n\t"
+      "setp.ne.b32 q0, %9, 0;\n\t"
+      "setp.eq.b32 qt, %8, %8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%5], [%6], %7, %8, q0;\n\t"
+      "add.s64 bd, %7, 2;\n\t"
+      "add.u32 ta, %6, 8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%5], [ta], bd, %8, qt;\n\t"
+      "add.s64 bd, bd, 2;\n\t"
+      "add.u32 ta, ta, 8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%5], [ta], bd, %8, qt;\n\t"
+      "add.s64 bd, bd, 2;\n\t"
+      "add.u32 ta, ta, 8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%5], [ta], bd, %8, qt;\n\t"
+      "and.pred qa, qa, qb;\n\t"
+      "selp.u32 %0, 1, 0, qa;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar_a)), "r"(pa), "r"(smem_u32(bar_b)), "r"(pb), "r"(tmem_d), "r"(tmem_a),
+        "l"(bdesc), "r"(idesc), "r"(acc0)
+      : "memory");
+  return ok != 0;
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread
 // has completed.
 B200_DEVI void umma_commit(uint64_t* bar) {
