@@ -478,13 +478,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // TMEM lane quarter q holds 32 features x N tokens. Each 16-token chunk
     // is finished in registers, staged in shared memory as bf16 rows and
     // written out with 16-byte coalesced stores (rows beyond the tile and
-    // features beyond n_feat are never written).
+    // features beyond n_feat are never written). Gated tiles pair the gate
+    // (lanes 0-63) and up (64-127) rows of a feature through a shared
+    // exchange buffer; the down projection needs no exchange, so each warp
+    // stages and writes its own features.
     const int q = warp - kWarpEpi;
     const int te = threadIdx.x - kWarpEpi * 32;
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
     float* xbuf = reinterpret_cast<float*>(sbase + p.x_off);                      // [4][16][32] f32
     uint16_t* stage = reinterpret_cast<uint16_t*>(sbase + p.x_off + 8192);        // [2][16][128] bf16
     float* rowv = reinterpret_cast<float*>(sbase + p.x_off + 16384);             // [256] f32
+    const bool scaled = !p.gated && p.row_w != nullptr;
     int tc = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
       // tile bookkeeping and bias first: their loads overlap the accumulator wait
@@ -501,6 +505,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           b1 = __bfloat162float(p.bias[(long long)(tl.e * 2 + 1) * p.feat_pad + f]);
         } else {
           b0 = __bfloat162float(p.bias[(long long)tl.e * p.feat_pad + f]);
+        }
+      }
+      if (scaled) {
+        // the routing weights of the tile's rows, published by the barrier below
+        named_bar_sync(1, 128);   // every reader of the previous tile's weights is done
+        for (int i = te; i < tl.nrows; i += 128) {
+          const int src = p.row_src[tl.row0 + i];
+          rowv[i] = p.row_w_bf16
+                        ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.row_w)[src])
+                        : reinterpret_cast<const float*>(p.row_w)[src];
         }
       }
       const int bank0 = (tc * p.nkb) & (p.nacc - 1);
@@ -536,36 +550,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<const uint4*>(st + j * 64 + c8);
         }
       } else {
-        const bool scaled = p.row_w != nullptr;
-        if (scaled) {
-          for (int i = te; i < tl.nrows; i += 128) {
-            const int src = p.row_src[tl.row0 + i];
-            rowv[i] = p.row_w_bf16
-                          ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.row_w)[src])
-                          : reinterpret_cast<const float*>(p.row_w)[src];
-          }
-          named_bar_sync(1, 128);
-        }
+        // Each warp stages its 32 features x 16 tokens in its own buffer
+        // (two, alternating) and writes 16 rows x 64 bytes with 16-byte
+        // stores: no barrier across warps inside the tile. The routing
+        // weights of the tile's rows are published once per tile.
+        uint16_t* wst = stage + q * 1024;   // [2][16][32] bf16 of this warp
+        uint16_t* out0 = reinterpret_cast<uint16_t*>(p.out) + (long long)tl.row0 * p.ldo;
         for (int c0 = 0, ci = 0; c0 < ncols; c0 += 16, ++ci) {
           float acc[16];
           load_acc(tq + slot * p.nacc * p.bn + c0, p.bn, bank0, p.nacc, p.nbanks, acc);
-          uint16_t* st = stage + (ci & 1) * 16 * 128;    // [16][128]
+          uint16_t* st = wst + (ci & 1) * 512;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float y = bf16_rn(acc[j]);
             if (p.bias != nullptr) y = bf16_rn(y + b0);
             if (scaled) y = bf16_rn(y * rowv[c0 + j]);
-            st[j * 128 + fl] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
+            st[j * 32 + lane] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
           }
-          named_bar_sync(1, 128);
+          __syncwarp();
+          // lane l, pass i: chunk row (l + 32 i) / 4, features 8 ((l + 32 i) & 3) .. + 7
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = te + 128 * h;
-            const int j = c >> 4;
-            const int c8 = (c & 15) * 8;
-            if (c0 + j < tl.nrows && tl.ft * 128 + c8 < p.n_feat)
-              *reinterpret_cast<uint4*>(p.out + (long long)(tl.row0 + c0 + j) * p.ldo + tl.ft * 128 + c8) =
-                  *reinterpret_cast<const uint4*>(st + j * 128 + c8);
+          for (int i = 0; i < 2; ++i) {
+            const int c = lane + 32 * i;
+            const int j = c0 + (c >> 2);
+            const int fo = tl.ft * 128 + 32 * q + 8 * (c & 3);
+            if (j < tl.nrows && fo < p.n_feat)
+              *reinterpret_cast<uint4*>(out0 + (long long)j * p.ldo + fo) =
+                  *reinterpret_cast<const uint4*>(st + c * 8);
           }
         }
       }

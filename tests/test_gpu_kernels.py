@@ -267,6 +267,42 @@ def test_gated_gemm_integer_exact(cuda, fmt, tile, split):
     _status_clean(cuda)
 
 
+@pytest.mark.parametrize("planes", [1, 2])
+def test_fp8_per_chunk_scales_exact(cuda, planes):
+    """FP8 scale blocks that do not cover whole 64 x 64 halves (32 x 32 here)
+    travel as per-(row, 16-column chunk) scales inside each blob; with
+    power-of-two scales every dequantised weight and partial sum is exact."""
+    E, feat, K, T, topk, (br, bc) = 3, 200, 320, 90, 2, (32, 32)
+    g, wv, x, idx = _int_case(_lib.W_FP8, E, planes * feat, K, T, topk, seed=31 + planes)
+    wv = wv.reshape(E, planes, feat, K)
+    Fp, Kp = -(-feat // 128) * 128, -(-K // 64) * 64
+    nbr, nbc = -(-feat // br), -(-K // bc)
+    scale = torch.pow(2.0, torch.randint(-2, 3, (E, planes, nbr, nbc), generator=g).float())
+    w = torch.zeros(E, planes, Fp, Kp, dtype=torch.uint8)
+    w[:, :, :feat, :K] = wv.to(torch.float8_e4m3fn).view(torch.uint8)
+    blobs = layout.pack_fp8_blobs(w, scale, planes, feat, (br, bc))
+    weff = wv * scale.repeat_interleave(br, 2)[:, :, :feat].repeat_interleave(bc, 3)[..., :K]
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    R = T * topk
+    e_of_row = torch.repeat_interleave(torch.arange(E), counts.long())
+    xr = x[(perm // topk).long()]
+    out = torch.zeros(R, Fp if planes == 2 else feat, dtype=torch.bfloat16, device=cuda)
+    ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R,
+                    wfmt=_lib.W_FP8, planes=planes, feat_pad=Fp, n_feat=feat, k_pad=Kp,
+                    weight=blobs.to(cuda), fp8_block=(br, bc),
+                    b_src=x.bfloat16().to(cuda), k_valid=K, b_map=perm.to(cuda), b_div=topk,
+                    epilogue=_lib.EPI_SWIGLU if planes == 2 else _lib.EPI_DOWN, out=out)
+    pre = torch.einsum("rk,rpfk->rpf", xr.double(), weff.double()[e_of_row])   # [R, planes, feat]
+    got = out.cpu()[:, :feat]
+    if planes == 1:
+        assert torch.equal(got, pre[:, 0].bfloat16())
+    else:
+        ref = torch.nn.functional.silu(pre[:, 0].bfloat16()) * pre[:, 1].bfloat16()
+        assert float((got != ref).float().mean()) < 1e-3
+        assert float((got.float() - ref.float()).abs().max()) <= float(ref.float().abs().max()) * 2 ** -7
+    _status_clean(cuda)
+
+
 # ------------------------------------------------------------------ dequantisers, exact
 @pytest.mark.parametrize("storage", ["fp8", "mxfp4"])
 def test_dequant_exact_via_one_hot(cuda, storage):
