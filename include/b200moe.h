@@ -48,9 +48,10 @@ int b200moe_device_status(int device, int clear, int* out_status);
 
 /* ------------------------------------------------------------ router
  * Fused router: logits = hidden[T,H] . weight[E,H]^T (+ bias) accumulated in
- * fp32 in a fixed order (H split into 8-element vectors dealt round-robin to
- * 32 partial sums, each sequential, then combined pairwise with offsets
- * 16, 8, 4, 2, 1), followed by softmax / top-k / per-expert counts.
+ * fp32 in a fixed order (H split into 64-column segments, each one fmaf
+ * chain in increasing h from 0, the segment sums then added in increasing
+ * order; H % 8 == 0, H <= 8192), followed by softmax / top-k / per-expert
+ * counts.
  * Top-k order: value descending, equal values by ascending expert id.
  *
  * mode B200MOE_ROUTER_QWEN3 replaces Qwen3MoeTopKRouter.forward

@@ -127,7 +127,8 @@ int b200moe_router(int device, void* stream, int mode, const void* hidden, long 
   if (mode == B200MOE_ROUTER_GPT_OSS) B200_CHECK(bias != nullptr, "GPT-OSS router needs a bias");
   if (!logits_given && T > 0) {
     B200_CHECK(hidden && weight, "hidden and weight are required");
-    if (H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "router needs H %% 8 == 0 (H=%d)", H);
+    if (H % 8 != 0 || H > 8192)
+      return fail(B200MOE_ERR_UNSUPPORTED, "router needs H %% 8 == 0 and H <= 8192 (H=%d)", H);
     B200_CHECK(aligned16(hidden) && aligned16(weight) && ld_hidden % 8 == 0 && ld_hidden >= H,
                "hidden/weight must be 16-byte aligned with ld %% 8 == 0");
   }

@@ -94,22 +94,20 @@ void oracle_decode_mxfp4(const uint8_t* blocks, const uint8_t* scales, int rows,
 }
 
 /* Fixed-order fp32 dot product of two bf16 vectors of length H (H % 8 == 0):
-   vector v = h/8 goes to partial v % 32, accumulated in increasing h with
-   fmaf; partials combined pairwise with offsets 16, 8, 4, 2, 1. */
+   segment s covers h in [64 s, min(64 s + 64, H)) and is one fmaf chain in
+   increasing h starting from 0; the segments are then added in increasing s
+   (dot = ((seg0 + seg1) + seg2) + ...). The same order as the router kernels
+   (moe_serving_profile_b200/csrc/router.cu), independent of T and of the
+   launch shape. */
 float oracle_dot_bf16(const uint16_t* x, const uint16_t* w, int H) {
-  float p[32];
-  for (int i = 0; i < 32; ++i) p[i] = 0.0f;
-  for (int v = 0; v < H / 8; ++v)
-    for (int j = 0; j < 8; ++j) {
-      const int h = v * 8 + j;
-      p[v % 32] = fmaf(oracle_bf16_to_f32(x[h]), oracle_bf16_to_f32(w[h]), p[v % 32]);
-    }
-  for (int o = 16; o >= 1; o >>= 1) {
-    float q[32];
-    for (int i = 0; i < 32; ++i) q[i] = p[i] + p[i ^ o];
-    memcpy(p, q, sizeof(p));
+  float dot = 0.0f;
+  for (int s0 = 0; s0 < H; s0 += 64) {
+    const int s1 = s0 + 64 < H ? s0 + 64 : H;
+    float seg = 0.0f;
+    for (int h = s0; h < s1; ++h) seg = fmaf(oracle_bf16_to_f32(x[h]), oracle_bf16_to_f32(w[h]), seg);
+    dot = s0 == 0 ? seg : dot + seg;
   }
-  return p[0];
+  return dot;
 }
 
 /* mode 0: bf16 logits, mode 1: bf16 logits with bias (bf16 [E]), mode 2: fp32.
