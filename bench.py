@@ -455,6 +455,7 @@ def main():
         del g
     graphs.clear()
     if world > 1:
+        parallel.close()   # NVLink exchange buffers (collective)
         dist.barrier()
         dist.destroy_process_group()
 

@@ -35,6 +35,7 @@ extern "C" {
 #define B200MOE_STATUS_WAIT_TIMEOUT 1 /* a bounded device wait gave up */
 #define B200MOE_STATUS_BAD_TILE 2     /* inconsistent tile bookkeeping */
 #define B200MOE_STATUS_BAD_INDEX 4    /* an expert id outside [0, E) was dropped */
+#define B200MOE_STATUS_PEER_TIMEOUT 8 /* a wait for another rank's signal gave up */
 
 /* Message describing the last non-zero return on this host thread. */
 const char* b200moe_last_error(void);
@@ -252,6 +253,43 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
  */
 int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_src,
                         const int* map, int div, int n, int H, void* dst, long long ld_dst);
+
+/* ------------------------------------------------------------ NVLink exchange
+ * Fused combine + all-reduce of the replicated-token expert-parallel layer
+ * ("fast" numerics, moe_serving/qwen3_parallel.py:105-118: every rank
+ * combines its own experts' rows, the [T, H] partial sums are all-reduced)
+ * in one kernel over peer memory, replacing b200moe_combine (expert order,
+ * [expert_lo, expert_hi)) followed by an NCCL all-reduce:
+ *   out[t] = bf16( sum over ranks p = 0 .. world-1 in order of
+ *                  fp32(partial_p[t]) ),
+ *   partial_p[t] = rank p's ordered combine of its experts' rows (bf16
+ *                  running sum, b200moe_combine's arithmetic).
+ * Every rank owns one exchange buffer of b200moe_p2p_buffer_bytes(t_cap, H,
+ * world) bytes from b200moe_p2p_alloc (zeroed): per-block flags and an inbox
+ * that every rank pushes its partial rows into. It is exported with b200moe_p2p_export
+ * and mapped by the other ranks with b200moe_p2p_import (CUDA IPC; plain
+ * peer loads and stores over NVLink, no multicast objects). peers[world] are
+ * the buffers' addresses in this process, peers[rank] the local one. All
+ * ranks must call with the same T (<= t_cap), K, H, world, in the same order;
+ * calls are ordered by per-block epochs kept inside the buffers (block b
+ * owns rows t = b mod 1024), so they can be captured in a CUDA graph and
+ * replayed. A peer that does not arrive within
+ * timeout_ns (0: 2 s) sets B200MOE_STATUS_PEER_TIMEOUT; those rows of out are
+ * then not written. world <= 8, K <= 32, H % 8 == 0.
+ */
+size_t b200moe_p2p_buffer_bytes(int t_cap, int H, int world);
+int b200moe_p2p_alloc(int device, size_t bytes, void** out_ptr);
+int b200moe_p2p_free(int device, void* ptr);
+/* handle: 64 bytes (cudaIpcMemHandle_t) */
+int b200moe_p2p_export(int device, void* ptr, unsigned char* handle);
+int b200moe_p2p_import(int device, const unsigned char* handle, void** out_ptr);
+int b200moe_p2p_close(int device, void* ptr);
+int b200moe_combine_allreduce(int device, void* stream, const void* rows, long long ld_rows,
+                              const int* inverse, const long long* indices, int T, int K, int H,
+                              int expert_lo, int expert_hi, int scale_rows, const void* weights,
+                              int weights_bf16, int world, int rank, void* const* peers,
+                              int t_cap, void* out, long long ld_out,
+                              unsigned long long timeout_ns);
 
 /* ------------------------------------------------------------ token all-to-all
  * Receive-side plan of the dispatch exchange of moe_serving/moe.py:123-131

@@ -16,7 +16,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libb200moe.so"
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
-STATUS_WAIT_TIMEOUT, STATUS_BAD_TILE, STATUS_BAD_INDEX = 1, 2, 4
+STATUS_WAIT_TIMEOUT, STATUS_BAD_TILE, STATUS_BAD_INDEX, STATUS_PEER_TIMEOUT = 1, 2, 4, 8
 
 ROUTER_QWEN3, ROUTER_GPT_OSS, ROUTER_NATIVE = 0, 1, 2
 W_BF16, W_FP8, W_MXFP4 = 0, 1, 2
@@ -37,6 +37,13 @@ EXPORTED = (
     "b200moe_gather_rows",
     "b200moe_a2a_recv_plan",
     "b200moe_gemm_args_size",
+    "b200moe_p2p_buffer_bytes",
+    "b200moe_p2p_alloc",
+    "b200moe_p2p_free",
+    "b200moe_p2p_export",
+    "b200moe_p2p_import",
+    "b200moe_p2p_close",
+    "b200moe_combine_allreduce",
 )
 
 
@@ -119,6 +126,24 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_gather_rows.argtypes = [
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int, c_int, c_void_p,
         c_longlong,
+    ]
+    lib.b200moe_p2p_buffer_bytes.restype = c_size_t
+    lib.b200moe_p2p_buffer_bytes.argtypes = [c_int, c_int, c_int]
+    lib.b200moe_p2p_alloc.restype = c_int
+    lib.b200moe_p2p_alloc.argtypes = [c_int, c_size_t, POINTER(c_void_p)]
+    lib.b200moe_p2p_free.restype = c_int
+    lib.b200moe_p2p_free.argtypes = [c_int, c_void_p]
+    lib.b200moe_p2p_export.restype = c_int
+    lib.b200moe_p2p_export.argtypes = [c_int, c_void_p, c_char_p]
+    lib.b200moe_p2p_import.restype = c_int
+    lib.b200moe_p2p_import.argtypes = [c_int, c_char_p, POINTER(c_void_p)]
+    lib.b200moe_p2p_close.restype = c_int
+    lib.b200moe_p2p_close.argtypes = [c_int, c_void_p]
+    lib.b200moe_combine_allreduce.restype = c_int
+    lib.b200moe_combine_allreduce.argtypes = [
+        c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+        c_int, c_int, c_void_p, c_int, c_int, c_int, POINTER(c_void_p), c_int, c_void_p,
+        c_longlong, ctypes.c_ulonglong,
     ]
     lib.b200moe_a2a_recv_plan.restype = c_int
     lib.b200moe_a2a_recv_plan.argtypes = [

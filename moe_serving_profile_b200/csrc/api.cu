@@ -447,6 +447,97 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
   return B200MOE_OK;
 }
 
+size_t b200moe_p2p_buffer_bytes(int t_cap, int H, int world) {
+  if (t_cap < 0 || H < 0 || world < 1 || world > b200::kP2PMaxRanks) return 0;
+  return b200::kP2PHeaderBytes +
+         2ull * static_cast<size_t>(world) * static_cast<size_t>(t_cap) * static_cast<size_t>(H) * 2ull;
+}
+
+int b200moe_p2p_alloc(int device, size_t bytes, void** out_ptr) {
+  B200_CHECK(out_ptr != nullptr && bytes >= b200::kP2PHeaderBytes, "bad exchange buffer request");
+  *out_ptr = nullptr;
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  void* p = nullptr;
+  B200_CUDA(cudaMalloc(&p, bytes));   // its own allocation: the IPC handle covers exactly it
+  const cudaError_t err = cudaMemset(p, 0, bytes);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return fail(B200MOE_ERR_CUDA, "exchange buffer clear failed: %s", cudaGetErrorString(err));
+  }
+  B200_CUDA(cudaDeviceSynchronize());
+  *out_ptr = p;
+  return B200MOE_OK;
+}
+
+int b200moe_p2p_free(int device, void* ptr) {
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  if (ptr) B200_CUDA(cudaFree(ptr));
+  return B200MOE_OK;
+}
+
+int b200moe_p2p_export(int device, void* ptr, unsigned char* handle) {
+  B200_CHECK(ptr && handle, "ptr and handle are required");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  B200_CUDA(cudaIpcGetMemHandle(&h, ptr));
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  return B200MOE_OK;
+}
+
+int b200moe_p2p_import(int device, const unsigned char* handle, void** out_ptr) {
+  B200_CHECK(handle && out_ptr, "handle and out_ptr are required");
+  *out_ptr = nullptr;
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  B200_CUDA(cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return B200MOE_OK;
+}
+
+int b200moe_p2p_close(int device, void* ptr) {
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  if (ptr) B200_CUDA(cudaIpcCloseMemHandle(ptr));
+  return B200MOE_OK;
+}
+
+int b200moe_combine_allreduce(int device, void* stream, const void* rows, long long ld_rows,
+                              const int* inverse, const long long* indices, int T, int K, int H,
+                              int expert_lo, int expert_hi, int scale_rows, const void* weights,
+                              int weights_bf16, int world, int rank, void* const* peers,
+                              int t_cap, void* out, long long ld_out,
+                              unsigned long long timeout_ns) {
+  B200_CHECK(T >= 0 && K >= 1 && H >= 8 && t_cap >= 0, "bad sizes");
+  if (K > 32 || H % 8 != 0)
+    return fail(B200MOE_ERR_UNSUPPORTED, "combine_allreduce needs K <= 32 and H %% 8 == 0");
+  if (world < 1 || world > b200::kP2PMaxRanks)
+    return fail(B200MOE_ERR_UNSUPPORTED, "combine_allreduce supports 1..%d ranks", b200::kP2PMaxRanks);
+  B200_CHECK(rank >= 0 && rank < world, "rank %d outside [0, %d)", rank, world);
+  B200_CHECK(T <= t_cap, "T=%d exceeds the exchange buffer's %d rows", T, t_cap);
+  B200_CHECK(peers != nullptr, "peers are required");
+  for (int i = 0; i < world; ++i)
+    B200_CHECK(peers[i] != nullptr && aligned16(peers[i]), "peer buffer %d missing or unaligned", i);
+  B200_CHECK(!scale_rows || weights, "scale_rows needs weights");
+  if (T > 0) {
+    B200_CHECK(out && inverse && indices && rows, "rows, out, inverse and indices are required");
+    B200_CHECK(aligned16(rows) && aligned16(out) && ld_rows % 8 == 0 && ld_out % 8 == 0,
+               "rows/out must be 16-byte aligned with ld %% 8 == 0");
+  }
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_combine_allreduce(static_cast<cudaStream_t>(stream), rows, ld_rows, inverse,
+                                           indices, T, K, H, expert_lo, expert_hi, scale_rows,
+                                           weights, weights_bf16, world, rank, peers, t_cap, out,
+                                           ld_out, timeout_ns ? timeout_ns : b200::kWaitLimitNs, sp));
+  return B200MOE_OK;
+}
+
 int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_src,
                         const int* map, int div, int n, int H, void* dst, long long ld_dst) {
   B200_CHECK(n >= 0 && H >= 8 && div >= 1, "bad sizes");

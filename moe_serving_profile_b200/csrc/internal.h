@@ -34,6 +34,19 @@ cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            int scale_rows, const void* weights, int weights_bf16, void* out,
                            long long ld_out);
 
+// Exchange-buffer layout of the fused combine + all-reduce (p2p.cu).
+constexpr int kP2PBlocks = 1024;    // fixed grid: block b owns rows t = b (mod 1024)
+constexpr int kP2PMaxRanks = 8;
+constexpr size_t kP2PHeaderBytes = 40960;  // flags [1024][8] u32 + epochs [1024] u32, padded
+static_assert(kP2PBlocks * kP2PMaxRanks * 4 + kP2PBlocks * 4 <= kP2PHeaderBytes, "p2p header");
+
+cudaError_t launch_combine_allreduce(cudaStream_t st, const void* rows, long long ld_rows,
+                                     const int* inverse, const long long* indices, int T, int K,
+                                     int H, int expert_lo, int expert_hi, int scale_rows,
+                                     const void* weights, int weights_bf16, int world, int rank,
+                                     void* const* peers, int t_cap, void* out, long long ld_out,
+                                     unsigned long long timeout_ns, int* status);
+
 cudaError_t launch_gather_rows(cudaStream_t st, const void* src, long long ld_src,
                                const int* map, int div, int n, int H, void* dst,
                                long long ld_dst);

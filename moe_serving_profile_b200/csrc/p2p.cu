@@ -1,0 +1,228 @@
+// Combine + cross-rank reduction in one kernel over NVLink peer memory: the
+// replicated-token expert-parallel layer's "fast" exchange
+// (moe_serving/qwen3_parallel.py:105-118 combines each rank's own experts and
+// all-reduces the [T, H] partial sums) without a separate collective launch.
+//
+// Every rank owns one exchange buffer (cudaMalloc'd, mapped into the other
+// ranks' address spaces with CUDA IPC; plain loads and stores, no multicast):
+//   [kP2PBlocks][8] u32        flags: slot (b, src) = the epoch of block b's
+//                              last signal from rank src, written by rank src
+//   [kP2PBlocks]    u32        this rank's epoch per block (local)
+//   [2][world][t_cap][H] bf16  inbox: the partial rows every rank sent here,
+//                              double-buffered by epoch parity
+// Block b owns the rows t = b (mod kP2PBlocks) on every rank (the grid is
+// min(T, kP2PBlocks) blocks), so a row's writer and readers are the same
+// block everywhere and every block keeps its own epoch sequence:
+//   1. combine: partial[t] = bf16 running sum of the row's local-expert
+//      contributions in ascending expert order (the combine kernel's order),
+//      stored into slot [rank][t] of every rank's inbox (posted NVLink
+//      stores: the sender never waits on a remote round trip);
+//   2. signal: fence, then store the block's new epoch into slot (b, rank) of
+//      every peer; wait (bounded) until every peer's slot (b, p) here holds
+//      it;
+//   3. reduce: out[t] = bf16(sum over p = 0 .. world-1, in rank order, of the
+//      fp32 values of inbox [p][t]), read from local memory.
+// Epoch parity selects the inbox half, so a rank writes half P of a peer's
+// inbox only two calls later, after that peer has signalled the call in
+// between, which it does only after finishing its reads of half P.
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kMaxK = 32;
+
+struct P2PParams {
+  const __nv_bfloat16* rows;
+  long long ld_rows;
+  const int* inverse;
+  const long long* indices;
+  int T, K, H, lo, hi, scale_rows, weights_bf16, world, rank, t_cap;
+  const void* weights;
+  uint8_t* peer[kP2PMaxRanks];   // every rank's exchange buffer (peer[rank] is local)
+  __nv_bfloat16* out;
+  long long ld_out;
+  unsigned long long timeout_ns;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t* flags_of(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
+__device__ __forceinline__ uint32_t* seq_of(uint8_t* base) {
+  return reinterpret_cast<uint32_t*>(base) + kP2PBlocks * kP2PMaxRanks;
+}
+// inbox row [parity][src][t] of the buffer at base
+__device__ __forceinline__ __nv_bfloat16* inbox_row(uint8_t* base, int parity, int src, int t,
+                                                    int world, int t_cap, int H) {
+  return reinterpret_cast<__nv_bfloat16*>(base + kP2PHeaderBytes) +
+         (((long long)parity * world + src) * t_cap + t) * H;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_constant__ P2PParams p) {
+  const int b = blockIdx.x;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  uint8_t* mine = p.peer[p.rank];
+  if (threadIdx.x == 0) s_epoch = seq_of(mine)[b] + 1;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int parity = static_cast<int>(epoch & 1u);
+  const int nvec = p.H >> 3;
+
+  // ---- 1. partial sums of this block's rows, pushed to every rank's inbox
+  for (int t = b; t < p.T; t += kP2PBlocks) {   // gridDim.x == min(T, kP2PBlocks)
+    int rsel[kMaxK];
+    int ksel[kMaxK];
+    long long key[kMaxK];
+    int n = 0;
+    for (int k = 0; k < p.K; ++k) {
+      const long long e = p.indices[(long long)t * p.K + k];
+      const int r = p.inverse[(long long)t * p.K + k];
+      if (r < 0 || e < p.lo || e >= p.hi) continue;
+      const long long kk = e * kMaxK + k;
+      int q = n++;   // insertion sort by (expert, slot)
+      while (q > 0 && key[q - 1] > kk) {
+        key[q] = key[q - 1];
+        rsel[q] = rsel[q - 1];
+        ksel[q] = ksel[q - 1];
+        --q;
+      }
+      key[q] = kk;
+      rsel[q] = r;
+      ksel[q] = k;
+    }
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int i = 0; i < n; ++i) {
+        float wv = 1.f;
+        if (p.scale_rows) {
+          const long long wi = (long long)t * p.K + ksel[i];
+          wv = p.weights_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.weights)[wi])
+                              : reinterpret_cast<const float*>(p.weights)[wi];
+        }
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(p.rows + rsel[i] * p.ld_rows) + v);
+        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float c0 = __uint_as_float(wd[j] << 16);
+          float c1 = __uint_as_float(wd[j] & 0xffff0000u);
+          if (p.scale_rows) {
+            c0 = bf16r(c0 * wv);
+            c1 = bf16r(c1 * wv);
+          }
+          acc[2 * j] = bf16r(acc[2 * j] + c0);
+          acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      for (int q = 0; q < p.world; ++q)
+        reinterpret_cast<uint4*>(inbox_row(p.peer[q], parity, p.rank, t, p.world, p.t_cap, p.H))[v] = o;
+    }
+  }
+
+  // ---- 2. signal every peer, wait for every peer (bounded)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();   // this block's pushed rows before its signal
+    seq_of(mine)[b] = epoch;
+    for (int q = 0; q < p.world; ++q)
+      if (q != p.rank) st_release_sys(flags_of(p.peer[q]) + b * kP2PMaxRanks + p.rank, epoch);
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < p.world && ok; ++q) {
+      if (q == p.rank) continue;
+      const uint32_t* f = flags_of(mine) + b * kP2PMaxRanks + q;
+      while (static_cast<int>(ld_acquire_sys(f) - epoch) < 0) {
+        if (globaltimer_ns() - t0 > p.timeout_ns) {
+          atomicOr(p.status, kStatusPeerTimeout);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;   // the status word reports it; the output rows are not written
+
+  // ---- 3. sum the inbox rows in rank order (fp32), one bf16 rounding
+  for (int t = b; t < p.T; t += kP2PBlocks) {
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int q = 0; q < p.world; ++q) {
+        const __nv_bfloat16* src = inbox_row(mine, parity, q, t, p.world, p.t_cap, p.H);
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src) + v);   // L2: peers rewrite it
+        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] += __uint_as_float(wd[j] << 16);
+          acc[2 * j + 1] += __uint_as_float(wd[j] & 0xffff0000u);
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(p.out + t * p.ld_out)[v] = o;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_combine_allreduce(cudaStream_t st, const void* rows, long long ld_rows,
+                                     const int* inverse, const long long* indices, int T, int K,
+                                     int H, int expert_lo, int expert_hi, int scale_rows,
+                                     const void* weights, int weights_bf16, int world, int rank,
+                                     void* const* peers, int t_cap, void* out, long long ld_out,
+                                     unsigned long long timeout_ns, int* status) {
+  P2PParams p{};
+  p.rows = static_cast<const __nv_bfloat16*>(rows);
+  p.ld_rows = ld_rows;
+  p.inverse = inverse;
+  p.indices = indices;
+  p.T = T;
+  p.K = K;
+  p.H = H;
+  p.lo = expert_lo;
+  p.hi = expert_hi;
+  p.scale_rows = scale_rows;
+  p.weights = weights;
+  p.weights_bf16 = weights_bf16;
+  p.world = world;
+  p.rank = rank;
+  p.t_cap = t_cap;
+  for (int i = 0; i < world; ++i) p.peer[i] = static_cast<uint8_t*>(peers[i]);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.timeout_ns = timeout_ns;
+  p.status = status;
+  // every rank launches the same grid; at most kP2PBlocks blocks of 128
+  // threads, which fit on the device at once, so no block waits on one that
+  // cannot start. T = 0 launches nothing (no block's epoch advances anywhere).
+  if (T == 0) return cudaSuccess;
+  combine_allreduce_kernel<<<T < kP2PBlocks ? T : kP2PBlocks, 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -22,6 +22,7 @@ enum StatusBits : int {
   kStatusWaitTimeout = 1 << 0,   // an mbarrier wait ran past its limit
   kStatusBadTile = 1 << 1,       // tile bookkeeping found an impossible value
   kStatusBadIndex = 1 << 2,      // an expert index outside [0, E)
+  kStatusPeerTimeout = 1 << 3,   // a wait for another rank's signal ran past its limit
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

@@ -155,7 +155,8 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     if numerics == "fast":
         contrib = run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
                               expert_begin=expert_begin)
-        partial = ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT,
-                              expert_lo=expert_begin, expert_hi=expert_begin + w.n_experts)
-        return parallel.reduce(partial)
+        # combine of the local experts + SUM over the group: one NVLink kernel
+        # (parallel.combine_reduce) or combine + NCCL all-reduce
+        return parallel.combine_reduce(contrib, perm.inverse, indices, expert_begin,
+                                       expert_begin + w.n_experts)
     raise ValueError(f"numerics must be reference or fast, got {numerics!r}")

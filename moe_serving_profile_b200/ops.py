@@ -219,6 +219,33 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *,
     return out
 
 
+def combine_allreduce(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *,
+                      expert_lo: int, expert_hi: int, peers, t_cap: int, rank: int,
+                      weights: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                      timeout_ns: int = 0) -> torch.Tensor:
+    """Fused expert-order combine of [expert_lo, expert_hi) and a SUM over the
+    ranks whose exchange buffers are ``peers`` (device addresses, this rank's
+    at ``rank``); see b200moe_combine_allreduce."""
+    device = _dev(indices, "indices")
+    T, K = indices.shape
+    H = rows.shape[1]
+    _bf16_rows(rows, "contribution rows")
+    if out is None:
+        out = torch.empty(T, H, device=indices.device, dtype=torch.bfloat16)
+    _bf16_rows(out, "output")
+    arr = (ctypes.c_void_p * len(peers))(*peers)
+    wbf16 = int(weights is not None and weights.dtype == torch.bfloat16)
+    check(
+        lib.b200moe_combine_allreduce(
+            device, _stream(device), _ptr(rows), rows.stride(0), _ptr(inverse), _ptr(indices),
+            T, K, H, expert_lo, expert_hi, int(weights is not None), _ptr(weights), wbf16,
+            len(peers), rank, arr, t_cap, _ptr(out), out.stride(0), timeout_ns,
+        ),
+        "combine_allreduce",
+    )
+    return out
+
+
 def gather_rows(src: torch.Tensor, index_map: torch.Tensor, div: int = 1,
                 out: torch.Tensor | None = None) -> torch.Tensor:
     """out[i] = src[index_map[i] // div] for bf16 rows."""

@@ -8,8 +8,61 @@ block's group in the same order. Tokens are replicated within a block.
 
 from __future__ import annotations
 
+import ctypes
+import os
+
 import torch
 import torch.distributed as dist
+
+# Peer bytes a rank reads in the fused combine + all-reduce (T * H * 2 *
+# (size - 1)); larger exchanges use the NCCL all-reduce.
+P2P_MAX_BYTES = 16 << 20
+
+
+class PeerExchange:
+    """Exchange buffers of the fused combine + all-reduce
+    (b200moe_combine_allreduce): one cudaMalloc'd buffer per rank of an
+    expert-parallel group, mapped into the other ranks with CUDA IPC (plain
+    peer loads and stores over NVLink). Created collectively, outside CUDA
+    graph capture; ``close`` is collective too."""
+
+    def __init__(self, group, rank: int, size: int, device: torch.device, t_cap: int, hidden: int):
+        from moe_serving_profile_b200._lib import check, lib
+
+        self.group, self.rank, self.size = group, rank, size
+        self.device, self.t_cap, self.hidden = device, t_cap, hidden
+        dev = device.index
+        nbytes = lib.b200moe_p2p_buffer_bytes(t_cap, hidden, size)
+        ptr = ctypes.c_void_p()
+        check(lib.b200moe_p2p_alloc(dev, nbytes, ctypes.byref(ptr)), "p2p_alloc")
+        self.local = ptr.value
+        handle = ctypes.create_string_buffer(64)
+        check(lib.b200moe_p2p_export(dev, self.local, handle), "p2p_export")
+        handles = [None] * size
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.peers = []
+        for i, h in enumerate(handles):
+            if i == rank:
+                self.peers.append(self.local)
+                continue
+            q = ctypes.c_void_p()
+            check(lib.b200moe_p2p_import(dev, h, ctypes.byref(q)), "p2p_import")
+            self.peers.append(q.value)
+        dist.barrier(group=group)   # every buffer mapped everywhere before first use
+
+    def close(self) -> None:
+        from moe_serving_profile_b200._lib import lib
+
+        if self.peers is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)   # no rank still reads a peer's buffer
+        for i, q in enumerate(self.peers):
+            if i != self.rank:
+                lib.b200moe_p2p_close(self.device.index, q)
+        dist.barrier(group=self.group)
+        lib.b200moe_p2p_free(self.device.index, self.local)
+        self.peers = None
 
 
 class ParallelGroup:
@@ -22,6 +75,7 @@ class ParallelGroup:
         self.rank = grank % size
         self.start_rank = grank - self.rank
         self.group = None
+        self._exchange = None
         if size > 1:
             for first in range(0, world, size):
                 g = dist.new_group(list(range(first, first + size)))
@@ -33,6 +87,47 @@ class ParallelGroup:
         if self.size > 1:
             dist.all_reduce(tensor, group=self.group)
         return tensor
+
+    def combine_reduce(self, rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor,
+                       expert_lo: int, expert_hi: int,
+                       weights: torch.Tensor | None = None) -> torch.Tensor:
+        """SUM over the group of each rank's expert-order combine of its
+        experts [expert_lo, expert_hi): the fused NVLink kernel when the
+        exchange fits (B200MOE_P2P=0 turns it off), else combine + all-reduce."""
+        from moe_serving_profile_b200 import _lib, ops
+
+        T, H = indices.shape[0], rows.shape[1]
+        ex = self._peer_exchange(rows.device, H, T)
+        if ex is not None:
+            return ops.combine_allreduce(rows, inverse, indices, expert_lo=expert_lo,
+                                         expert_hi=expert_hi, peers=ex.peers, t_cap=ex.t_cap,
+                                         rank=self.rank, weights=weights)
+        partial = ops.combine(rows, inverse, indices, order=_lib.ORDER_EXPERT,
+                              expert_lo=expert_lo, expert_hi=expert_hi, weights=weights)
+        return self.reduce(partial)
+
+    def _peer_exchange(self, device: torch.device, hidden: int, T: int):
+        if (self.size == 1 or self.size > 8 or device.type != "cuda"
+                or os.environ.get("B200MOE_P2P", "1") == "0"):
+            return None
+        t_cap = P2P_MAX_BYTES // (hidden * 2 * (self.size - 1))
+        if T > t_cap:
+            return None
+        ex = self._exchange
+        if ex is None or ex.hidden != hidden or ex.device != device:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the NVLink exchange buffers are created by an eager call "
+                                   "before CUDA graph capture")
+            if ex is not None:
+                ex.close()
+            ex = self._exchange = PeerExchange(self.group, self.rank, self.size, device, t_cap, hidden)
+        return ex
+
+    def close(self) -> None:
+        """Release the NVLink exchange buffers (collective)."""
+        if self._exchange is not None:
+            self._exchange.close()
+            self._exchange = None
 
     def broadcast(self, tensor: torch.Tensor, owner: int = 0) -> torch.Tensor:
         if self.size > 1:

@@ -153,6 +153,66 @@ def test_combine_bit_exact(cuda, order, scale):
     assert torch.equal(out.cpu(), ref)
 
 
+def _p2p_buffer(cuda, t_cap, H, world):
+    import ctypes
+    ptr = ctypes.c_void_p()
+    nbytes = _lib.lib.b200moe_p2p_buffer_bytes(t_cap, H, world)
+    _lib.check(_lib.lib.b200moe_p2p_alloc(cuda.index, nbytes, ctypes.byref(ptr)), "p2p_alloc")
+    return ptr.value
+
+
+@pytest.mark.parametrize("scale", [False, True])
+def test_combine_allreduce_single_rank_equals_combine(cuda, scale):
+    """One rank: the fused kernel's partial is the expert-order combine and
+    the rank sum is that partial (one bf16 rounding of an exact value), so it
+    equals b200moe_combine bit for bit, in consecutive calls (epochs 1, 2, 3)."""
+    T, K, E, H = 300, 8, 128, 2048
+    g = torch.Generator().manual_seed(11)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).long()
+    rows = torch.randn(T * K, H, generator=g).bfloat16().to(cuda)
+    wts = torch.rand(T, K, generator=g).to(cuda)
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    inv, idx = inv.to(cuda), idx.to(cuda)
+    buf = _p2p_buffer(cuda, 512, H, 1)
+    try:
+        ref = ops.combine(rows, inv, idx, order=_lib.ORDER_EXPERT, expert_lo=16, expert_hi=80,
+                          weights=wts if scale else None)
+        for _ in range(3):
+            out = ops.combine_allreduce(rows, inv, idx, expert_lo=16, expert_hi=80, peers=[buf],
+                                        t_cap=512, rank=0, weights=wts if scale else None)
+            assert torch.equal(out, ref)
+        _status_clean(cuda)
+    finally:
+        torch.cuda.synchronize(cuda)
+        _lib.lib.b200moe_p2p_free(cuda.index, buf)
+
+
+def test_combine_allreduce_peer_timeout_sets_status(cuda):
+    """A peer that never signals: every block's wait gives up after the
+    timeout, the kernel returns, the status word says PEER_TIMEOUT and the
+    context stays usable (no fault, no hang)."""
+    import ctypes
+    T, K, E, H = 64, 2, 8, 256
+    idx = torch.randint(0, E, (T, K))
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    rows = torch.ones(T * K, H, dtype=torch.bfloat16, device=cuda)
+    bufs = [_p2p_buffer(cuda, T, H, 2), _p2p_buffer(cuda, T, H, 2)]   # "rank 1": nobody signals
+    out = torch.full((T, H), 7.0, dtype=torch.bfloat16, device=cuda)
+    try:
+        ops.combine_allreduce(rows, inv.to(cuda), idx.to(cuda), expert_lo=0, expert_hi=E, peers=bufs,
+                              t_cap=T, rank=0, out=out, timeout_ns=20_000_000)
+        torch.cuda.synchronize(cuda)
+        st = ctypes.c_int()
+        _lib.check(_lib.lib.b200moe_device_status(cuda.index, 1, ctypes.byref(st)), "status")
+        assert st.value & _lib.STATUS_PEER_TIMEOUT
+        assert bool((out == 7.0).all())   # rows are not written after a timeout
+        assert float((torch.ones(4, device=cuda) * 2).sum()) == 8.0   # the context still runs kernels
+    finally:
+        torch.cuda.synchronize(cuda)
+        for b in bufs:
+            _lib.lib.b200moe_p2p_free(cuda.index, b)
+
+
 def test_gather_rows_exact(cuda):
     src = torch.randn(50, 2048).bfloat16()
     m = torch.randint(0, 400, (333,), dtype=torch.int32)

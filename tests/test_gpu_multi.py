@@ -6,7 +6,11 @@
   within the BF16 layer tolerance;
 * token all-to-all (native.routed_forward with ProcessGroupCollective): each
   rank's output equals native.simulate_routed (all ranks in one process, the
-  same kernels) bit for bit.
+  same kernels) bit for bit;
+* the fused NVLink combine + all-reduce (ParallelGroup.combine_reduce) equals
+  its definition, bf16(fp32(partial_0) + fp32(partial_1)), bit for bit, in
+  eager calls and in CUDA graph replays; the NCCL path
+  (B200MOE_P2P=0) agrees within bf16 rounding.
 
 Ranks are spawned processes, one per GPU, with a 60 s process-group timeout;
 the parent gives them a bounded time to report.
@@ -93,7 +97,42 @@ def _worker(rank: int, port: int, q):
         out = native.routed_forward(hiddens[rank], routes[rank][0], routes[rank][1], banks[rank], plan,
                                     native.ProcessGroupCollective())
         res["a2a_equal"] = bool(torch.equal(out, sim[rank]))
+        # ---- fused NVLink combine + all-reduce
+        from moe_serving_profile_b200 import _lib, ops
+        T2, K2, E2, H2 = 200, 8, 128, 2048
+        g2 = torch.Generator().manual_seed(21)
+        idx2 = torch.stack([torch.randperm(E2, generator=g2)[:K2] for _ in range(T2)]).long()
+        rows2 = torch.randn(T2 * K2, H2, generator=g2).bfloat16().to(dev)
+        _, _, _, inv2 = oracle.permute(idx2, E2)
+        inv2, idx2 = inv2.to(dev), idx2.to(dev)
+        half = E2 // WORLD
+        parts = [ops.combine(rows2, inv2, idx2, order=_lib.ORDER_EXPERT, expert_lo=q * half,
+                             expert_hi=(q + 1) * half).float() for q in range(WORLD)]
+        exact = (parts[0] + parts[1]).bfloat16()
+        lo, hi = rank * half, (rank + 1) * half
+        eager = [pg.combine_reduce(rows2, inv2, idx2, lo, hi) for _ in range(3)]
+        res["p2p_used"] = pg._exchange is not None
+        res["p2p_equal"] = all(bool(torch.equal(o, exact)) for o in eager)
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            gout = pg.combine_reduce(rows2, inv2, idx2, lo, hi)
+        ok = True
+        for _ in range(2):
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            ok = ok and bool(torch.equal(gout, exact))
+        del graph
+        res["p2p_graph_equal"] = ok
+        os.environ["B200MOE_P2P"] = "0"
+        nccl = pg.combine_reduce(rows2, inv2, idx2, lo, hi)
+        os.environ["B200MOE_P2P"] = "1"
+        res["nccl_close"] = float((nccl.float() - exact.float()).abs().max()) <= \
+            float(exact.float().abs().max()) * 2 ** -7
+        res["status"] = _lib.device_status(rank)
         torch.cuda.synchronize(dev)
+        pg.close()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, res))
@@ -118,3 +157,5 @@ def test_expert_parallel_over_nccl():
         assert res["reference_equal"], f"rank {r}: replicated-token EP differs from one GPU"
         assert res["fast_rel_l2"] < 1e-2, res
         assert res["a2a_equal"], f"rank {r}: all-to-all differs from the one-process run"
+        assert res["p2p_used"] and res["p2p_equal"] and res["p2p_graph_equal"], res
+        assert res["nccl_close"] and res["status"] == 0, res
