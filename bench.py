@@ -279,6 +279,8 @@ def main():
     hbm, tf_burst, tf_sust, peak_kind = peaks()
 
     router, packed = build_layer(cfg, dev, world, rank)
+    if parallel is not None:
+        router.shard_over(parallel)   # large batches: each rank routes a slice, one all-gather
     batches = list(cfg.batches)
     xs = {T: S.make_hidden(T, cfg.hidden, seed=1000 + T, device=dev) for T in batches}
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)

@@ -265,8 +265,12 @@ int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_
  *   partial_p[t] = rank p's ordered combine of its experts' rows (bf16
  *                  running sum, b200moe_combine's arithmetic).
  * Every rank owns one exchange buffer of b200moe_p2p_buffer_bytes(t_cap, H,
- * world) bytes from b200moe_p2p_alloc (zeroed): per-block flags and an inbox
- * that every rank pushes its partial rows into. It is exported with b200moe_p2p_export
+ * world) bytes from b200moe_p2p_alloc (zeroed): per-block flags, an inbox
+ * that ranks push partial rows into and an area for finished rows. Up to
+ * 16 MiB pushed per rank (T * H * 2 * (world - 1)) every rank pushes its
+ * partial rows to every rank (one-shot); above, each row goes to one owner
+ * rank, which sums it and pushes the finished row to every rank (two-shot).
+ * The result is the same either way. It is exported with b200moe_p2p_export
  * and mapped by the other ranks with b200moe_p2p_import (CUDA IPC; plain
  * peer loads and stores over NVLink, no multicast objects). peers[world] are
  * the buffers' addresses in this process, peers[rank] the local one. All
@@ -290,6 +294,14 @@ int b200moe_combine_allreduce(int device, void* stream, const void* rows, long l
                               int weights_bf16, int world, int rank, void* const* peers,
                               int t_cap, void* out, long long ld_out,
                               unsigned long long timeout_ns);
+
+/* As b200moe_gather_rows, restricted to the rows [offsets[expert_lo],
+ * offsets[expert_hi]) (device offsets of b200moe_permute, 0 <= expert_lo <=
+ * expert_hi <= E): the rows of one rank's experts under expert parallelism.
+ * Other rows of dst are left as they are. */
+int b200moe_gather_rows_range(int device, void* stream, const void* src, long long ld_src,
+                              const int* map, int div, int n, int H, void* dst, long long ld_dst,
+                              const int* offsets, int expert_lo, int expert_hi);
 
 /* ------------------------------------------------------------ token all-to-all
  * Receive-side plan of the dispatch exchange of moe_serving/moe.py:123-131

@@ -35,6 +35,7 @@ EXPORTED = (
     "b200moe_expert_gemm",
     "b200moe_combine",
     "b200moe_gather_rows",
+    "b200moe_gather_rows_range",
     "b200moe_a2a_recv_plan",
     "b200moe_gemm_args_size",
     "b200moe_p2p_buffer_bytes",
@@ -144,6 +145,11 @@ def _load() -> ctypes.CDLL:
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
         c_int, c_int, c_void_p, c_int, c_int, c_int, POINTER(c_void_p), c_int, c_void_p,
         c_longlong, ctypes.c_ulonglong,
+    ]
+    lib.b200moe_gather_rows_range.restype = c_int
+    lib.b200moe_gather_rows_range.argtypes = [
+        c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int, c_int, c_void_p,
+        c_longlong, c_void_p, c_int, c_int,
     ]
     lib.b200moe_a2a_recv_plan.restype = c_int
     lib.b200moe_a2a_recv_plan.argtypes = [

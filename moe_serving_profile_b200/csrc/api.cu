@@ -448,9 +448,10 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
 }
 
 size_t b200moe_p2p_buffer_bytes(int t_cap, int H, int world) {
-  if (t_cap < 0 || H < 0 || world < 1 || world > b200::kP2PMaxRanks) return 0;
-  return b200::kP2PHeaderBytes +
-         2ull * static_cast<size_t>(world) * static_cast<size_t>(t_cap) * static_cast<size_t>(H) * 2ull;
+  if (t_cap < 0 || H < 8 || world < 1 || world > b200::kP2PMaxRanks) return 0;
+  const size_t rows = 2ull * world * static_cast<size_t>(b200::p2p_inbox_rows(t_cap, H, world)) +
+                      2ull * static_cast<size_t>(t_cap);
+  return b200::kP2PHeaderBytes + rows * static_cast<size_t>(H) * 2ull;
 }
 
 int b200moe_p2p_alloc(int device, size_t bytes, void** out_ptr) {
@@ -535,6 +536,24 @@ int b200moe_combine_allreduce(int device, void* stream, const void* rows, long l
                                            indices, T, K, H, expert_lo, expert_hi, scale_rows,
                                            weights, weights_bf16, world, rank, peers, t_cap, out,
                                            ld_out, timeout_ns ? timeout_ns : b200::kWaitLimitNs, sp));
+  return B200MOE_OK;
+}
+
+int b200moe_gather_rows_range(int device, void* stream, const void* src, long long ld_src,
+                              const int* map, int div, int n, int H, void* dst, long long ld_dst,
+                              const int* offsets, int expert_lo, int expert_hi) {
+  B200_CHECK(n >= 0 && H >= 8 && div >= 1, "bad sizes");
+  B200_CHECK(expert_lo >= 0 && expert_hi >= expert_lo, "bad expert range");
+  if (H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "gather_rows needs H %% 8 == 0");
+  if (n == 0 || expert_hi == expert_lo) return B200MOE_OK;
+  B200_CHECK(src && map && dst && offsets, "src, map, dst and offsets are required");
+  B200_CHECK(aligned16(src) && aligned16(dst) && ld_src % 8 == 0 && ld_dst % 8 == 0,
+             "rows must be 16-byte aligned with ld %% 8 == 0");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_gather_rows_range(static_cast<cudaStream_t>(stream), src, ld_src, map, div,
+                                           n, H, dst, ld_dst, offsets, expert_lo, expert_hi,
+                                           8 * g_sm_count[device]));
   return B200MOE_OK;
 }
 

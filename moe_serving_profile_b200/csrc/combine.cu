@@ -93,7 +93,39 @@ __global__ void __launch_bounds__(128) gather_rows_kernel(const __nv_bfloat16* _
   for (int v = threadIdx.x; v < nvec; v += blockDim.x) b[v] = __ldg(a + v);
 }
 
+// Rows [offsets[lo], offsets[hi]) of the permuted order only (the local
+// experts' rows under expert parallelism), grid-strided.
+__global__ void __launch_bounds__(128) gather_rows_range_kernel(
+    const __nv_bfloat16* __restrict__ src, long long ld_src, const int* __restrict__ map, int div,
+    int n, int H, __nv_bfloat16* __restrict__ dst, long long ld_dst, const int* __restrict__ offsets,
+    int lo, int hi) {
+  const int r0 = max(0, min(n, offsets[lo])), r1 = max(r0, min(n, offsets[hi]));
+  const int nvec = H >> 3;
+  for (int i = r0 + blockIdx.x; i < r1; i += gridDim.x) {
+    const int m = map[i];
+    uint4* b = reinterpret_cast<uint4*>(dst + i * ld_dst);
+    if (m < 0) {
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) b[v] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint4* a = reinterpret_cast<const uint4*>(src + (long long)(m / div) * ld_src);
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) b[v] = __ldg(a + v);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_rows_range(cudaStream_t st, const void* src, long long ld_src,
+                                     const int* map, int div, int n, int H, void* dst,
+                                     long long ld_dst, const int* offsets, int expert_lo,
+                                     int expert_hi, int max_blocks) {
+  if (n == 0) return cudaSuccess;
+  const int blocks = n < max_blocks ? n : max_blocks;
+  gather_rows_range_kernel<<<blocks, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(src), ld_src,
+                                                   map, div, n, H, static_cast<__nv_bfloat16*>(dst),
+                                                   ld_dst, offsets, expert_lo, expert_hi);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            const int* inverse, const long long* indices, int T, int K, int H,

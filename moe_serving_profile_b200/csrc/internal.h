@@ -35,10 +35,24 @@ cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            long long ld_out);
 
 // Exchange-buffer layout of the fused combine + all-reduce (p2p.cu).
-constexpr int kP2PBlocks = 1024;    // fixed grid: block b owns rows t = b (mod 1024)
+constexpr int kP2PBlocks = 1024;    // block b owns rows t = b (mod 1024); a multiple of every world size
 constexpr int kP2PMaxRanks = 8;
-constexpr size_t kP2PHeaderBytes = 40960;  // flags [1024][8] u32 + epochs [1024] u32, padded
-static_assert(kP2PBlocks * kP2PMaxRanks * 4 + kP2PBlocks * 4 <= kP2PHeaderBytes, "p2p header");
+constexpr size_t kP2PHeaderBytes = 69632;  // flags [2][1024][8] u32 + epochs [1024] u32
+static_assert(2 * kP2PBlocks * kP2PMaxRanks * 4 + kP2PBlocks * 4 <= kP2PHeaderBytes, "p2p header");
+constexpr long long kP2POneShotBytes = 16ll << 20;   // one-shot up to this many pushed bytes per rank
+
+// The exchange of T rows pushes every partial row to every rank (one-shot)
+// or to its row's owner only (two-shot).
+inline bool p2p_two_shot(int T, int H, int world) {
+  return world > 1 && (long long)T * H * 2 * (world - 1) > kP2POneShotBytes;
+}
+// Inbox rows per (parity, source) of a buffer for up to t_cap rows.
+inline int p2p_inbox_rows(int t_cap, int H, int world) {
+  long long one = world > 1 ? kP2POneShotBytes / ((long long)H * 2 * (world - 1)) : t_cap;
+  if (one > t_cap) one = t_cap;
+  const int two = (t_cap + world - 1) / world;
+  return static_cast<int>(one > two ? one : two);
+}
 
 cudaError_t launch_combine_allreduce(cudaStream_t st, const void* rows, long long ld_rows,
                                      const int* inverse, const long long* indices, int T, int K,
@@ -46,6 +60,11 @@ cudaError_t launch_combine_allreduce(cudaStream_t st, const void* rows, long lon
                                      const void* weights, int weights_bf16, int world, int rank,
                                      void* const* peers, int t_cap, void* out, long long ld_out,
                                      unsigned long long timeout_ns, int* status);
+
+cudaError_t launch_gather_rows_range(cudaStream_t st, const void* src, long long ld_src,
+                                     const int* map, int div, int n, int H, void* dst,
+                                     long long ld_dst, const int* offsets, int expert_lo,
+                                     int expert_hi, int max_blocks);
 
 cudaError_t launch_gather_rows(cudaStream_t st, const void* src, long long ld_src,
                                const int* map, int div, int n, int H, void* dst,

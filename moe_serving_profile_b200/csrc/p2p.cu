@@ -5,26 +5,32 @@
 //
 // Every rank owns one exchange buffer (cudaMalloc'd, mapped into the other
 // ranks' address spaces with CUDA IPC; plain loads and stores, no multicast):
-//   [kP2PBlocks][8] u32        flags: slot (b, src) = the epoch of block b's
-//                              last signal from rank src, written by rank src
-//   [kP2PBlocks]    u32        this rank's epoch per block (local)
-//   [2][world][t_cap][H] bf16  inbox: the partial rows every rank sent here,
-//                              double-buffered by epoch parity
-// Block b owns the rows t = b (mod kP2PBlocks) on every rank (the grid is
-// min(T, kP2PBlocks) blocks), so a row's writer and readers are the same
-// block everywhere and every block keeps its own epoch sequence:
-//   1. combine: partial[t] = bf16 running sum of the row's local-expert
-//      contributions in ascending expert order (the combine kernel's order),
-//      stored into slot [rank][t] of every rank's inbox (posted NVLink
-//      stores: the sender never waits on a remote round trip);
-//   2. signal: fence, then store the block's new epoch into slot (b, rank) of
-//      every peer; wait (bounded) until every peer's slot (b, p) here holds
-//      it;
-//   3. reduce: out[t] = bf16(sum over p = 0 .. world-1, in rank order, of the
-//      fp32 values of inbox [p][t]), read from local memory.
-// Epoch parity selects the inbox half, so a rank writes half P of a peer's
-// inbox only two calls later, after that peer has signalled the call in
-// between, which it does only after finishing its reads of half P.
+//   [2][kP2PBlocks][8] u32    flags: slot (phase, b, src) = the epoch of
+//                             block b's last phase signal from rank src,
+//                             written by rank src
+//   [kP2PBlocks] u32          this rank's epoch per block (local)
+//   [2][world][A][H] bf16     inbox: partial rows sent here, by source rank
+//   [2][t_cap][H] bf16        finished rows (two-shot)
+// (the leading [2] of the row areas is the epoch parity). Block b owns the
+// rows t = b (mod kP2PBlocks) on every rank (the grid is min(T, kP2PBlocks)
+// blocks), so a row's writer and readers are the same block everywhere and
+// every block keeps its own epoch sequence. A block first combines its rows:
+// partial[t] = bf16 running sum of the row's local-expert contributions in
+// ascending expert order (the combine kernel's order). Then:
+//   one-shot (T * H * 2 * (world - 1) <= kP2POneShotBytes):
+//     push partial[t] into inbox [rank][t] of every rank (posted NVLink
+//     stores); signal every peer, wait for every peer (bounded); out[t] =
+//     bf16(fp32 sum of inbox [0 .. world)[t] in rank order), local reads.
+//   two-shot (larger exchanges): the rows of block b belong to rank
+//     o = b % world (kP2PBlocks is a multiple of every world size); push
+//     partial[t] only to inbox [rank][t / world] of rank o and signal it;
+//     rank o waits for every source, sums in rank order as above, pushes the
+//     finished row into every rank's finished area [t] and signals them; every
+//     rank copies its finished rows to out. Each rank sends about
+//     2 T H 2 (world - 1) / world bytes instead of T H 2 (world - 1).
+// Epoch parity selects the row areas, so a rank writes an area of a peer
+// again only two calls later, after that peer has signalled the call in
+// between, which it does only after it has read the area.
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -38,7 +44,7 @@ struct P2PParams {
   long long ld_rows;
   const int* inverse;
   const long long* indices;
-  int T, K, H, lo, hi, scale_rows, weights_bf16, world, rank, t_cap;
+  int T, K, H, lo, hi, scale_rows, weights_bf16, world, rank, t_cap, a_rows, two_shot;
   const void* weights;
   uint8_t* peer[kP2PMaxRanks];   // every rank's exchange buffer (peer[rank] is local)
   __nv_bfloat16* out;
@@ -47,15 +53,22 @@ struct P2PParams {
   int* status;
 };
 
-__device__ __forceinline__ uint32_t* flags_of(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
-__device__ __forceinline__ uint32_t* seq_of(uint8_t* base) {
-  return reinterpret_cast<uint32_t*>(base) + kP2PBlocks * kP2PMaxRanks;
+__device__ __forceinline__ uint32_t* flags_of(uint8_t* base, int phase) {
+  return reinterpret_cast<uint32_t*>(base) + phase * kP2PBlocks * kP2PMaxRanks;
 }
-// inbox row [parity][src][t] of the buffer at base
-__device__ __forceinline__ __nv_bfloat16* inbox_row(uint8_t* base, int parity, int src, int t,
-                                                    int world, int t_cap, int H) {
+__device__ __forceinline__ uint32_t* seq_of(uint8_t* base) {
+  return reinterpret_cast<uint32_t*>(base) + 2 * kP2PBlocks * kP2PMaxRanks;
+}
+// inbox row [parity][src][i]
+__device__ __forceinline__ __nv_bfloat16* inbox_row(uint8_t* base, const P2PParams& p, int parity,
+                                                    int src, int i) {
   return reinterpret_cast<__nv_bfloat16*>(base + kP2PHeaderBytes) +
-         (((long long)parity * world + src) * t_cap + t) * H;
+         (((long long)parity * p.world + src) * p.a_rows + i) * p.H;
+}
+// finished row [parity][t]
+__device__ __forceinline__ __nv_bfloat16* final_row(uint8_t* base, const P2PParams& p, int parity, int t) {
+  return reinterpret_cast<__nv_bfloat16*>(base + kP2PHeaderBytes) +
+         (2ll * p.world * p.a_rows + (long long)parity * p.t_cap + t) * p.H;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -65,6 +78,54 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Thread 0: fence this block's stores, then store the epoch into slot
+// (phase, b, rank) of every listed peer.
+__device__ __forceinline__ void signal_peers(const P2PParams& p, int phase, int b, uint32_t epoch,
+                                             int only) {
+  __threadfence_system();
+  for (int q = 0; q < p.world; ++q)
+    if (q != p.rank && (only < 0 || q == only))
+      st_release_sys(flags_of(p.peer[q], phase) + b * kP2PMaxRanks + p.rank, epoch);
+}
+
+// Thread 0: wait until slot (phase, b, q) here holds the epoch for every
+// listed source q (bounded). Returns false after the timeout (status set).
+__device__ __forceinline__ bool wait_peers(const P2PParams& p, int phase, int b, uint32_t epoch,
+                                           int only) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int q = 0; q < p.world; ++q) {
+    if (q == p.rank || (only >= 0 && q != only)) continue;
+    const uint32_t* f = flags_of(p.peer[p.rank], phase) + b * kP2PMaxRanks + q;
+    while (static_cast<int>(ld_acquire_sys(f) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > p.timeout_ns) {
+        atomicOr(p.status, kStatusPeerTimeout);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  __threadfence();
+  return true;
+}
+
+__device__ __forceinline__ void acc_row(float (&acc)[8], const uint4& u) {
+  const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc[2 * j] += __uint_as_float(wd[j] << 16);
+    acc[2 * j + 1] += __uint_as_float(wd[j] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_row(const float (&acc)[8]) {
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  return o;
 }
 
 __global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_constant__ P2PParams p) {
@@ -77,8 +138,9 @@ __global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_con
   const uint32_t epoch = s_epoch;
   const int parity = static_cast<int>(epoch & 1u);
   const int nvec = p.H >> 3;
+  const int owner = b % p.world;   // two-shot: the rank that finishes this block's rows
 
-  // ---- 1. partial sums of this block's rows, pushed to every rank's inbox
+  // ---- 1. partial sums of this block's rows, pushed to the inbox(es)
   for (int t = b; t < p.T; t += kP2PBlocks) {   // gridDim.x == min(T, kP2PBlocks)
     int rsel[kMaxK];
     int ksel[kMaxK];
@@ -125,67 +187,75 @@ __global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_con
           acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
         }
       }
-      uint4 o;
-      o.x = pack_bf16x2(acc[0], acc[1]);
-      o.y = pack_bf16x2(acc[2], acc[3]);
-      o.z = pack_bf16x2(acc[4], acc[5]);
-      o.w = pack_bf16x2(acc[6], acc[7]);
-      for (int q = 0; q < p.world; ++q)
-        reinterpret_cast<uint4*>(inbox_row(p.peer[q], parity, p.rank, t, p.world, p.t_cap, p.H))[v] = o;
+      const uint4 o = pack_row(acc);
+      if (p.two_shot) {
+        reinterpret_cast<uint4*>(inbox_row(p.peer[owner], p, parity, p.rank, t / p.world))[v] = o;
+      } else {
+        for (int q = 0; q < p.world; ++q)
+          reinterpret_cast<uint4*>(inbox_row(p.peer[q], p, parity, p.rank, t))[v] = o;
+      }
     }
   }
 
-  // ---- 2. signal every peer, wait for every peer (bounded)
+  // ---- 2. exchange
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();   // this block's pushed rows before its signal
     seq_of(mine)[b] = epoch;
-    for (int q = 0; q < p.world; ++q)
-      if (q != p.rank) st_release_sys(flags_of(p.peer[q]) + b * kP2PMaxRanks + p.rank, epoch);
-    int ok = 1;
-    const uint64_t t0 = globaltimer_ns();
-    for (int q = 0; q < p.world && ok; ++q) {
-      if (q == p.rank) continue;
-      const uint32_t* f = flags_of(mine) + b * kP2PMaxRanks + q;
-      while (static_cast<int>(ld_acquire_sys(f) - epoch) < 0) {
-        if (globaltimer_ns() - t0 > p.timeout_ns) {
-          atomicOr(p.status, kStatusPeerTimeout);
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
-      }
+    if (!p.two_shot) {
+      signal_peers(p, 0, b, epoch, -1);
+      s_ok = wait_peers(p, 0, b, epoch, -1);
+    } else if (owner != p.rank) {
+      signal_peers(p, 0, b, epoch, owner);
+      s_ok = 1;
+    } else {
+      s_ok = wait_peers(p, 0, b, epoch, -1);
     }
-    __threadfence();
-    s_ok = ok;
   }
   __syncthreads();
   if (!s_ok) return;   // the status word reports it; the output rows are not written
 
-  // ---- 3. sum the inbox rows in rank order (fp32), one bf16 rounding
-  for (int t = b; t < p.T; t += kP2PBlocks) {
-    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-      float acc[8];
+  if (!p.two_shot) {
+    // ---- 3. sum the inbox rows in rank order (fp32), one bf16 rounding
+    for (int t = b; t < p.T; t += kP2PBlocks) {
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        float acc[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int q = 0; q < p.world; ++q) {
-        const __nv_bfloat16* src = inbox_row(mine, parity, q, t, p.world, p.t_cap, p.H);
-        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src) + v);   // L2: peers rewrite it
-        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[2 * j] += __uint_as_float(wd[j] << 16);
-          acc[2 * j + 1] += __uint_as_float(wd[j] & 0xffff0000u);
-        }
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int q = 0; q < p.world; ++q)   // L2 reads: peers rewrite the inbox
+          acc_row(acc, __ldcg(reinterpret_cast<const uint4*>(inbox_row(mine, p, parity, q, t)) + v));
+        reinterpret_cast<uint4*>(p.out + t * p.ld_out)[v] = pack_row(acc);
       }
-      uint4 o;
-      o.x = pack_bf16x2(acc[0], acc[1]);
-      o.y = pack_bf16x2(acc[2], acc[3]);
-      o.z = pack_bf16x2(acc[4], acc[5]);
-      o.w = pack_bf16x2(acc[6], acc[7]);
-      reinterpret_cast<uint4*>(p.out + t * p.ld_out)[v] = o;
     }
+    return;
   }
+
+  if (owner == p.rank) {
+    // ---- 3a. the owner finishes the rows and pushes them to every rank
+    for (int t = b; t < p.T; t += kP2PBlocks) {
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int q = 0; q < p.world; ++q)
+          acc_row(acc, __ldcg(reinterpret_cast<const uint4*>(inbox_row(mine, p, parity, q, t / p.world)) + v));
+        const uint4 o = pack_row(acc);
+        for (int q = 0; q < p.world; ++q)
+          if (q != p.rank) reinterpret_cast<uint4*>(final_row(p.peer[q], p, parity, t))[v] = o;
+        reinterpret_cast<uint4*>(p.out + t * p.ld_out)[v] = o;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) signal_peers(p, 1, b, epoch, -1);
+    return;
+  }
+  // ---- 3b. the other ranks wait for the owner's finished rows
+  if (threadIdx.x == 0) s_ok = wait_peers(p, 1, b, epoch, owner);
+  __syncthreads();
+  if (!s_ok) return;
+  for (int t = b; t < p.T; t += kP2PBlocks)
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x)
+      reinterpret_cast<uint4*>(p.out + t * p.ld_out)[v] =
+          __ldcg(reinterpret_cast<const uint4*>(final_row(mine, p, parity, t)) + v);
 }
 
 }  // namespace
@@ -212,6 +282,8 @@ cudaError_t launch_combine_allreduce(cudaStream_t st, const void* rows, long lon
   p.world = world;
   p.rank = rank;
   p.t_cap = t_cap;
+  p.a_rows = p2p_inbox_rows(t_cap, H, world);
+  p.two_shot = p2p_two_shot(T, H, world) ? 1 : 0;
   for (int i = 0; i < world; ++i) p.peer[i] = static_cast<uint8_t*>(peers[i]);
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;

@@ -76,7 +76,8 @@ def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K:
     if bn >= 64:
         # large token tiles: gather the routed rows once into permuted order
         # so the GEMM reads them as plain 2D tiles instead of per-row gathers
-        b_src = ops.gather_rows(hidden, perm.perm_src, div)
+        b_src = ops.gather_rows(hidden, perm.perm_src, div, offsets=perm.offsets,
+                                expert_lo=expert_begin, expert_hi=expert_begin + w.n_experts)
         b_map, b_div = None, 1
     else:
         b_src, b_map, b_div = hidden, perm.perm_src, div

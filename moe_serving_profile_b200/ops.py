@@ -247,14 +247,25 @@ def combine_allreduce(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.
 
 
 def gather_rows(src: torch.Tensor, index_map: torch.Tensor, div: int = 1,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-    """out[i] = src[index_map[i] // div] for bf16 rows."""
+                out: torch.Tensor | None = None, offsets: torch.Tensor | None = None,
+                expert_lo: int = 0, expert_hi: int = 0) -> torch.Tensor:
+    """out[i] = src[index_map[i] // div] for bf16 rows; with ``offsets``
+    (a permutation's), only rows [offsets[expert_lo], offsets[expert_hi])."""
     device = _dev(src, "src")
     _bf16_rows(src, "src")
     n = index_map.numel()
     H = src.shape[1]
     if out is None:
         out = torch.empty(n, H, device=src.device, dtype=torch.bfloat16)
+    if offsets is not None:
+        check(
+            lib.b200moe_gather_rows_range(
+                device, _stream(device), _ptr(src), src.stride(0), _ptr(index_map), div, n, H,
+                _ptr(out), out.stride(0), _ptr(offsets), expert_lo, expert_hi,
+            ),
+            "gather_rows_range",
+        )
+        return out
     check(
         lib.b200moe_gather_rows(
             device, _stream(device), _ptr(src), src.stride(0), _ptr(index_map), div, n, H,

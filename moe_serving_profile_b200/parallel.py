@@ -14,9 +14,9 @@ import os
 import torch
 import torch.distributed as dist
 
-# Peer bytes a rank reads in the fused combine + all-reduce (T * H * 2 *
-# (size - 1)); larger exchanges use the NCCL all-reduce.
-P2P_MAX_BYTES = 16 << 20
+# Largest batch the fused combine + all-reduce exchanges (its buffers hold
+# this many rows); larger batches use combine + the NCCL all-reduce.
+P2P_MAX_ROWS = 8192
 
 
 class PeerExchange:
@@ -110,7 +110,7 @@ class ParallelGroup:
         if (self.size == 1 or self.size > 8 or device.type != "cuda"
                 or os.environ.get("B200MOE_P2P", "1") == "0"):
             return None
-        t_cap = P2P_MAX_BYTES // (hidden * 2 * (self.size - 1))
+        t_cap = P2P_MAX_ROWS
         if T > t_cap:
             return None
         ex = self._exchange

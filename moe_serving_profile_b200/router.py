@@ -6,14 +6,49 @@ indices)`` — so forward hooks such as the reference's ``RoutingRecorder``
 (moe_serving/gpt_oss_parallel.py:273-288) keep working, but run the fused
 router kernel. Each forward also leaves the per-expert token counts of the
 batch in ``last_counts`` (int32, on the device) for load statistics.
+
+Under replicated-token expert parallelism every rank needs every token's
+routing. With ``shard_over(parallel)`` a batch of at least
+``SHARD_MIN_TOKENS`` tokens (a multiple of the group size) is routed in
+slices, one per rank, and the slices are all-gathered; the router is
+row-independent with a fixed summation order, so every rank still sees
+bit-identical results.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
 from torch import nn
 
 from moe_serving_profile_b200 import _lib, ops
+
+SHARD_MIN_TOKENS = 1024
+
+
+def _route(mode: int, h: torch.Tensor, weight, bias, top_k: int, normalize: bool, parallel):
+    """(first output, scores, indices, counts) of ops.router, routed in
+    per-rank slices and all-gathered when sharding applies. The first output
+    is the fp32 probabilities (Qwen3) or the bf16 logits (others)."""
+    T = h.shape[0]
+    n = 1 if parallel is None else parallel.size
+    if n == 1 or T < SHARD_MIN_TOKENS or T % n or not h.is_cuda:
+        out = ops.router(mode, h, weight, bias, top_k, normalize)
+        return (out.probs if mode == _lib.ROUTER_QWEN3 else out.logits), out.scores, out.indices, out.counts
+    ts = T // n
+    out = ops.router(mode, h[parallel.rank * ts:(parallel.rank + 1) * ts], weight, bias, top_k, normalize)
+    parts = [out.probs if mode == _lib.ROUTER_QWEN3 else out.logits, out.scores, out.indices, out.counts]
+    flat = torch.cat([p.reshape(-1).view(torch.uint8) for p in parts])   # one collective
+    gathered = torch.empty(n, flat.numel(), dtype=torch.uint8, device=h.device)
+    dist.all_gather_into_tensor(gathered, flat, group=parallel.group)
+    res, o = [], 0
+    for p in parts:
+        nb = p.numel() * p.element_size()
+        chunk = gathered[:, o:o + nb].contiguous().view(p.dtype)
+        res.append(chunk.reshape(n * p.shape[0], *p.shape[1:]) if p is not parts[3] else
+                   chunk.reshape(n, -1).sum(0, dtype=torch.int32))
+        o += nb
+    return tuple(res)
 
 
 class Qwen3Router(nn.Module):
@@ -32,13 +67,20 @@ class Qwen3Router(nn.Module):
         # load-skew workloads). None keeps the exact Qwen3 router.
         self.bias: torch.Tensor | None = None
         self.last_counts: torch.Tensor | None = None
+        self.parallel = None
+
+    def shard_over(self, parallel) -> "Qwen3Router":
+        """Route large batches in per-rank slices of ``parallel`` (a
+        ParallelGroup whose ranks all call forward on the same tokens)."""
+        self.parallel = parallel
+        return self
 
     def forward(self, hidden_states: torch.Tensor):
         h = hidden_states.reshape(-1, self.hidden_dim)
-        out = ops.router(_lib.ROUTER_QWEN3, h, self.weight, self.bias, self.top_k,
-                         self.norm_topk_prob)
-        self.last_counts = out.counts
-        return out.probs, out.scores, out.indices
+        probs, scores, indices, counts = _route(_lib.ROUTER_QWEN3, h, self.weight, self.bias,
+                                                self.top_k, self.norm_topk_prob, self.parallel)
+        self.last_counts = counts
+        return probs, scores, indices
 
 
 class GptOssRouter(nn.Module):
@@ -54,12 +96,19 @@ class GptOssRouter(nn.Module):
         self.weight = nn.Parameter(torch.zeros(self.num_experts, self.hidden_dim), requires_grad=False)
         self.bias = nn.Parameter(torch.zeros(self.num_experts), requires_grad=False)
         self.last_counts: torch.Tensor | None = None
+        self.parallel = None
+
+    def shard_over(self, parallel) -> "GptOssRouter":
+        """Route large batches in per-rank slices of ``parallel`` (see Qwen3Router)."""
+        self.parallel = parallel
+        return self
 
     def forward(self, hidden_states: torch.Tensor):
         h = hidden_states.reshape(-1, self.hidden_dim)
-        out = ops.router(_lib.ROUTER_GPT_OSS, h, self.weight, self.bias, self.top_k, False)
-        self.last_counts = out.counts
-        return out.logits, out.scores, out.indices
+        logits, scores, indices, counts = _route(_lib.ROUTER_GPT_OSS, h, self.weight, self.bias,
+                                                 self.top_k, False, self.parallel)
+        self.last_counts = counts
+        return logits, scores, indices
 
 
 def native_route(hidden: torch.Tensor, gate_weight: torch.Tensor, top_k: int,

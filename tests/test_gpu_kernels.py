@@ -213,6 +213,20 @@ def test_combine_allreduce_peer_timeout_sets_status(cuda):
             _lib.lib.b200moe_p2p_free(cuda.index, b)
 
 
+def test_gather_rows_range_only_touches_the_experts_rows(cuda):
+    T, K, E, H = 300, 4, 16, 512
+    g = torch.Generator().manual_seed(3)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).long()
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    src = torch.randn(T, H, generator=g).bfloat16().to(cuda)
+    full = ops.gather_rows(src, perm.to(cuda), K)
+    out = torch.full((T * K, H), 5.0, dtype=torch.bfloat16, device=cuda)
+    ops.gather_rows(src, perm.to(cuda), K, out=out, offsets=offsets.to(cuda), expert_lo=4, expert_hi=11)
+    r0, r1 = int(offsets[4]), int(offsets[11])
+    assert torch.equal(out[r0:r1], full[r0:r1])
+    assert bool((out[:r0] == 5.0).all()) and bool((out[r1:] == 5.0).all())
+
+
 def test_gather_rows_exact(cuda):
     src = torch.randn(50, 2048).bfloat16()
     m = torch.randint(0, 400, (333,), dtype=torch.int32)

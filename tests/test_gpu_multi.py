@@ -9,8 +9,11 @@
   same kernels) bit for bit;
 * the fused NVLink combine + all-reduce (ParallelGroup.combine_reduce) equals
   its definition, bf16(fp32(partial_0) + fp32(partial_1)), bit for bit, in
-  eager calls and in CUDA graph replays; the NCCL path
-  (B200MOE_P2P=0) agrees within bf16 rounding.
+  eager calls and in CUDA graph replays, for the one-shot exchange (T = 200)
+  and the two-shot one (T = 4200); the NCCL path
+  (B200MOE_P2P=0) agrees within bf16 rounding;
+* a router sharded over the group (each rank routes a slice, one
+  all-gather) returns what the whole-batch router returns, bit for bit.
 
 Ranks are spawned processes, one per GPU, with a 60 s process-group timeout;
 the parent gives them a bounded time to report.
@@ -130,6 +133,30 @@ def _worker(rank: int, port: int, q):
         os.environ["B200MOE_P2P"] = "1"
         res["nccl_close"] = float((nccl.float() - exact.float()).abs().max()) <= \
             float(exact.float().abs().max()) * 2 ** -7
+        # two-shot exchange (T * H * 2 > 16 MiB at two ranks): same definition
+        T3 = 4200
+        idx3 = torch.stack([torch.randperm(E2, generator=g2)[:K2] for _ in range(T3)]).long()
+        rows3 = torch.randn(T3 * K2, H2, generator=g2).bfloat16().to(dev)
+        _, _, _, inv3 = oracle.permute(idx3, E2)
+        inv3, idx3 = inv3.to(dev), idx3.to(dev)
+        parts3 = [ops.combine(rows3, inv3, idx3, order=_lib.ORDER_EXPERT, expert_lo=q * half,
+                              expert_hi=(q + 1) * half).float() for q in range(WORLD)]
+        exact3 = (parts3[0] + parts3[1]).bfloat16()
+        res["p2p_two_shot_equal"] = all(bool(torch.equal(pg.combine_reduce(rows3, inv3, idx3, lo, hi),
+                                                        exact3)) for _ in range(2))
+        del rows3
+        # ---- router sharded over the group == routed whole, bit for bit
+        from moe_serving_profile_b200.router import Qwen3Router
+        rconf = SimpleNamespace(num_experts_per_tok=8, num_experts=128, norm_topk_prob=True,
+                                hidden_size=2048)
+        whole = Qwen3Router(rconf).to(dev)
+        whole.weight.data = w.router
+        shard = Qwen3Router(rconf).to(dev).shard_over(pg)
+        shard.weight.data = w.router
+        xr = S.make_hidden(2048, 2048, seed=9, device=dev)
+        a, b = whole(xr), shard(xr)
+        res["router_shard_equal"] = all(bool(torch.equal(u, v)) for u, v in zip(a, b)) and \
+            bool(torch.equal(whole.last_counts, shard.last_counts))
         res["status"] = _lib.device_status(rank)
         torch.cuda.synchronize(dev)
         pg.close()
@@ -159,3 +186,5 @@ def test_expert_parallel_over_nccl():
         assert res["a2a_equal"], f"rank {r}: all-to-all differs from the one-process run"
         assert res["p2p_used"] and res["p2p_equal"] and res["p2p_graph_equal"], res
         assert res["nccl_close"] and res["status"] == 0, res
+        assert res["router_shard_equal"], res
+        assert res["p2p_two_shot_equal"], res
