@@ -188,7 +188,9 @@ typedef struct b200moe_gemm_args {
   int expert_begin;     /* first global expert id handled by this launch */
   int n_experts;        /* local experts in the weight stack */
   int max_rows;         /* upper bound on rows of these experts (T*K) */
-  int token_tile;       /* 0 = choose; else 16, 32, 64, 128 or 256 */
+  int token_tile;       /* 0 = choose (a power of two covering 1.5x the mean rows per
+                           expert, at most 128 for quantised weights); else 16,
+                           32, 64, 128 or 256 */
   int split_k;          /* reserved: must be 0 or 1 */
   /* weights (A operand) */
   int wfmt;             /* B200MOE_W_* */

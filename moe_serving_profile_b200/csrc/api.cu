@@ -264,8 +264,10 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
     // slot (their A stages hold the other half of tensor memory), which
     // measured slower than two 128-token tiles
     const int max_auto = a->wfmt == B200MOE_W_BF16 ? 256 : 128;
-    const int avg = (a->max_rows + a->n_experts - 1) / a->n_experts;
-    bn = std::min(max_auto, std::max(16, pow2_ceil(avg)));
+    // 1.5x the mean rows per expert, so that one tile usually holds an
+    // expert's rows
+    const long long avg = (3ll * a->max_rows + 2ll * a->n_experts - 1) / (2ll * a->n_experts);
+    bn = std::min(max_auto, std::max(16, pow2_ceil(static_cast<int>(std::min(avg, 1ll << 20)))));
   }
   const int feat_tile = gated ? 64 : 128;
   const int feat_tiles = a->feat_pad / feat_tile;

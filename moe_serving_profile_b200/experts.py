@@ -30,8 +30,11 @@ def _sm_count(device: int) -> int:
 
 def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256) -> int:
     """Token tile (the MMA N) for one grouped GEMM launch: the smallest power
-    of two in [16, max_tile] covering the mean rows per expert."""
-    rows = T * K / num_experts
+    of two in [16, max_tile] covering 1.5x the mean rows per expert, so that
+    one tile usually holds an expert's rows (a second, nearly empty tile costs
+    a whole tile's k-block loop: 512 tokens with 32-token tiles took 2.3x
+    the time of 64-token tiles on B200)."""
+    rows = 1.5 * T * K / num_experts
     bn = 16
     while bn < max_tile and bn < rows:
         bn *= 2

@@ -104,9 +104,9 @@ def test_wrappers_refuse_cpu_tensors():
         ops.gather_rows(torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(4, dtype=torch.int32), 1)
 
 
-@pytest.mark.parametrize("T,K,E,bn", [(1, 8, 128, 16), (64, 8, 128, 16), (512, 8, 128, 32),
+@pytest.mark.parametrize("T,K,E,bn", [(1, 8, 128, 16), (64, 8, 128, 16), (512, 8, 128, 64),
                                       (4096, 8, 128, 256), (2048, 4, 32, 256), (16, 4, 32, 16),
-                                      (64, 4, 32, 16), (256, 8, 128, 16)])
+                                      (64, 4, 32, 16), (256, 8, 128, 32), (1024, 8, 128, 128)])
 def test_tile_policy(T, K, E, bn):
     assert tile_policy(T, K, E) == bn
 
