@@ -157,9 +157,10 @@ int b200moe_permute_noalloc(int device, void* stream, const long long* indices, 
  *     fp32 scales of rows 0-63 and 64-127 then 8 zero bytes (blob 8208 B);
  *     other FP8 blocks, fp32 [128 rows][4 chunks of 16 columns] (blob
  *     10240 B); MXFP4, ue8m0 [128 rows][2 groups of 32 columns] (blob 4352 B).
- * Quantised weights are converted by the CTA into tensor memory; with a
- * 256-token tile the accumulator then has one slot (the epilogue of a tile
- * does not overlap the next tile's main loop).
+ * Quantised weights are converted by the CTA into tensor memory: up to
+ * 128-token tiles beside 8 A stages, 160-token tiles beside 6, both with two
+ * accumulator slots; with a 256-token tile the accumulator has one slot (the
+ * epilogue of a tile does not overlap the next tile's main loop).
  * Epilogues:
  *   B200MOE_EPI_SWIGLU     bf16(bf16(silu(bf16 g)) * bf16 u)
  *                          (moe_serving/qwen3_parallel.py:84-94)
@@ -189,8 +190,8 @@ typedef struct b200moe_gemm_args {
   int n_experts;        /* local experts in the weight stack */
   int max_rows;         /* upper bound on rows of these experts (T*K) */
   int token_tile;       /* 0 = choose (a power of two covering 1.5x the mean rows per
-                           expert, at most 128 for quantised weights); else 16,
-                           32, 64, 128 or 256 */
+                           expert; 160 instead of 256 for quantised weights);
+                           else 16, 32, 64, 128, 160 or 256 */
   int split_k;          /* reserved: must be 0 or 1 */
   /* weights (A operand) */
   int wfmt;             /* B200MOE_W_* */

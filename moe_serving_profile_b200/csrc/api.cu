@@ -249,8 +249,9 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
                "fp8 weights need a scale block with columns a multiple of 16");
   if (a->row_weight) B200_CHECK(a->row_src != nullptr, "row_weight needs row_src");
   B200_CHECK(a->token_tile == 0 || a->token_tile == 16 || a->token_tile == 32 ||
-                 a->token_tile == 64 || a->token_tile == 128 || a->token_tile == 256,
-             "token_tile must be 0 or a power of two in [16, 256]");
+                 a->token_tile == 64 || a->token_tile == 128 || a->token_tile == 160 ||
+                 a->token_tile == 256,
+             "token_tile must be 0, 16, 32, 64, 128, 160 or 256");
   if (a->split_k > 1) return fail(B200MOE_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
   B200_CHECK(a->split_k >= 0, "split_k must be 0 or 1");
   int* sp = nullptr;
@@ -260,10 +261,10 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   const bool gated = a->planes == 2;
   int bn = a->token_tile;
   if (bn == 0) {
-    // quantised weights: 256-token tiles would leave a single accumulator
-    // slot (their A stages hold the other half of tensor memory), which
-    // measured slower than two 128-token tiles
-    const int max_auto = a->wfmt == B200MOE_W_BF16 ? 256 : 128;
+    // quantised weights: at most 160 tokens, the largest tile with two
+    // accumulator slots beside the tensor-memory A stages (a 256-token tile
+    // would get one slot, which measured slower)
+    const int max_auto = a->wfmt == B200MOE_W_BF16 ? 256 : 160;
     // 1.5x the mean rows per expert, so that one tile usually holds an
     // expert's rows
     const long long avg = (3ll * a->max_rows + 2ll * a->n_experts - 1) / (2ll * a->n_experts);
@@ -308,9 +309,10 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
       return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
   } else {
     // token-row stages: 8, matching the A stages (one commit releases both),
-    // while at least 8 raw stages still fit; else 4
-    na = 8;
-    nb = 8;
+    // while at least 8 raw stages still fit; else 4. A 160-token tile keeps
+    // two accumulator slots (columns 0..319) beside 6 A stages (320..511).
+    na = bn == 160 ? 6 : 8;
+    nb = na;
     if (nb * b_stage + xbytes + barbytes + 8 * rpb > budget) nb = 4;
     const uint32_t fixed = nb * b_stage + xbytes + barbytes;
     nr = fixed < budget ? static_cast<int>((budget - fixed) / rpb) : 0;
@@ -370,13 +372,13 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.nbanks = std::min(p.nacc, p.nkb);
   // quantised weights keep their A stages in TMEM columns 256..511, so a
   // 256-token tile gets a single accumulator slot
-  p.acc_slots = (rpb && bn > 128) ? 1 : 2;
+  p.acc_slots = (rpb && bn > 160) ? 1 : 2;
   p.joint_ab = na == nb ? 1 : 0;
   // two MMA issuers when there are banks for both and the A / B rings split
   // evenly between them
   p.n_issuers = (p.nacc % 2 == 0 && na % 2 == 0 && nb % 2 == 0) ? 2 : 1;
   p.tmem_cols = rpb ? 512u : static_cast<uint32_t>(std::max(32, pow2_ceil(p.acc_slots * p.nacc * bn)));
-  p.a_col0 = 256u;
+  p.a_col0 = (rpb && bn == 160) ? 320u : 256u;
 
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
   if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");

@@ -38,14 +38,15 @@ def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256) -> int:
     bn = 16
     while bn < max_tile and bn < rows:
         bn *= 2
-    return bn
+    return min(bn, max_tile)
 
 
 def _max_tile(w: ExpertWeights) -> int:
-    # quantised weights: two 128-token tiles beat one 256-token tile, whose
-    # accumulator would have a single slot (the A stages hold the other half
-    # of tensor memory)
-    return 256 if w.fmt == _lib.W_BF16 else 128
+    # quantised weights: at most 160 tokens, the largest tile whose two
+    # accumulator slots fit beside the converted-weight stages in tensor
+    # memory (a 256-token tile would get a single slot); 160 keeps an expert
+    # with up to 320 rows at two tiles (4096 tokens: 18 % faster than 128)
+    return 256 if w.fmt == _lib.W_BF16 else 160
 
 
 def run_experts(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,

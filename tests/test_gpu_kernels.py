@@ -276,7 +276,7 @@ def _pack_weight(fmt, wv, planes=1):
 
 
 @pytest.mark.parametrize("fmt", [_lib.W_FP8, _lib.W_MXFP4, _lib.W_BF16])
-@pytest.mark.parametrize("tile,split", [(16, 1), (32, 0), (64, 1), (128, 1), (256, 1), (0, 0)])
+@pytest.mark.parametrize("tile,split", [(16, 1), (32, 0), (64, 1), (128, 1), (160, 1), (256, 1), (0, 0)])
 def test_down_gemm_integer_exact(cuda, fmt, tile, split):
     E, feat, K, T, topk = 6, 296, 448, 150, 3
     g, wv, x, idx = _int_case(fmt, E, feat, K, T, topk, seed=fmt * 10 + tile + split)
@@ -314,7 +314,7 @@ def test_gemm_rejects_split_k(cuda):
 
 
 @pytest.mark.parametrize("fmt", [_lib.W_FP8, _lib.W_MXFP4, _lib.W_BF16])
-@pytest.mark.parametrize("tile,split", [(16, 1), (64, 1), (128, 1), (256, 1)])
+@pytest.mark.parametrize("tile,split", [(16, 1), (64, 1), (128, 1), (160, 1), (256, 1)])
 def test_gated_gemm_integer_exact(cuda, fmt, tile, split):
     """Gate/up planes with exact pre-activations; SwiGLU epilogue vs torch."""
     E, inter, H, T, topk = 5, 200, 320, 97, 2

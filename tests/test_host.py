@@ -109,6 +109,7 @@ def test_wrappers_refuse_cpu_tensors():
                                       (64, 4, 32, 16), (256, 8, 128, 32), (1024, 8, 128, 128)])
 def test_tile_policy(T, K, E, bn):
     assert tile_policy(T, K, E) == bn
+    assert tile_policy(T, K, E, 160) == min(bn, 160)
 
 
 def test_fp8_layout_pads_with_zeros():
