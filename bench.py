@@ -10,7 +10,8 @@ with the workload's shapes (random-init, quantised as the checkpoints are).
 time, each batch replayed from a CUDA graph with L2 flushed (a 256 MiB write)
 before it, timed with CUDA events. ``e2e`` is the same metric through the
 public modules (router + ParallelExperts forward, eager) with the tokens
-copied from pinned host memory and the outputs copied back every batch.
+copied from pinned host memory and the outputs copied back every batch; the
+copies run on their own streams and overlap other batches' compute.
 
 N > 1 (torchrun, one rank per GPU): replicated-token expert parallelism, the
 reference's record_* layout: every rank routes all tokens and runs its E/N
@@ -403,12 +404,29 @@ def main():
     h2d = sum(T * cfg.hidden * 2 for T in batches)
     d2h = h2d
 
+    # Copies run on their own streams: every batch's tokens go host -> device
+    # on copy_in up front, each output goes device -> host on copy_out as soon
+    # as its layer call ends, so transfers overlap other batches' compute.
+    copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    dev_x = {T: torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=dev) for T in batches}
+
     def e2e_step():
-        with torch.cuda.stream(stream):
+        copy_in.wait_stream(stream)   # the previous step's layer calls have read dev_x
+        landed = {}
+        with torch.cuda.stream(copy_in):
             for T in batches:
-                xd = host_x[T].to(dev, non_blocking=True)
-                o = layer_call(cfg, router, packed, xd, parallel, rank, world)
+                dev_x[T].copy_(host_x[T], non_blocking=True)
+                landed[T] = torch.cuda.Event()
+                landed[T].record(copy_in)
+        for T in batches:
+            stream.wait_event(landed[T])
+            with torch.cuda.stream(stream):
+                o = layer_call(cfg, router, packed, dev_x[T], parallel, rank, world)
+            copy_out.wait_stream(stream)
+            with torch.cuda.stream(copy_out):
                 host_o[T].copy_(o, non_blocking=True)
+                o.record_stream(copy_out)
+        stream.wait_stream(copy_out)
 
     for _ in range(2):
         e2e_step()
@@ -417,9 +435,10 @@ def main():
         dist.barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
+    copy_in.wait_stream(stream)   # the timed region starts before the first copy
     for _ in range(args.steps):
         e2e_step()
-    e.record(stream)
+    e.record(stream)   # after every copy of the last step (stream waited on copy_out)
     torch.cuda.synchronize(dev)
     e2e_ms = s.elapsed_time(e) / args.steps
     if world > 1:
