@@ -49,19 +49,28 @@ __global__ void __launch_bounds__(128) combine_kernel(
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (int i = 0; i < n; ++i) {
-      const uint4 q = __ldg(reinterpret_cast<const uint4*>(rows + rsel[i] * ld_rows) + v);
-      const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+    // up to 8 rows' vectors are loaded before any is added, then added in
+    // the sorted order (the loads overlap; the arithmetic order is unchanged)
+    for (int i0 = 0; i0 < n; i0 += 8) {
+      uint4 q[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float c0 = __uint_as_float(wd[j] << 16);
-        float c1 = __uint_as_float(wd[j] & 0xffff0000u);
-        if (scale_rows) {
-          c0 = bf16r(c0 * wsel[i]);
-          c1 = bf16r(c1 * wsel[i]);
+      for (int u = 0; u < 8; ++u)
+        if (i0 + u < n) q[u] = __ldg(reinterpret_cast<const uint4*>(rows + rsel[i0 + u] * ld_rows) + v);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (i0 + u >= n) break;
+        const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float c0 = __uint_as_float(wd[j] << 16);
+          float c1 = __uint_as_float(wd[j] & 0xffff0000u);
+          if (scale_rows) {
+            c0 = bf16r(c0 * wsel[i0 + u]);
+            c1 = bf16r(c1 * wsel[i0 + u]);
+          }
+          acc[2 * j] = bf16r(acc[2 * j] + c0);
+          acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
         }
-        acc[2 * j] = bf16r(acc[2 * j] + c0);
-        acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
       }
     }
     uint4 o;

@@ -166,25 +166,33 @@ __global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_con
       float acc[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int i = 0; i < n; ++i) {
-        float wv = 1.f;
-        if (p.scale_rows) {
-          const long long wi = (long long)t * p.K + ksel[i];
-          wv = p.weights_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.weights)[wi])
-                              : reinterpret_cast<const float*>(p.weights)[wi];
-        }
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(p.rows + rsel[i] * p.ld_rows) + v);
-        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+      // up to 8 rows' vectors are loaded before any is added (same order)
+      for (int i0 = 0; i0 < n; i0 += 8) {
+        uint4 qv[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float c0 = __uint_as_float(wd[j] << 16);
-          float c1 = __uint_as_float(wd[j] & 0xffff0000u);
+        for (int u = 0; u < 8; ++u)
+          if (i0 + u < n) qv[u] = __ldg(reinterpret_cast<const uint4*>(p.rows + rsel[i0 + u] * p.ld_rows) + v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (i0 + u >= n) break;
+          float wv = 1.f;
           if (p.scale_rows) {
-            c0 = bf16r(c0 * wv);
-            c1 = bf16r(c1 * wv);
+            const long long wi = (long long)t * p.K + ksel[i0 + u];
+            wv = p.weights_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.weights)[wi])
+                                : reinterpret_cast<const float*>(p.weights)[wi];
           }
-          acc[2 * j] = bf16r(acc[2 * j] + c0);
-          acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
+          const uint32_t wd[4] = {qv[u].x, qv[u].y, qv[u].z, qv[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float c0 = __uint_as_float(wd[j] << 16);
+            float c1 = __uint_as_float(wd[j] & 0xffff0000u);
+            if (p.scale_rows) {
+              c0 = bf16r(c0 * wv);
+              c1 = bf16r(c1 * wv);
+            }
+            acc[2 * j] = bf16r(acc[2 * j] + c0);
+            acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
+          }
         }
       }
       const uint4 o = pack_row(acc);
