@@ -84,6 +84,15 @@ int b200moe_router(int device, void* stream, int mode, const void* hidden,
                    int E, int K, int normalize, void* logits, void* probs, void* scores,
                    long long* indices, int* counts, int logits_given);
 
+/* Compact routing record of one router call (the per-layer capture of
+ * moe_serving/record_routing.py:71-77: expert ids as int16, routing weights
+ * as fp16): out_indices[i] = (int16) indices[i], out_scores[i] =
+ * fp16_rn(scores[i]) for i < n, scores fp32 (scores_bf16 = 0) or bf16 (1).
+ * Written on the device so a recorder reads a whole step back with one
+ * copy instead of converting and copying at every layer. Ids must fit int16. */
+int b200moe_route_record(int device, void* stream, const long long* indices, const void* scores,
+                         int scores_bf16, long long n, void* out_indices, void* out_scores);
+
 /* ------------------------------------------------------------ permutation
  * Expert-contiguous permutation of the T*K (token, slot) assignments.
  * Within an expert, rows are ordered slot-major then by token, the order of

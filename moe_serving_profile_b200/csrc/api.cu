@@ -148,6 +148,18 @@ int b200moe_router(int device, void* stream, int mode, const void* hidden, long 
   return B200MOE_OK;
 }
 
+int b200moe_route_record(int device, void* stream, const long long* indices, const void* scores,
+                         int scores_bf16, long long n, void* out_indices, void* out_scores) {
+  B200_CHECK(n >= 0 && (scores_bf16 == 0 || scores_bf16 == 1), "bad record arguments");
+  if (n == 0) return B200MOE_OK;
+  B200_CHECK(indices && scores && out_indices && out_scores, "indices, scores and outputs are required");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_route_record(static_cast<cudaStream_t>(stream), indices, scores, scores_bf16, n,
+                                      out_indices, out_scores));
+  return B200MOE_OK;
+}
+
 int b200moe_permute_workspace(int T, int K, int E, size_t* bytes) {
   B200_CHECK(bytes != nullptr, "bytes is NULL");
   B200_CHECK(T >= 0 && K >= 1 && E >= 1, "bad sizes");

@@ -15,6 +15,9 @@ cudaError_t launch_router_select(cudaStream_t st, int mode, const void* logits, 
                                  int K, int normalize, void* probs, void* scores,
                                  long long* indices, int* counts);
 
+cudaError_t launch_route_record(cudaStream_t st, const long long* indices, const void* scores,
+                                int scores_bf16, long long n, void* out_idx, void* out_scores);
+
 size_t permute_workspace_bytes(int T, int K, int E);
 cudaError_t launch_permute(cudaStream_t st, const long long* indices, int T, int K, int E,
                            int* counts, int* offsets, int* perm_src, int* inverse,

@@ -412,6 +412,25 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
   }
 }
 
+// Compact routing record: int64 expert ids -> int16, fp32 / bf16 weights ->
+// fp16 (round to nearest even), 4 assignments per thread.
+__global__ void __launch_bounds__(256) route_record_kernel(const long long* __restrict__ indices,
+                                                           const void* __restrict__ scores,
+                                                           int scores_bf16, long long n,
+                                                           int16_t* __restrict__ out_idx,
+                                                           __half* __restrict__ out_scores) {
+  const long long i0 = 4ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const long long i = i0 + u;
+    if (i >= n) return;
+    out_idx[i] = static_cast<int16_t>(indices[i]);
+    const float w = scores_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(scores)[i])
+                                : reinterpret_cast<const float*>(scores)[i];
+    out_scores[i] = __float2half_rn(w);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_router_logits(cudaStream_t st, int mode, const void* hidden, long long ldx,
@@ -454,6 +473,15 @@ cudaError_t launch_router_select(cudaStream_t st, int mode, const void* logits, 
   router_select_kernel<<<blocks, 256, 0, st>>>(logits, T, E, K, mode, normalize,
                                                static_cast<float*>(probs), scores, indices,
                                                counts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_record(cudaStream_t st, const long long* indices, const void* scores,
+                                int scores_bf16, long long n, void* out_idx, void* out_scores) {
+  if (n == 0) return cudaSuccess;
+  const long long threads = (n + 3) / 4;
+  route_record_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
+      indices, scores, scores_bf16, n, static_cast<int16_t*>(out_idx), static_cast<__half*>(out_scores));
   return cudaGetLastError();
 }
 

@@ -93,6 +93,30 @@ def router(mode: int, hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Te
     return RouterOut(logits_t, probs, scores, indices, counts)
 
 
+def route_record(indices: torch.Tensor, scores: torch.Tensor,
+                 out_indices: torch.Tensor | None = None,
+                 out_scores: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(int16 expert ids, fp16 routing weights) of one router call, on the device."""
+    device = _dev(indices, "indices")
+    if indices.dtype != torch.int64 or not indices.is_contiguous():
+        raise ValueError("indices must be contiguous int64")
+    if scores.dtype not in (torch.float32, torch.bfloat16) or not scores.is_contiguous():
+        raise ValueError("scores must be contiguous float32 or bfloat16")
+    if scores.shape != indices.shape:
+        raise ValueError("indices and scores shapes differ")
+    if out_indices is None:
+        out_indices = torch.empty(indices.shape, device=indices.device, dtype=torch.int16)
+    if out_scores is None:
+        out_scores = torch.empty(indices.shape, device=indices.device, dtype=torch.float16)
+    check(
+        lib.b200moe_route_record(device, _stream(device), _ptr(indices), _ptr(scores),
+                                 int(scores.dtype == torch.bfloat16), indices.numel(),
+                                 _ptr(out_indices), _ptr(out_scores)),
+        "route_record",
+    )
+    return out_indices, out_scores
+
+
 # --------------------------------------------------------------------------- permutation
 @dataclass
 class Permutation:

@@ -127,3 +127,38 @@ def test_recv_plan_transposes_segments(cuda):
     assert plan.map_back.cpu().tolist() == back
     assert plan.offsets.cpu().tolist() == [0] + torch.cumsum(counts.sum(0), 0).tolist()
     assert _lib.device_status(cuda.index) == 0
+
+
+def test_routing_records_match_the_reference_capture(cuda):
+    """Per step, every router call's ids as int16 and weights as fp16 (the
+    capture of moe_serving/record_routing.py:71-77), read back in one copy:
+    equal to converting each router output on the host."""
+    from types import SimpleNamespace
+
+    from torch import nn
+
+    from moe_serving_profile_b200.recording import RoutingRecords
+    from moe_serving_profile_b200.router import GptOssRouter, Qwen3Router
+
+    g = torch.Generator().manual_seed(3)
+    q = Qwen3Router(SimpleNamespace(num_experts_per_tok=8, num_experts=128, norm_topk_prob=True,
+                                    hidden_size=256)).to(cuda)
+    q.weight.data = (torch.randn(128, 256, generator=g) * 0.05).bfloat16().to(cuda)
+    o = GptOssRouter(SimpleNamespace(num_experts_per_tok=4, num_local_experts=32,
+                                     hidden_size=256)).to(cuda)
+    o.weight.data = (torch.randn(32, 256, generator=g) * 0.05).bfloat16().to(cuda)
+    o.bias.data = (torch.randn(32, generator=g) * 0.1).bfloat16().to(cuda)
+    model = nn.ModuleDict({"layer0": q, "layer1": o})
+    rec = RoutingRecords.attach(model)
+    try:
+        for T in (5, 300):
+            x = torch.randn(T, 256, generator=g).bfloat16().to(cuda)
+            rec.begin()
+            outs = {"layer0": q(x), "layer1": o(x)}
+            step = rec.end()
+            assert set(step) == {"layer0", "layer1"}
+            for name, (_, scores, idx) in outs.items():
+                assert torch.equal(step[name]["indices"], idx.to(torch.int16).cpu())
+                assert torch.equal(step[name]["scores"], scores.to(torch.float16).cpu())
+    finally:
+        rec.close()
