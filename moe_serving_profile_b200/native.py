@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 from moe_serving_profile_b200 import _lib, ops
-from moe_serving_profile_b200.experts import check_inputs, run_experts
+from moe_serving_profile_b200.experts import check_inputs, run_experts, tile_policy
 from moe_serving_profile_b200.layout import bf16_experts
 from moe_serving_profile_b200.router import native_route
 
@@ -175,6 +175,47 @@ class LocalSwiGLUExperts(torch.nn.Module):
         return ops.gather_rows(y, perm.inverse, 1)
 
 
+class SharedSwiGLU(torch.nn.Module):
+    """The shared expert every token passes through (moe_serving/moe.py:84-95):
+    sigmoid(hidden . score) * down(silu(hidden . gate) * (hidden . up)), all
+    bf16. gate / up [I_s, H], down [H, I_s], score [1, H]. The two
+    projections run as a one-expert launch of the grouped GEMM over all T rows
+    (SwiGLU epilogue, then the down epilogue); the [T, 1] score projection and
+    the final scaling are a GEMV and one elementwise multiply."""
+
+    def __init__(self, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor,
+                 score: torch.Tensor):
+        super().__init__()
+        for t in (gate, up, down, score):
+            if t.dtype != torch.bfloat16:
+                raise ValueError("SharedSwiGLU weights must be bfloat16")
+        self.hidden = down.shape[0]
+        self.intermediate = down.shape[1]
+        self.weights = bf16_experts(gate[None], up[None], down[None])
+        self.score = torch.nn.Parameter(score, requires_grad=False)
+
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        T = hidden.shape[0]
+        if T == 0:
+            return hidden.new_empty(0, self.hidden)
+        w = self.weights
+        hidden = hidden.contiguous()
+        offsets = torch.zeros(2, dtype=torch.int32, device=hidden.device)
+        offsets[1] = T
+        bn = tile_policy(T, 1, 1)
+        act = torch.empty(T, w.i_pad, device=hidden.device, dtype=torch.bfloat16)
+        ops.expert_gemm(offsets=offsets, expert_begin=0, n_experts=1, max_rows=T, wfmt=_lib.W_BF16,
+                        planes=2, feat_pad=w.i_pad, n_feat=w.inter, k_pad=w.h_k, weight=w.w1,
+                        b_src=hidden, k_valid=self.hidden, epilogue=_lib.EPI_SWIGLU, out=act,
+                        token_tile=bn)
+        y = torch.empty(T, self.hidden, device=hidden.device, dtype=torch.bfloat16)
+        ops.expert_gemm(offsets=offsets, expert_begin=0, n_experts=1, max_rows=T, wfmt=_lib.W_BF16,
+                        planes=1, feat_pad=w.h_f, n_feat=self.hidden, k_pad=w.i_pad, weight=w.w2,
+                        b_src=act, k_valid=self.intermediate, epilogue=_lib.EPI_DOWN, out=y,
+                        token_tile=bn)
+        return torch.sigmoid(torch.nn.functional.linear(hidden, self.score)) * y
+
+
 def route(hidden: torch.Tensor, gate_weight: torch.Tensor, top_k: int,
           renormalize: bool) -> tuple[torch.Tensor, torch.Tensor]:
     """moe_serving/moe.py:97-107: (index int64 [T,K], weight [T,K] in hidden's dtype)."""
@@ -257,18 +298,16 @@ def routed_forward(hidden: torch.Tensor, expert_index: torch.Tensor, expert_weig
 
 
 class MoELayer(torch.nn.Module):
-    """Router + token all-to-all experts (moe_serving/moe.py:140-168). The
-    shared expert is not implemented on this path."""
+    """Router + token all-to-all experts + optional shared expert
+    (moe_serving/moe.py:140-168)."""
 
     def __init__(self, gate_weight: torch.Tensor, experts: LocalSwiGLUExperts, plan: ExpertPlan,
-                 top_k: int, renormalize: bool = True, shared=None,
+                 top_k: int, renormalize: bool = True, shared: SharedSwiGLU | None = None,
                  collective: Collective | None = None, layer_id: int = 0):
         super().__init__()
-        if shared is not None:
-            raise NotImplementedError("the shared expert is not implemented on the b200 path")
         self.gate_weight = torch.nn.Parameter(gate_weight, requires_grad=False)
         self.experts = experts
-        self.shared = None
+        self.shared = shared
         self.plan = plan
         self.top_k = top_k
         self.renormalize = renormalize
@@ -280,6 +319,8 @@ class MoELayer(torch.nn.Module):
                          self.renormalize)
         output = routed_forward(hidden, out.indices, out.scores, self.experts, self.plan,
                                 self.collective)
+        if self.shared is not None:
+            output = output + self.shared(hidden)
         return output, RoutingStats(counts=out.counts.to(torch.int64).cpu(), layer=self.layer_id)
 
 
@@ -301,12 +342,14 @@ def simulate_routed(hiddens: list[torch.Tensor], indices: list[torch.Tensor],
 
 def simulate_ranks(hiddens: list[torch.Tensor], gates: torch.Tensor,
                    expert_banks: list[LocalSwiGLUExperts], top_k: int, renormalize: bool = True,
-                   shared=None) -> list[torch.Tensor]:
+                   shared: list[SharedSwiGLU] | None = None) -> list[torch.Tensor]:
     """Every rank inside one process (moe_serving/moe.py:171-224): the same
     kernels as ``routed_forward`` with ``exchange_inplace`` standing in for
-    the all-to-all. Used to check the all-to-all math on one GPU."""
-    if shared is not None:
-        raise NotImplementedError("the shared expert is not implemented on the b200 path")
+    the all-to-all, plus each rank's shared expert. Used to check the
+    all-to-all math on one GPU."""
     routes = [route(h, gates, top_k, renormalize) for h in hiddens]
-    return simulate_routed(hiddens, [r[0] for r in routes], [r[1] for r in routes], expert_banks,
+    outs = simulate_routed(hiddens, [r[0] for r in routes], [r[1] for r in routes], expert_banks,
                            gates.shape[0])
+    if shared is not None:
+        outs = [o + shared[r](h) for r, (o, h) in enumerate(zip(outs, hiddens))]
+    return outs

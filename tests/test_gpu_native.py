@@ -162,3 +162,34 @@ def test_routing_records_match_the_reference_capture(cuda):
                 assert torch.equal(step[name]["scores"], scores.to(torch.float16).cpu())
     finally:
         rec.close()
+
+
+@pytest.mark.parametrize("T", [1, 37, 300])
+def test_shared_expert_and_layer(cuda, T):
+    """SharedSwiGLU (moe_serving/moe.py:84-95) against the same op in fp32
+    PyTorch, and MoELayer with a shared expert = routed part + shared part
+    (moe.py:161-162), also through simulate_ranks."""
+    H, I_s, E, I, K = 512, 384, 16, 256, 4
+    g = torch.Generator().manual_seed(T)
+    sg = (torch.randn(I_s, H, generator=g) * 0.05).bfloat16()
+    su = (torch.randn(I_s, H, generator=g) * 0.05).bfloat16()
+    sd = (torch.randn(H, I_s, generator=g) * 0.05).bfloat16()
+    sc = (torch.randn(1, H, generator=g) * 0.05).bfloat16()
+    h = torch.randn(T, H, generator=g).bfloat16()
+    shared = native.SharedSwiGLU(sg.to(cuda), su.to(cuda), sd.to(cuda), sc.to(cuda))
+    out = shared(h.to(cuda))
+    hf = h.float()
+    act = torch.nn.functional.silu(hf @ sg.float().T) * (hf @ su.float().T)
+    ref = torch.sigmoid(hf @ sc.float().T) * (act @ sd.float().T)
+    _close(out.cpu(), ref.bfloat16(), "shared expert")
+
+    gate_up, down, gate, (hh,) = _case(E, H, I, K, [T], seed=T + 1)
+    experts = native.LocalSwiGLUExperts(gate_up.to(cuda), down.to(cuda))
+    plan = native.ExpertPlan(E, 1, 0)
+    layer = native.MoELayer(gate.to(cuda), experts, plan, K, shared=shared)
+    y, stats = layer(hh.to(cuda))
+    idx, wts = native.route(hh.to(cuda), gate.to(cuda), K, True)
+    routed = native.routed_forward(hh.to(cuda), idx, wts, experts, plan, native.SingleRank())
+    assert torch.equal(y, routed + shared(hh.to(cuda)))
+    sim = native.simulate_ranks([hh.to(cuda)], gate.to(cuda), [experts], K, shared=[shared])
+    assert torch.equal(sim[0], y)
