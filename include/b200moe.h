@@ -282,7 +282,8 @@ int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_
  * 16 MiB pushed per rank (T * H * 2 * (world - 1)) every rank pushes its
  * partial rows to every rank (one-shot); above, each row goes to one owner
  * rank, which sums it and pushes the finished row to every rank (two-shot).
- * The result is the same either way. It is exported with b200moe_p2p_export
+ * The result is the same either way. Two-shot needs a world size of 2, 4 or
+ * 8 (B200MOE_ERR_UNSUPPORTED otherwise). It is exported with b200moe_p2p_export
  * and mapped by the other ranks with b200moe_p2p_import (CUDA IPC; plain
  * peer loads and stores over NVLink, no multicast objects). peers[world] are
  * the buffers' addresses in this process, peers[rank] the local one. All

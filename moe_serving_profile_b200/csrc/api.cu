@@ -536,6 +536,9 @@ int b200moe_combine_allreduce(int device, void* stream, const void* rows, long l
     return fail(B200MOE_ERR_UNSUPPORTED, "combine_allreduce supports 1..%d ranks", b200::kP2PMaxRanks);
   B200_CHECK(rank >= 0 && rank < world, "rank %d outside [0, %d)", rank, world);
   B200_CHECK(T <= t_cap, "T=%d exceeds the exchange buffer's %d rows", T, t_cap);
+  if (!b200::p2p_supported(T, H, world))
+    return fail(B200MOE_ERR_UNSUPPORTED,
+                "exchanges above 16 MiB per rank need a world size dividing 1024 (world=%d)", world);
   B200_CHECK(peers != nullptr, "peers are required");
   for (int i = 0; i < world; ++i)
     B200_CHECK(peers[i] != nullptr && aligned16(peers[i]), "peer buffer %d missing or unaligned", i);

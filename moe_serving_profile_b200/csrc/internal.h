@@ -38,16 +38,20 @@ cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            long long ld_out);
 
 // Exchange-buffer layout of the fused combine + all-reduce (p2p.cu).
-constexpr int kP2PBlocks = 1024;    // block b owns rows t = b (mod 1024); a multiple of every world size
+constexpr int kP2PBlocks = 1024;    // block b owns rows t = b (mod 1024)
 constexpr int kP2PMaxRanks = 8;
 constexpr size_t kP2PHeaderBytes = 69632;  // flags [2][1024][8] u32 + epochs [1024] u32
 static_assert(2 * kP2PBlocks * kP2PMaxRanks * 4 + kP2PBlocks * 4 <= kP2PHeaderBytes, "p2p header");
 constexpr long long kP2POneShotBytes = 16ll << 20;   // one-shot up to this many pushed bytes per rank
 
 // The exchange of T rows pushes every partial row to every rank (one-shot)
-// or to its row's owner only (two-shot).
+// or to its row's owner only (two-shot; the owner of row t is t % world and
+// its inbox slot t / world, which needs world to divide kP2PBlocks).
 inline bool p2p_two_shot(int T, int H, int world) {
   return world > 1 && (long long)T * H * 2 * (world - 1) > kP2POneShotBytes;
+}
+inline bool p2p_supported(int T, int H, int world) {
+  return !p2p_two_shot(T, H, world) || kP2PBlocks % world == 0;
 }
 // Inbox rows per (parity, source) of a buffer for up to t_cap rows.
 inline int p2p_inbox_rows(int t_cap, int H, int world) {

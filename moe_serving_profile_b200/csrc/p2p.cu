@@ -21,8 +21,8 @@
 //     push partial[t] into inbox [rank][t] of every rank (posted NVLink
 //     stores); signal every peer, wait for every peer (bounded); out[t] =
 //     bf16(fp32 sum of inbox [0 .. world)[t] in rank order), local reads.
-//   two-shot (larger exchanges): the rows of block b belong to rank
-//     o = b % world (kP2PBlocks is a multiple of every world size); push
+//   two-shot (larger exchanges, world sizes dividing kP2PBlocks: 2, 4, 8):
+//     the rows of block b belong to rank o = b % world (= t % world); push
 //     partial[t] only to inbox [rank][t / world] of rank o and signal it;
 //     rank o waits for every source, sums in rank order as above, pushes the
 //     finished row into every rank's finished area [t] and signals them; every

@@ -17,6 +17,8 @@ import torch.distributed as dist
 # Largest batch the fused combine + all-reduce exchanges (its buffers hold
 # this many rows); larger batches use combine + the NCCL all-reduce.
 P2P_MAX_ROWS = 8192
+# Above this many pushed bytes per rank the fused exchange runs two-shot.
+P2P_ONE_SHOT_BYTES = 16 << 20
 
 
 class PeerExchange:
@@ -113,6 +115,8 @@ class ParallelGroup:
         t_cap = P2P_MAX_ROWS
         if T > t_cap:
             return None
+        if T * hidden * 2 * (self.size - 1) > P2P_ONE_SHOT_BYTES and 1024 % self.size:
+            return None   # the two-shot exchange needs a group size of 2, 4 or 8
         ex = self._exchange
         if ex is None or ex.hidden != hidden or ex.device != device:
             if torch.cuda.is_current_stream_capturing():

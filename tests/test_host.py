@@ -203,3 +203,15 @@ def test_backend_checks_and_metadata():
     assert "fp8" in backend.backend_metadata("qwen3", "fast")["experts"]
     with pytest.raises(ValueError):
         backend.backend_metadata("qwen3", "efficient")
+
+
+def test_two_shot_exchange_needs_a_group_size_dividing_1024():
+    """Above 16 MiB pushed per rank the fused exchange runs two-shot, whose
+    row-to-owner slots need the group size to divide 1024: 3 ranks are
+    refused (before any device work), 4 pass the argument checks."""
+    peers = (ctypes.c_void_p * 4)(*([0x1000] * 4))
+    fake = ctypes.c_void_p(0x1000)
+    args = lambda world: (0, None, fake, 2048, fake, fake, 4000, 8, 2048, 0, 128, 0, None, 0, world, 0,
+                          peers, 8192, fake, 2048, 0)
+    assert _lib.lib.b200moe_combine_allreduce(*args(3)) == _lib.ERR_UNSUPPORTED
+    assert _lib.lib.b200moe_combine_allreduce(*args(4)) != _lib.ERR_UNSUPPORTED
