@@ -10,6 +10,7 @@
 """
 
 import ctypes
+import json
 import re
 
 import pytest
@@ -215,3 +216,54 @@ def test_two_shot_exchange_needs_a_group_size_dividing_1024():
                           peers, 8192, fake, 2048, 0)
     assert _lib.lib.b200moe_combine_allreduce(*args(3)) == _lib.ERR_UNSUPPORTED
     assert _lib.lib.b200moe_combine_allreduce(*args(4)) != _lib.ERR_UNSUPPORTED
+
+
+def test_checkpoint_loader_packs_what_layout_packs(tmp_path):
+    """Load-time preparation from a safetensors checkpoint (sharded, with an
+    index) gives the same packed experts as packing the same tensors directly,
+    for one expert-parallel rank's slice (CPU)."""
+    from safetensors.torch import save_file
+
+    from moe_serving_profile_b200 import loader
+    from moe_serving_profile_b200 import synthetic as S
+
+    cfg = S.LayerConfig("probe", "qwen3", 256, 4, 2, 128, "fp8", (1,))
+    w = S.make_qwen(cfg, seed=2)
+    shard_a, shard_b, index = {}, {}, {}
+    for e in range(cfg.experts):
+        for proj, wt, sc in (("gate_proj", w.gate, w.gate_scale), ("up_proj", w.up, w.up_scale),
+                             ("down_proj", w.down, w.down_scale)):
+            name = f"model.layers.3.mlp.experts.{e}.{proj}"
+            shard = shard_a if e < 2 else shard_b
+            shard[name + ".weight"] = wt[e].contiguous()
+            shard[name + ".weight_scale_inv"] = sc[e].contiguous()
+            index[name + ".weight"] = index[name + ".weight_scale_inv"] = "a.safetensors" if e < 2 \
+                else "b.safetensors"
+    save_file(shard_a, str(tmp_path / "a.safetensors"))
+    save_file(shard_b, str(tmp_path / "b.safetensors"))
+    (tmp_path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": index}))
+    got = loader.qwen3_fp8_experts(tmp_path, layer=3, start=2, count=2, block=cfg.block, device="cpu")
+    want = layout.fp8_experts(w.gate[2:4], w.gate_scale[2:4], w.up[2:4], w.up_scale[2:4],
+                              w.down[2:4], w.down_scale[2:4], cfg.block)
+    assert torch.equal(got.w1, want.w1) and torch.equal(got.w2, want.w2)
+    assert (got.n_experts, got.hidden, got.inter) == (2, 256, 128)
+
+
+def test_checkpoint_loader_gpt_oss_slices_the_expert_axis(tmp_path):
+    from safetensors.torch import save_file
+
+    from moe_serving_profile_b200 import loader
+    from moe_serving_profile_b200 import synthetic as S
+
+    cfg = S.LayerConfig("probe", "gpt_oss", 128, 4, 2, 64, "mxfp4", (1,))
+    w = S.make_gpt_oss(cfg, seed=4)
+    p = "model.layers.0.mlp.experts."
+    save_file({p + "gate_up_proj_blocks": w.gu_blocks.contiguous(), p + "gate_up_proj_scales": w.gu_scales,
+               p + "gate_up_proj_bias": w.gu_bias, p + "down_proj_blocks": w.dn_blocks.contiguous(),
+               p + "down_proj_scales": w.dn_scales, p + "down_proj_bias": w.dn_bias},
+              str(tmp_path / "model.safetensors"))
+    got = loader.gpt_oss_mxfp4_experts(tmp_path, layer=0, start=1, count=2, device="cpu")
+    want = layout.gpt_oss_mxfp4_experts(w.gu_blocks[1:3], w.gu_scales[1:3], w.gu_bias[1:3],
+                                        w.dn_blocks[1:3], w.dn_scales[1:3], w.dn_bias[1:3], 1.702, 7.0)
+    assert torch.equal(got.w1, want.w1) and torch.equal(got.w2, want.w2)
+    assert torch.equal(got.b1, want.b1) and torch.equal(got.b2, want.b2)
