@@ -93,6 +93,19 @@ int b200moe_router(int device, void* stream, int mode, const void* hidden,
 int b200moe_route_record(int device, void* stream, const long long* indices, const void* scores,
                          int scores_bf16, long long n, void* out_indices, void* out_scores);
 
+/* Dynamic FP8 activation quantisation of the W8A8 ("efficient") FP8 path
+ * (moe_serving/efficient_kernels.py:243-274, the activation side of the hub
+ * finegrained-fp8 matmul_grouped): per row r and 128-column group g,
+ * s[r,g] = amax / 448 over the group's bf16 values (1 for an all-zero
+ * group) and q[r,c] = e4m3fn(x[src(r),c] / s[r,g]), round to nearest even,
+ * saturating at +-448; q = 0 for k_valid <= c < k_pad.
+ * x: bf16 rows of stride ldx elements; src(r) = map[r] / map_div when map is
+ * given (the permuted-row gather perm_src / K), else r. q: e4m3 [rows, k_pad];
+ * s: fp32 [rows, ceil(k_pad / 128)]. Needs k_valid % 4 == 0, ldx % 4 == 0,
+ * k_pad % 16 == 0 and k_valid <= k_pad. */
+int b200moe_act_quant_fp8(int device, void* stream, const void* x, long long ldx, const int* map,
+                          int map_div, int rows, int k_valid, int k_pad, void* q, float* s);
+
 /* ------------------------------------------------------------ permutation
  * Expert-contiguous permutation of the T*K (token, slot) assignments.
  * Within an expert, rows are ordered slot-major then by token, the order of

@@ -30,6 +30,7 @@ EXPORTED = (
     "b200moe_device_status",
     "b200moe_router",
     "b200moe_route_record",
+    "b200moe_act_quant_fp8",
     "b200moe_permute_workspace",
     "b200moe_permute",
     "b200moe_permute_noalloc",
@@ -105,6 +106,9 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_route_record.restype = c_int
     lib.b200moe_route_record.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_longlong,
                                          c_void_p, c_void_p]
+    lib.b200moe_act_quant_fp8.restype = c_int
+    lib.b200moe_act_quant_fp8.argtypes = [c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int,
+                                          c_int, c_int, c_void_p, c_void_p]
     lib.b200moe_permute_workspace.restype = c_int
     lib.b200moe_permute_workspace.argtypes = [c_int, c_int, c_int, POINTER(c_size_t)]
     lib.b200moe_permute.restype = c_int

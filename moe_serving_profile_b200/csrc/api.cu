@@ -49,6 +49,7 @@ std::mutex g_mu;
 int* g_status_ptr[kMaxDevices] = {};
 int g_sm_count[kMaxDevices] = {};
 bool g_gemm_attr[kMaxDevices] = {};
+bool g_w8a8_attr[kMaxDevices][4] = {};
 void* g_permute_scratch_ptr[kMaxDevices] = {};
 
 int use_device(int device, int** status) {
@@ -157,6 +158,25 @@ int b200moe_route_record(int device, void* stream, const long long* indices, con
   if (rc) return rc;
   B200_CUDA(b200::launch_route_record(static_cast<cudaStream_t>(stream), indices, scores, scores_bf16, n,
                                       out_indices, out_scores));
+  return B200MOE_OK;
+}
+
+int b200moe_act_quant_fp8(int device, void* stream, const void* x, long long ldx, const int* map,
+                          int map_div, int rows, int k_valid, int k_pad, void* q, float* s) {
+  B200_CHECK(rows >= 0 && k_valid >= 0 && k_pad >= k_valid, "bad sizes rows=%d k_valid=%d k_pad=%d", rows,
+             k_valid, k_pad);
+  B200_CHECK(k_valid % 4 == 0 && k_pad % 16 == 0 && ldx % 4 == 0 && ldx >= k_valid,
+             "need k_valid %% 4 == 0, k_pad %% 16 == 0, ldx %% 4 == 0 and ldx >= k_valid");
+  B200_CHECK(map == nullptr || map_div >= 1, "map_div must be >= 1");
+  B200_CHECK((long long)rows * ((k_pad + 127) / 128) < (1ll << 40), "too many groups");
+  if (rows == 0 || k_pad == 0) return B200MOE_OK;
+  B200_CHECK(x && q && s, "x, q and s are required");
+  B200_CHECK(reinterpret_cast<uintptr_t>(x) % 8 == 0 && reinterpret_cast<uintptr_t>(q) % 4 == 0,
+             "x must be 8-byte and q 4-byte aligned");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_act_quant(static_cast<cudaStream_t>(stream), x, ldx, map, map_div, rows, k_valid,
+                                   k_pad, q, s));
   return B200MOE_OK;
 }
 
@@ -438,6 +458,111 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   cfg.dynamicSmemBytes = smem;
   cfg.stream = static_cast<cudaStream_t>(stream);
   void* args[] = {&wmap, &bmap, &p};
+  B200_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
+  return B200MOE_OK;
+}
+
+int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* a, const void* q,
+                      const float* q_scale) {
+  B200_CHECK(a != nullptr, "args is NULL");
+  if (a->max_rows <= 0) return B200MOE_OK;
+  B200_CHECK(a->offsets && a->weight && q && q_scale && a->out, "offsets, weight, q, q_scale, out are required");
+  B200_CHECK(a->wfmt == B200MOE_W_FP8, "W8A8 needs FP8 weights");
+  B200_CHECK(a->sc_br >= 64 && a->sc_br % 64 == 0 && a->sc_bc == 128,
+             "W8A8 needs FP8 scale blocks of 128 columns and a multiple of 64 rows");
+  B200_CHECK(a->planes == 1 || a->planes == 2, "planes must be 1 or 2");
+  B200_CHECK((a->planes == 2 && a->epilogue == B200MOE_EPI_SWIGLU) ||
+                 (a->planes == 1 && a->epilogue == B200MOE_EPI_DOWN),
+             "W8A8 supports the SwiGLU gate/up and the down epilogues");
+  B200_CHECK(a->bias == nullptr, "W8A8 has no bias");
+  B200_CHECK(a->b_map == nullptr, "W8A8 reads quantised permuted rows (b_map must be NULL)");
+  B200_CHECK(a->n_experts >= 1 && a->expert_begin >= 0, "bad expert range");
+  if (a->n_experts > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "at most 1024 experts per launch");
+  B200_CHECK(a->feat_pad >= 128 && a->feat_pad % 128 == 0, "feat_pad must be a positive multiple of 128");
+  B200_CHECK(a->n_feat >= 1 && a->n_feat <= a->feat_pad, "n_feat out of range");
+  B200_CHECK(a->k_pad >= 64 && a->k_pad % 64 == 0, "k_pad must be a positive multiple of 64");
+  B200_CHECK(a->b_rows >= 1 && aligned16(q), "q must be 16-byte aligned with b_rows >= 1");
+  B200_CHECK(aligned16(a->weight), "weight must be 16-byte aligned");
+  B200_CHECK(a->ldo >= a->n_feat && a->ldo % 8 == 0 && a->n_feat % 8 == 0 && aligned16(a->out),
+             "output rows must be 16-byte aligned (ldo %% 8 == 0, n_feat %% 8 == 0)");
+  if (a->row_weight) B200_CHECK(a->row_src != nullptr, "row_weight needs row_src");
+  B200_CHECK(a->token_tile == 0 || a->token_tile == 16 || a->token_tile == 32 || a->token_tile == 64 ||
+                 a->token_tile == 128,
+             "W8A8 token_tile must be 0, 16, 32, 64 or 128");
+  int* sp = nullptr;
+  int rc = use_device(device, &sp);
+  if (rc) return rc;
+
+  const bool gated = a->planes == 2;
+  int bn = a->token_tile;
+  if (bn == 0) {
+    const long long avg = (3ll * a->max_rows + 2ll * a->n_experts - 1) / (2ll * a->n_experts);
+    bn = std::min(128, std::max(16, pow2_ceil(static_cast<int>(std::min(avg, 1ll << 20)))));
+  }
+  const int feat_tiles = a->feat_pad / (gated ? 64 : 128);
+  const long long tiles_ub = (long long)(std::min(a->n_experts, a->max_rows) + a->max_rows / bn) * feat_tiles;
+
+  b200::W8A8Params p{};
+  p.offsets = a->offsets;
+  p.expert_begin = a->expert_begin;
+  p.n_experts = a->n_experts;
+  p.gated = gated ? 1 : 0;
+  p.feat_tiles = feat_tiles;
+  p.n_feat = a->n_feat;
+  p.nkb = a->k_pad / 64;
+  p.ngroups = (p.nkb + 1) / 2;
+  p.wblob = static_cast<const uint8_t*>(a->weight);
+  p.blob_bytes = 8192u + 16u;   // e4m3 rows + one fp32 scale per 64-row half
+  p.qs = q_scale;
+  p.qs_groups = (a->k_pad + 127) / 128;
+  p.row_w = a->row_weight;
+  p.row_w_bf16 = a->row_weight_bf16;
+  p.row_src = a->row_src;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.ldo = a->ldo;
+  p.status = sp;
+  // shared memory: stages of (8 KB weights + bn x 64 B token rows) on 1024-byte
+  // boundaries, the epilogue buffers, barriers + tile prefix
+  const uint32_t budget = 232448u - 2048u;
+  p.stage_bytes = (8192u + static_cast<uint32_t>(bn) * 64u + 1023u) & ~1023u;
+  const uint32_t xbytes = (b200::w8a8_epilogue_bytes(bn, p.gated) + 1023u) & ~1023u;
+  const uint32_t barbytes = ((8u * (2u * 16u + 5u) + 8u + 4u * (a->n_experts + 1) + 1023u) / 1024u) * 1024u;
+  p.ns = static_cast<int>(std::min<uint32_t>(16u, (budget - xbytes - barbytes) / p.stage_bytes));
+  if (p.ns < 2) return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
+  p.x_off = p.ns * p.stage_bytes;
+  p.bar_off = p.x_off + xbytes;
+  const uint32_t smem = p.bar_off + barbytes + 1024u;   // + alignment slack
+  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(2 * bn)));
+
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap qmap;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->k_pad), static_cast<cuuint64_t>(a->b_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a->k_pad)};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(bn)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "activation tensor map failed (%d)", (int)cr);
+  }
+  const int ti = bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : 3;
+  const void* kern = b200::w8a8_kernel_ptr(bn);
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_w8a8_attr[device][ti]) {
+      B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024));
+      g_w8a8_attr[device][ti] = true;
+    }
+  }
+  const int grid = static_cast<int>(std::min<long long>(g_sm_count[device], tiles_ub));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  void* args[] = {&qmap, &p};
   B200_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
   return B200MOE_OK;
 }

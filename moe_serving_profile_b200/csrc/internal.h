@@ -1,6 +1,7 @@
 // Launchers shared between the kernel translation units and the C ABI layer.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -17,6 +18,31 @@ cudaError_t launch_router_select(cudaStream_t st, int mode, const void* logits, 
 
 cudaError_t launch_route_record(cudaStream_t st, const long long* indices, const void* scores,
                                 int scores_bf16, long long n, void* out_idx, void* out_scores);
+
+// Per-(row, 128-column) FP8 activation quantisation (w8a8.cu).
+cudaError_t launch_act_quant(cudaStream_t st, const void* x, long long ldx, const int* map, int div,
+                             int rows, int k_valid, int k_pad, void* q, float* s);
+
+// W8A8 grouped GEMM (w8a8.cu): kernel parameters, filled by the host.
+struct W8A8Params {
+  const int* offsets;          // permuted-row offsets of the global experts
+  int expert_begin, n_experts;
+  int gated, feat_tiles, n_feat, nkb, ngroups;
+  const uint8_t* wblob;        // FP8 blobs (one fp32 scale per 64-row half)
+  uint32_t blob_bytes;
+  const float* qs;             // activation scales [rows][qs_groups]
+  int qs_groups;
+  const void* row_w;
+  int row_w_bf16;
+  const int* row_src;
+  __nv_bfloat16* out;
+  long long ldo;
+  int* status;
+  int ns;                      // pipeline stages
+  uint32_t stage_bytes, x_off, bar_off, tmem_cols;
+};
+uint32_t w8a8_epilogue_bytes(int bn, int gated);
+const void* w8a8_kernel_ptr(int bn);   // token tile 16, 32, 64 or 128; else NULL
 
 size_t permute_workspace_bytes(int T, int K, int E);
 cudaError_t launch_permute(cudaStream_t st, const long long* indices, int T, int K, int E,

@@ -249,6 +249,37 @@ B200_DEVI uint64_t sdesc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// As sdesc_k_sw128 for rows of 64 bytes in the 64-byte-swizzled canonical
+// layout (16-byte chunk c of row r at c ^ ((r >> 1) & 3); 8-row atoms of 512
+// bytes). The tile base must be 512-byte aligned.
+B200_DEVI uint64_t sdesc_k_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address  [0,14)
+  d |= static_cast<uint64_t>(1) << 16;                   // LBO (unused here) [16,30)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;            // SBO = 512 B  [32,46)
+  d |= static_cast<uint64_t>(1) << 46;                   // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(4) << 61;                   // layout: 64-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: kind::f8f6f4, A = B = E4M3, D = F32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4)                                  // D format F32 (A, B format 0 = E4M3)
+         | (static_cast<uint32_t>(N >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
+}
+
+// D (+)= A * B for one 32-byte (32 x e4m3) slice of K.
+B200_DEVI void umma_e4m3(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Instruction descriptor: kind::f16, A = B = BF16, D = F32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                                  // D format F32

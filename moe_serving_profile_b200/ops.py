@@ -117,6 +117,33 @@ def route_record(indices: torch.Tensor, scores: torch.Tensor,
     return out_indices, out_scores
 
 
+def act_quant_fp8(x: torch.Tensor, k_pad: int | None = None, rows_src: torch.Tensor | None = None,
+                  src_div: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dynamic FP8 activation quantisation of the W8A8 FP8 path: e4m3 ``q``
+    [rows, k_pad] and fp32 ``scales`` [rows, ceil(k_pad / 128)], one scale per
+    row and 128-column group (amax / 448). With ``rows_src`` (int32), row r
+    quantises ``x[rows_src[r] // src_div]`` (the permuted-row gather)."""
+    device = _dev(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be a 2-D bfloat16 tensor with unit column stride")
+    k_valid = x.shape[1]
+    k_pad = k_valid if k_pad is None else k_pad
+    rows = x.shape[0]
+    if rows_src is not None:
+        _dev(rows_src, "rows_src")
+        if rows_src.dtype != torch.int32 or not rows_src.is_contiguous() or rows_src.dim() != 1:
+            raise ValueError("rows_src must be contiguous 1-D int32")
+        rows = rows_src.numel()
+    q = torch.empty((rows, k_pad), device=x.device, dtype=torch.float8_e4m3fn)
+    s = torch.empty((rows, -(-k_pad // 128)), device=x.device, dtype=torch.float32)
+    check(
+        lib.b200moe_act_quant_fp8(device, _stream(device), _ptr(x), x.stride(0), _ptr(rows_src),
+                                  int(src_div), rows, k_valid, k_pad, _ptr(q), _ptr(s)),
+        "act_quant_fp8",
+    )
+    return q, s
+
+
 # --------------------------------------------------------------------------- permutation
 @dataclass
 class Permutation:

@@ -229,6 +229,29 @@ def dequant_torch(w: torch.Tensor, scales: torch.Tensor, block, dtype=torch.bflo
     return (w.float() * expanded[:rows, :cols]).to(dtype)
 
 
+def act_quant_fp8(x: torch.Tensor, k_pad: int | None = None, rows_src: torch.Tensor | None = None,
+                  src_div: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dynamic per-(row, 128-column group) FP8 activation quantisation of the
+    W8A8 path (moe_serving/efficient_kernels.py:243-274 quantises the
+    activations inside the hub ``matmul_grouped``, which is not vendored in
+    the reference): s = amax / 448 per group (1 for an all-zero group),
+    q = e4m3fn(x / s) with round-to-nearest-even, saturating at +-448.
+    Columns k_valid .. k_pad - 1 quantise zeros."""
+    xf = x.float()
+    if rows_src is not None:
+        xf = xf[rows_src.long() // src_div]
+    rows, k = xf.shape
+    k_pad = k if k_pad is None else k_pad
+    groups = -(-k_pad // 128)
+    xp = torch.zeros(rows, groups * 128, dtype=torch.float32)
+    xp[:, :k] = xf
+    g = xp.view(rows, groups, 128)
+    amax = g.abs().amax(-1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (g / scale[..., None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(rows, groups * 128)[:, :k_pad].contiguous(), scale
+
+
 _E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
 
 
