@@ -155,6 +155,89 @@ def layer_call(cfg, router, packed, x, parallel, rank, ep):
                            numerics=numerics_for(ep))
 
 
+def w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst):
+    """The same layer in the reference's efficient FP8 numerics (W8A8,
+    ``numerics="efficient"``), reported beside the weight-only headline:
+    per-batch CUDA-graph replays after an L2 flush, and the W8A8 gate/up GEMM
+    of the largest batch timed alone."""
+    def call(x):
+        _, scores, idx = router(x)
+        return X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts, expert_begin=0,
+                               numerics="efficient")
+
+    batches = list(xs)
+    graphs = {}
+    with torch.cuda.stream(stream):
+        for T in batches:
+            for _ in range(2):
+                call(xs[T])
+    torch.cuda.synchronize(dev)
+    for T in batches:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            call(xs[T])
+        graphs[T] = g
+    warm = max(3, args.warmup)
+    recs = []
+    with torch.cuda.stream(stream):
+        for it in range(warm + args.steps):
+            for T in batches:
+                flush.fill_(T & 0xff)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                graphs[T].replay()
+                e.record(stream)
+                if it >= warm:
+                    recs.append((T, s, e))
+    torch.cuda.synchronize(dev)
+    ms = {T: 0.0 for T in batches}
+    for T, s, e in recs:
+        ms[T] += s.elapsed_time(e) / args.steps
+    per_batch = []
+    for T in batches:
+        with torch.cuda.stream(stream):
+            _, _, idx = router(xs[T])
+            counts = torch.bincount(idx.flatten(), minlength=cfg.experts).cpu()
+        gbs = S.algorithmic_bytes(cfg, T, counts) / (ms[T] / 1e3) / 1e9
+        tfs = S.algorithmic_flops(cfg, T) / (ms[T] / 1e3) / 1e12
+        per_batch.append({"tokens": T, "ms": round(ms[T], 4), "tokens_per_s": round(T / (ms[T] / 1e3), 1),
+                          "hbm_frac": round(gbs / hbm, 4), "tflops": round(tfs, 2)})
+    # the W8A8 gate/up GEMM of the largest batch, timed alone
+    Tm = max(batches)
+    with torch.cuda.stream(stream):
+        x = xs[Tm]
+        _, scores, idx = router(x)
+        perm = ops.permute(idx, cfg.experts)
+        R = Tm * cfg.top_k
+        q, qs = ops.act_quant_fp8(x, k_pad=packed.h_k, rows_src=perm.perm_src, src_div=cfg.top_k)
+        act = torch.empty(R, packed.i_pad, device=dev, dtype=torch.bfloat16)
+        kw = dict(offsets=perm.offsets, expert_begin=0, n_experts=packed.n_experts, max_rows=R, planes=2,
+                  feat_pad=packed.i_pad, n_feat=packed.inter, k_pad=packed.h_k, weight=packed.w1,
+                  fp8_block=packed.block, q=q, q_scale=qs, epilogue=_lib.EPI_SWIGLU, out=act,
+                  token_tile=X.tile_policy(Tm, cfg.top_k, cfg.experts, 128))
+        for _ in range(3):
+            ops.w8a8_gemm(**kw)
+        kms = 0.0
+        for _ in range(10):
+            flush.fill_(2)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            ops.w8a8_gemm(**kw)
+            e.record(stream)
+            e.synchronize()
+            kms += s.elapsed_time(e) / 10
+    gemm_tf = 2 * R * cfg.hidden * 2 * cfg.inter / (kms / 1e3) / 1e12
+    for g in graphs.values():
+        del g
+    total_ms = sum(ms.values())
+    return {"value": round(sum(batches) / (total_ms / 1e3), 1), "unit": "tokens/s",
+            "ms_per_step": round(total_ms, 4), "numerics": "efficient (W8A8: e4m3 activations per "
+            "row and 128 columns, e4m3 block-128 weights, kind::f8f6f4 MMAs)", "per_batch": per_batch,
+            "gate_up": {"tokens": Tm, "ms": round(kms, 4), "tflops": round(gemm_tf, 2),
+                        "frac_of_bf16_burst": round(gemm_tf / tf_burst, 4),
+                        "frac_of_fp8_nominal_2x_bf16": round(gemm_tf / (2 * tf_burst), 4)}}
+
+
 def kernel_launches(T: int, K: int, E: int) -> int:
     """Our kernels per layer call: router (2) + permute (1 or 3) + row gather
     (large token tiles only) + 2 GEMMs + combine."""
@@ -245,7 +328,12 @@ def profile_calls(args, cfg):
     for T in (args.tokens or cfg.batches):
         x = S.make_hidden(T, cfg.hidden, seed=1000 + T, device=dev)
         for _ in range(3):
-            layer_call(cfg, router, packed, x, None, 0, 1)
+            if args.w8a8_profile:
+                _, scores, idx = router(x)
+                X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts, expert_begin=0,
+                                numerics="efficient")
+            else:
+                layer_call(cfg, router, packed, x, None, 0, 1)
         torch.cuda.synchronize(dev)
     assert _lib.device_status(0) == 0
 
@@ -258,9 +346,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--workload", default="qwen3-30b-a3b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-w8a8", action="store_true", help="skip the W8A8 (efficient FP8) report")
     ap.add_argument("--profile", action="store_true",
                     help="eager layer calls only (for ncu): 3 calls per --tokens batch")
     ap.add_argument("--tokens", type=int, nargs="*", default=None)
+    ap.add_argument("--w8a8-profile", action="store_true",
+                    help="with --profile: the W8A8 (efficient FP8) layer instead of weight-only")
     args = ap.parse_args()
     cfg = S.CONFIGS[args.workload]
     if args.impl == "reference":
@@ -447,6 +538,10 @@ def main():
         e2e_ms = float(t[0])
     e2e_value = tokens / (e2e_ms / 1e3)
 
+    w8a8 = None
+    if world == 1 and cfg.storage == "fp8" and not args.no_w8a8:
+        w8a8 = w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample = cpu_sweep(cfg, budget_s=20.0)
@@ -471,6 +566,8 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches, "clocks": clocks.summary(), "cpu_baseline": cpu,
         }
+        if w8a8 is not None:
+            line["w8a8"] = w8a8
         print(json.dumps(line), flush=True)
     for g in graphs.values():
         del g

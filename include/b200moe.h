@@ -247,6 +247,24 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* args)
 /* sizeof(b200moe_gemm_args), so foreign bindings can check their mirror. */
 size_t b200moe_gemm_args_size(void);
 
+/* W8A8 grouped GEMM of the reference's efficient FP8 mode: replaces the
+ * hub finegrained-fp8 matmul_grouped calls of grouped_fp8
+ * (moe_serving/efficient_kernels.py:255-265). The B operand is e4m3 token
+ * rows already quantised per (row, 128-column group) by
+ * b200moe_act_quant_fp8, in permuted row order: q [b_rows, k_pad] and
+ * q_scale fp32 [b_rows, ceil(k_pad / 128)]. Weights are the packed FP8
+ * blobs of b200moe_expert_gemm (wfmt = B200MOE_W_FP8, scale blocks of a
+ * multiple of 64 rows x 128 columns). For weight row f and permuted row n:
+ *   D[n, f] = sum_g sw[f, g] * q_scale[n, g] * sum_{k in g} W[f, k] * q[n, k]
+ * (tensor-core fp32 inner sums, fp32 promotion). Epilogues: planes = 2 with
+ * B200MOE_EPI_SWIGLU writes bf16(bf16(silu(bf16 gate)) * bf16 up) (the
+ * reference's act_fn(gate) * up on the bf16 GEMM output); planes = 1 with
+ * B200MOE_EPI_DOWN writes bf16(D), times the row's routing weight when
+ * row_weight is given (bf16(bf16(D) * w)). b_src, ldb, k_valid, b_map and
+ * bias must be NULL / unused; token_tile is 0 (choose) or 16, 32, 64, 128. */
+int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* args, const void* q,
+                      const float* q_scale);
+
 /* ------------------------------------------------------------ combine
  * out[t, :] = ordered bf16 sum over the slots k of token t of the
  * contribution rows c[inverse[t*K+k], :], starting from bf16 zero and

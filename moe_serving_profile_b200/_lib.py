@@ -35,6 +35,7 @@ EXPORTED = (
     "b200moe_permute",
     "b200moe_permute_noalloc",
     "b200moe_expert_gemm",
+    "b200moe_w8a8_gemm",
     "b200moe_combine",
     "b200moe_gather_rows",
     "b200moe_gather_rows_range",
@@ -122,6 +123,8 @@ def _load() -> ctypes.CDLL:
     ]
     lib.b200moe_expert_gemm.restype = c_int
     lib.b200moe_expert_gemm.argtypes = [c_int, c_void_p, POINTER(GemmArgs)]
+    lib.b200moe_w8a8_gemm.restype = c_int
+    lib.b200moe_w8a8_gemm.argtypes = [c_int, c_void_p, POINTER(GemmArgs), c_void_p, c_void_p]
     lib.b200moe_gemm_args_size.restype = c_size_t
     lib.b200moe_gemm_args_size.argtypes = []
     if lib.b200moe_gemm_args_size() != ctypes.sizeof(GemmArgs):

@@ -112,6 +112,41 @@ def down(w: ExpertWeights, act: torch.Tensor, perm: ops.Permutation,
     return contrib
 
 
+def run_experts_w8a8(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
+                     weights: torch.Tensor | None, *, K: int, num_experts: int, expert_begin: int,
+                     contrib: torch.Tensor | None = None,
+                     b_map_div: int | None = None) -> torch.Tensor:
+    """``run_experts`` in the reference's efficient FP8 numerics (W8A8,
+    moe_serving/efficient_kernels.py:243-274): the routed token rows and the
+    gated activations are quantised to e4m3 per (row, 128-column group) and
+    multiplied with the e4m3 weights on the tensor cores; FP32 block scales
+    of both sides are applied per group in fp32."""
+    if w.fmt != _lib.W_FP8 or w.block[1] != 128 or w.block[0] % 64:
+        raise ValueError("W8A8 needs FP8 weights with scale blocks of 128 columns (rows a multiple of 64)")
+    T, H = hidden.shape
+    if H != w.hidden:
+        raise ValueError(f"hidden size {H} does not match the experts' {w.hidden}")
+    R = perm.perm_src.numel()
+    dev = hidden.device
+    bn = tile_policy(T, K, num_experts, 128)
+    div = K if b_map_div is None else b_map_div
+    q, qs = ops.act_quant_fp8(hidden, k_pad=w.h_k, rows_src=perm.perm_src, src_div=div)
+    act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16)
+    ops.w8a8_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts, max_rows=R,
+                  planes=2, feat_pad=w.i_pad, n_feat=w.inter, k_pad=w.h_k, weight=w.w1,
+                  fp8_block=w.block, q=q, q_scale=qs, epilogue=_lib.EPI_SWIGLU, out=act,
+                  token_tile=bn)
+    q2, qs2 = ops.act_quant_fp8(act[:, :w.inter], k_pad=w.i_pad)
+    if contrib is None:
+        contrib = torch.empty(R, w.hidden, device=dev, dtype=torch.bfloat16)
+    ops.w8a8_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts, max_rows=R,
+                  planes=1, feat_pad=w.h_f, n_feat=w.hidden, k_pad=w.i_pad, weight=w.w2,
+                  fp8_block=w.block, q=q2, q_scale=qs2, epilogue=_lib.EPI_DOWN,
+                  row_weight=None if weights is None else weights.reshape(-1),
+                  row_src=perm.perm_src, out=contrib, token_tile=bn)
+    return contrib
+
+
 def check_inputs(hidden: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor) -> tuple:
     if hidden.dtype != torch.bfloat16:
         raise ValueError(f"b200 experts compute in bfloat16, got hidden {hidden.dtype}")
@@ -138,6 +173,8 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     EP size, the contract of moe_serving/parallel_numerics.py:13-36).
     numerics "fast": each rank combines its own experts and the partial sums
     are all-reduced (moe_serving/qwen3_parallel.py:105-118).
+    numerics "efficient" (FP8 weights): the W8A8 experts of the reference's
+    grouped_fp8 (moe_serving/efficient_kernels.py:243-274), combined like "fast".
     """
     hidden, indices, weights = check_inputs(hidden, indices, weights)
     T, K = indices.shape
@@ -145,6 +182,15 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
         return torch.empty_like(hidden)
     perm = ops.permute(indices, num_experts)
     size = 1 if parallel is None else parallel.size
+    if numerics == "efficient":
+        # W8A8 experts; the rank-local partial sums are all-reduced, the
+        # reference's efficient EP exchange (efficient_kernels.py:274)
+        contrib = run_experts_w8a8(w, hidden, perm, weights, K=K, num_experts=num_experts,
+                                   expert_begin=expert_begin)
+        if size == 1:
+            return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
+        return parallel.combine_reduce(contrib, perm.inverse, indices, expert_begin,
+                                       expert_begin + w.n_experts)
     if size == 1:
         contrib = run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
                               expert_begin=expert_begin)
@@ -164,4 +210,4 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
         # (parallel.combine_reduce) or combine + NCCL all-reduce
         return parallel.combine_reduce(contrib, perm.inverse, indices, expert_begin,
                                        expert_begin + w.n_experts)
-    raise ValueError(f"numerics must be reference or fast, got {numerics!r}")
+    raise ValueError(f"numerics must be reference, fast or efficient, got {numerics!r}")

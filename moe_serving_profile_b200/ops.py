@@ -247,6 +247,50 @@ def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max
     return out
 
 
+def w8a8_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max_rows: int,
+              planes: int, feat_pad: int, n_feat: int, k_pad: int, weight: torch.Tensor,
+              fp8_block: tuple[int, int] = (128, 128), q: torch.Tensor, q_scale: torch.Tensor,
+              epilogue: int, row_weight: torch.Tensor | None = None,
+              row_src: torch.Tensor | None = None, out: torch.Tensor,
+              token_tile: int = 0) -> torch.Tensor:
+    """W8A8 grouped GEMM: packed FP8 weight blobs times e4m3 permuted rows
+    ``q`` [rows, k_pad] with per-(row, 128-column) scales ``q_scale``
+    (``act_quant_fp8``'s outputs)."""
+    device = _dev(weight, "weight")
+    _bf16_rows(out, "output")
+    if q.dtype != torch.float8_e4m3fn or q.dim() != 2 or not q.is_contiguous() or q.shape[1] != k_pad:
+        raise ValueError(f"q must be contiguous float8_e4m3fn [rows, {k_pad}]")
+    groups = -(-k_pad // 128)
+    if (q_scale.dtype != torch.float32 or not q_scale.is_contiguous()
+            or tuple(q_scale.shape) != (q.shape[0], groups)):
+        raise ValueError(f"q_scale must be contiguous float32 [{q.shape[0]}, {groups}]")
+    a = _lib.GemmArgs()
+    a.offsets = _ptr(offsets)
+    a.expert_begin = expert_begin
+    a.n_experts = n_experts
+    a.max_rows = max_rows
+    a.token_tile = token_tile
+    a.wfmt = _lib.W_FP8
+    a.planes = planes
+    a.feat_pad = feat_pad
+    a.n_feat = n_feat
+    a.k_pad = k_pad
+    a.weight = _ptr(weight)
+    a.sc_br, a.sc_bc = fp8_block
+    a.b_rows = q.shape[0]
+    a.b_div = 1
+    a.epilogue = epilogue
+    if row_weight is not None:
+        a.row_weight = _ptr(row_weight)
+        a.row_weight_bf16 = int(row_weight.dtype == torch.bfloat16)
+        a.row_src = _ptr(row_src)
+    a.out = _ptr(out)
+    a.ldo = out.stride(0)
+    check(lib.b200moe_w8a8_gemm(device, _stream(device), ctypes.byref(a), _ptr(q), _ptr(q_scale)),
+          "w8a8_gemm")
+    return out
+
+
 # --------------------------------------------------------------------------- combine
 def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *, order: int,
             experts_per_rank: int = 1, expert_lo: int = 0, expert_hi: int = 1 << 30,

@@ -7,6 +7,8 @@ fills with ``ExpertProjection(weight, scales, block_size)`` for ``gate_proj``,
 ``up_proj`` and ``down_proj`` (FP8 E4M3 with fp32 block scales, or bf16 with
 no scales), and ``forward(hidden [T,H] bf16, indices [T,K] int64 global ids,
 weights [T,K] fp32) -> [T,H] bf16`` already reduced over the EP group.
+``numerics="efficient"`` runs the W8A8 experts of the reference's
+grouped_fp8 (moe_serving/efficient_kernels.py:243-274).
 
 On the first forward (or an explicit ``prepare()``) the per-expert modules
 are packed into the device layout of :mod:`layout` and released, as the
@@ -22,7 +24,7 @@ from moe_serving_profile_b200 import experts as _experts
 from moe_serving_profile_b200 import layout
 from moe_serving_profile_b200.parallel import ParallelGroup
 
-NUMERICS = ("reference", "fast")
+NUMERICS = ("reference", "fast", "efficient")
 
 
 class ExpertProjection(nn.Module):
@@ -74,6 +76,8 @@ class ParallelExperts(nn.Module):
             self.packed = layout.bf16_experts(gw.to(torch.bfloat16), uw.to(torch.bfloat16),
                                               dw.to(torch.bfloat16))
         self.local = None
+        if self.numerics == "efficient" and self.packed.fmt != layout._lib.W_FP8:
+            raise ValueError("efficient Qwen mode requires block FP8 expert weights")
         return self.packed
 
     def forward(self, hidden, indices, weights):

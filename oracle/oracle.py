@@ -252,6 +252,63 @@ def act_quant_fp8(x: torch.Tensor, k_pad: int | None = None, rows_src: torch.Ten
     return q.view(rows, groups * 128)[:, :k_pad].contiguous(), scale
 
 
+def w8a8_matmul(q: torch.Tensor, q_scale: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor,
+                block) -> torch.Tensor:
+    """One expert's W8A8 product in float64, the math of the hub
+    finegrained-fp8 ``matmul_grouped`` that grouped_fp8 calls
+    (moe_serving/efficient_kernels.py:255-265):
+    D[n, f] = sum_g w_scale[f // br, g] * q_scale[n, g] * sum_{k in g} W[f, k] * q[n, k]
+    over 128-column groups g. q: e4m3 [n, k_pad]; w: e4m3 [F, K] (K <= k_pad);
+    w_scale: [ceil(F / br), ceil(K / 128)]. Returns float64 [n, F]."""
+    br, bc = block
+    assert bc == 128, "W8A8 groups are 128 columns"
+    n, k_pad = q.shape
+    F, K = w.shape
+    groups = q_scale.shape[1]
+    qf = torch.zeros(n, groups * 128, dtype=torch.float64)
+    qf[:, :k_pad] = q.double()
+    wf = torch.zeros(F, groups * 128, dtype=torch.float64)
+    wf[:, :K] = w.double()
+    sw = w_scale.double().repeat_interleave(br, 0)[:F]                     # [F, >= groups]
+    out = torch.zeros(n, F, dtype=torch.float64)
+    for g in range(groups):
+        part = qf[:, g * 128:(g + 1) * 128] @ wf[:, g * 128:(g + 1) * 128].T
+        gs = min(g, sw.shape[1] - 1)
+        out += part * q_scale[:, g].double()[:, None] * sw[:, gs][None, :]
+    return out
+
+
+def qwen_w8a8_project(x: torch.Tensor, gate_w, gate_s, up_w, up_s, down_w, down_s, block,
+                      k_pad_h: int, k_pad_i: int) -> torch.Tensor:
+    """One expert of grouped_fp8 (moe_serving/efficient_kernels.py:255-265):
+    dynamic FP8 quantisation of the token rows, W8A8 gate/up with a bf16
+    output, bf16(silu(gate)) * up in bf16, quantisation of the activation,
+    W8A8 down with a bf16 output."""
+    q, qs = act_quant_fp8(x, k_pad=k_pad_h)
+    gate = w8a8_matmul(q, qs, gate_w, gate_s, block).to(torch.bfloat16)
+    up = w8a8_matmul(q, qs, up_w, up_s, block).to(torch.bfloat16)
+    act = F.silu(gate.float()).to(torch.bfloat16) * up
+    q2, qs2 = act_quant_fp8(act, k_pad=k_pad_i)
+    return w8a8_matmul(q2, qs2, down_w, down_s, block).to(torch.bfloat16)
+
+
+def qwen_w8a8_layer(hidden, indices, weights, gate_w, gate_s, up_w, up_s, down_w, down_s, block,
+                    k_pad_h: int | None = None, k_pad_i: int | None = None):
+    """W8A8 Qwen3 expert layer on one rank: the per-expert math of grouped_fp8
+    with the contributions bf16(y * w) added in ascending expert order (the
+    combine the GEMM path shares with the reference numerics)."""
+    H = hidden.shape[1]
+    inter = gate_w.shape[1]
+    k_pad_h = -(-H // 64) * 64 if k_pad_h is None else k_pad_h
+    k_pad_i = -(-inter // 128) * 128 if k_pad_i is None else k_pad_i
+
+    def project(e, x):
+        return qwen_w8a8_project(x, gate_w[e], gate_s[e], up_w[e], up_s[e], down_w[e], down_s[e], block,
+                                 k_pad_h, k_pad_i)
+
+    return ordered_expert_merge(hidden, indices, weights, project)
+
+
 _E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
 
 

@@ -202,8 +202,11 @@ def test_backend_checks_and_metadata():
     m = backend.backend_metadata("gpt_oss", "reference")
     assert "mxfp4" in m["experts"] and "ordered" in m["expert_parallel"]
     assert "fp8" in backend.backend_metadata("qwen3", "fast")["experts"]
+    assert "w8a8" in backend.backend_metadata("qwen3", "efficient")["experts"]
+    with pytest.raises(NotImplementedError):
+        backend.backend_metadata("gpt_oss", "efficient")
     with pytest.raises(ValueError):
-        backend.backend_metadata("qwen3", "efficient")
+        backend.backend_metadata("qwen3", "exact")
 
 
 def test_two_shot_exchange_needs_a_group_size_dividing_1024():
