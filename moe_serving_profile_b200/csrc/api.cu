@@ -526,13 +526,17 @@ int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* a, cons
   const uint32_t budget = 232448u - 2048u;
   p.stage_bytes = (8192u + static_cast<uint32_t>(bn) * 64u + 1023u) & ~1023u;
   const uint32_t xbytes = (b200::w8a8_epilogue_bytes(bn, p.gated) + 1023u) & ~1023u;
-  const uint32_t barbytes = ((8u * (2u * 16u + 5u) + 8u + 4u * (a->n_experts + 1) + 1023u) / 1024u) * 1024u;
+  const uint32_t nbuf = static_cast<uint32_t>(b200::w8a8_tmem_buffers(bn));
+  // full/empty per stage, acc_full/acc_empty per TMEM buffer, mma_done; tmem
+  // address, tile total, tile prefix
+  const uint32_t barbytes =
+      ((8u * (2u * 16u + 2u * nbuf + 1u) + 8u + 4u * (a->n_experts + 1) + 1023u) / 1024u) * 1024u;
   p.ns = static_cast<int>(std::min<uint32_t>(16u, (budget - xbytes - barbytes) / p.stage_bytes));
   if (p.ns < 2) return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
   p.x_off = p.ns * p.stage_bytes;
   p.bar_off = p.x_off + xbytes;
   const uint32_t smem = p.bar_off + barbytes + 1024u;   // + alignment slack
-  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(2 * bn)));
+  p.tmem_cols = static_cast<uint32_t>(std::max(32, pow2_ceil(static_cast<int>(nbuf) * bn)));
 
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
   if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -559,7 +563,7 @@ int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* a, cons
   const int grid = static_cast<int>(std::min<long long>(g_sm_count[device], tiles_ub));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(b200::kW8A8Threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = static_cast<cudaStream_t>(stream);
   void* args[] = {&qmap, &p};

@@ -41,7 +41,9 @@ struct W8A8Params {
   int ns;                      // pipeline stages
   uint32_t stage_bytes, x_off, bar_off, tmem_cols;
 };
+constexpr int kW8A8Threads = 320;   // copy warp, MMA warp, 8 promotion + epilogue warps
 uint32_t w8a8_epilogue_bytes(int bn, int gated);
+int w8a8_tmem_buffers(int bn);      // group accumulators in tensor memory (ping-pong or 4-deep)
 const void* w8a8_kernel_ptr(int bn);   // token tile 16, 32, 64 or 128; else NULL
 
 size_t permute_workspace_bytes(int T, int K, int E);

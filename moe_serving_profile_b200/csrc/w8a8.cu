@@ -76,8 +76,16 @@ cudaError_t launch_act_quant(cudaStream_t st, const void* x, long long ldx, cons
 // ------------------------------------------------------------------ GEMM
 namespace w8 {
 
-constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 promotion + epilogue
-constexpr uint32_t kAStage = 8192;   // 128 weight rows x 64 e4m3
+constexpr int kThreads = kW8A8Threads;   // warp 0 copies, warp 1 MMA, warps 2-9 promotion + epilogue
+constexpr int kEpi = kThreads - 64;      // promotion / epilogue threads
+constexpr uint32_t kAStage = 8192;       // 128 weight rows x 64 e4m3
+
+// Group accumulators in tensor memory: 4 for token tiles up to 64 rows, so
+// the MMAs run up to three groups ahead of the promotion; 2 for 128.
+template <int BN>
+__host__ __device__ constexpr int tmem_bufs() {
+  return BN <= 64 ? 4 : 2;
+}
 
 struct Tile {
   int e, ft, row0, nrows;
@@ -119,6 +127,23 @@ __device__ __forceinline__ float swiglu_bf16(float g, float u) {
   return bf16_rn(bf16_rn(gb / (1.f + expf(-gb))) * ub);
 }
 
+// The promotion scales of one 128-column group: token scale qs[row, g] of
+// the tile's row `te` (0 past the tile's rows) and the weight block scales
+// of rows 0-63 and 64-127 (the blob of k-block 2g).
+struct GroupScales {
+  float q, w0, w1;
+};
+
+__device__ __forceinline__ GroupScales load_scales(const W8A8Params& p, const uint8_t* wb, const Tile& tl,
+                                                   int te, int g) {
+  GroupScales s;
+  s.q = te < tl.nrows ? __ldg(p.qs + (long long)(tl.row0 + te) * p.qs_groups + g) : 0.f;
+  const float2 w = __ldg(reinterpret_cast<const float2*>(wb + (long long)(2 * g) * p.blob_bytes + kAStage));
+  s.w0 = w.x;
+  s.w1 = w.y;
+  return s;
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ W8A8Params p) {
@@ -128,13 +153,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sbase = smem_raw + (base_u32 - raw_u32);
   if (*reinterpret_cast<volatile int*>(p.status) & kStatusWaitTimeout) return;
 
+  constexpr int NB = tmem_bufs<BN>();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(sbase + p.bar_off);
   uint64_t* empty = full + p.ns;
-  uint64_t* acc_full = empty + p.ns;    // [2]
-  uint64_t* acc_empty = acc_full + 2;   // [2]
-  uint64_t* mma_done = acc_empty + 2;
+  uint64_t* acc_full = empty + p.ns;    // [NB]
+  uint64_t* acc_empty = acc_full + NB;  // [NB]
+  uint64_t* mma_done = acc_empty + NB;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
   int* s_total = reinterpret_cast<int*>(s_tmem + 1);
   int* prefix = s_total + 1;            // [n_experts + 1]
@@ -164,9 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&full[i], 1);
         mbar_init(&empty[i], 1);
       }
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < NB; ++i) {
         mbar_init(&acc_full[i], 1);
-        mbar_init(&acc_empty[i], 4);
+        mbar_init(&acc_empty[i], kEpi / 32);
       }
       mbar_init(mma_done, 1);
       fence_mbar_init();
@@ -212,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     // Group g of a tile (k-blocks 2g, 2g + 1) accumulates into buffer
-    // gc % 2 (gc counts the CTA's groups), which the promotion warps drain.
+    // gc % NB (gc counts the CTA's groups), which the promotion warps drain.
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
       Ring ring(p.ns);
@@ -220,8 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         for (int g = 0; ok && g < p.ngroups; ++g, ++gc) {
-          const int buf = gc & 1;
-          if (!wait_bounded(&acc_empty[buf], ((gc >> 1) & 1) ^ 1, p.status)) {
+          const int buf = gc % NB;
+          if (!wait_bounded(&acc_empty[buf], ((gc / NB) & 1) ^ 1, p.status)) {
             ok = false;
             break;
           }
@@ -252,16 +278,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------ promotion + epilogue
-    // Thread te = 0..127; warp w reads TMEM lanes 32 (w % 4) .. + 31, so its
-    // lane i holds weight row r = 32 (w % 4) + i: for gated tiles rows 0..63
-    // are gate and 64..127 up rows of the same 64 features.
+    // Warp w reads TMEM lanes 32 (w % 4) .. + 31, so its lane i holds weight
+    // row r = 32 (w % 4) + i (gated tiles: rows 0..63 gate, 64..127 up rows
+    // of the same 64 features); warps 2-5 take token columns [0, BN/2),
+    // warps 6-9 [BN/2, BN).
+    constexpr int CB = BN / 2;
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const int half = r >> 6;
+    const int n0 = ((warp - 2) >> 2) * CB;
     const int te = threadIdx.x - 64;
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    float* sa_s = reinterpret_cast<float*>(sbase + p.x_off);   // [2][128] activation scales
-    float* rowv = sa_s + 256;                                   // [128] routing weights
+    float* sc_s = reinterpret_cast<float*>(sbase + p.x_off);   // [2 slots][2 halves][128] combined scales
+    float* rowv = sc_s + 512;                                   // [128] routing weights
     float* ux = rowv + 128;                                     // gated: [BN][64] up values
     uint16_t* ost = reinterpret_cast<uint16_t*>(ux + (p.gated ? BN * 64 : 0));
     const bool scaled = !p.gated && p.row_w != nullptr;
@@ -274,29 +303,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         rowv[te] = p.row_w_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.row_w)[src])
                                 : reinterpret_cast<const float*>(p.row_w)[src];
       }
-      float tot[BN];
+      float tot[CB];
 #pragma unroll
-      for (int n = 0; n < BN; ++n) tot[n] = 0.f;
+      for (int n = 0; n < CB; ++n) tot[n] = 0.f;
       bool ok = true;
+      // scales of group g are loaded one group ahead, off the critical path
+      GroupScales nxt{};
+      if (te < BN) nxt = load_scales(p, wb, tl, te, 0);
       for (int g = 0; g < p.ngroups; ++g, ++gc) {
-        const int buf = gc & 1;
-        float* sa = sa_s + buf * 128;
-        if (te < BN)
-          sa[te] = te < tl.nrows ? p.qs[(long long)(tl.row0 + te) * p.qs_groups + g] : 0.f;
-        // the weight block scale of this row's half for k-blocks 2g, 2g + 1
-        const float sw = *reinterpret_cast<const float*>(wb + (long long)(2 * g) * p.blob_bytes + kAStage +
-                                                         4 * half);
-        // publishes sa and lets the four warps agree on success
-        ok = named_bar_and(1, 128, wait_bounded(&acc_full[buf], (gc >> 1) & 1, p.status, 64));
+        const int buf = gc % NB;
+        float* sc = sc_s + (gc & 1) * 256;
+        if (te < BN) {
+          sc[te] = nxt.q * nxt.w0;
+          sc[128 + te] = nxt.q * nxt.w1;
+          if (g + 1 < p.ngroups) nxt = load_scales(p, wb, tl, te, g + 1);
+        }
+        // publishes sc and lets the eight warps agree on success
+        ok = named_bar_and(1, kEpi, wait_bounded(&acc_full[buf], (gc / NB) & 1, p.status, 64));
         if (!ok) break;
         tc_fence_after();
+        const float4* s4 = reinterpret_cast<const float4*>(sc + half * 128 + n0);
+        if constexpr (CB % 16 == 0) {
 #pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(tq + static_cast<uint32_t>(buf * BN + c0), v);
+          for (int c0 = 0; c0 < CB; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tq + static_cast<uint32_t>(buf * BN + n0 + c0), v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const float4 s = s4[(c0 + j) >> 2];
+              tot[c0 + j] = fmaf(__uint_as_float(v[j]), s.x, tot[c0 + j]);
+              tot[c0 + j + 1] = fmaf(__uint_as_float(v[j + 1]), s.y, tot[c0 + j + 1]);
+              tot[c0 + j + 2] = fmaf(__uint_as_float(v[j + 2]), s.z, tot[c0 + j + 2]);
+              tot[c0 + j + 3] = fmaf(__uint_as_float(v[j + 3]), s.w, tot[c0 + j + 3]);
+            }
+          }
+        } else {
+          uint32_t v[8];
+          tmem_ld8(tq + static_cast<uint32_t>(buf * BN + n0), v);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) tot[c0 + j] = fmaf(__uint_as_float(v[j]), sw * sa[c0 + j], tot[c0 + j]);
+          for (int j = 0; j < 8; j += 4) {
+            const float4 s = s4[j >> 2];
+            tot[j] = fmaf(__uint_as_float(v[j]), s.x, tot[j]);
+            tot[j + 1] = fmaf(__uint_as_float(v[j + 1]), s.y, tot[j + 1]);
+            tot[j + 2] = fmaf(__uint_as_float(v[j + 2]), s.z, tot[j + 2]);
+            tot[j + 3] = fmaf(__uint_as_float(v[j + 3]), s.w, tot[j + 3]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -306,30 +359,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.gated) {
         if (half == 1) {
 #pragma unroll
-          for (int n = 0; n < BN; ++n) ux[n * 64 + (r - 64)] = tot[n];
+          for (int n = 0; n < CB; ++n) ux[(n0 + n) * 64 + (r - 64)] = tot[n];
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpi);
         if (half == 0) {
 #pragma unroll
-          for (int n = 0; n < BN; ++n)
-            ost[n * 72 + r] = static_cast<uint16_t>(__float_as_uint(swiglu_bf16(tot[n], ux[n * 64 + r])) >> 16);
+          for (int n = 0; n < CB; ++n)
+            ost[(n0 + n) * 72 + r] =
+                static_cast<uint16_t>(__float_as_uint(swiglu_bf16(tot[n], ux[(n0 + n) * 64 + r])) >> 16);
         }
-        named_bar_sync(1, 128);
-        for (int i = te; i < BN * 8; i += 128) {
+        named_bar_sync(1, kEpi);
+        for (int i = te; i < BN * 8; i += kEpi) {
           const int n = i >> 3, c8 = (i & 7) * 8;
           if (n < tl.nrows && tl.ft * 64 + c8 < p.n_feat)
             *reinterpret_cast<uint4*>(p.out + (long long)(tl.row0 + n) * p.ldo + tl.ft * 64 + c8) =
                 *reinterpret_cast<const uint4*>(ost + n * 72 + c8);
         }
       } else {
+        // rowv (written before the group barriers) is visible here
 #pragma unroll
-        for (int n = 0; n < BN; ++n) {
+        for (int n = 0; n < CB; ++n) {
           float y = bf16_rn(tot[n]);
-          if (scaled) y = bf16_rn(y * rowv[n]);
-          ost[n * 136 + r] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
+          if (scaled) y = bf16_rn(y * rowv[n0 + n]);
+          ost[(n0 + n) * 136 + r] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
         }
-        named_bar_sync(1, 128);
-        for (int i = te; i < BN * 16; i += 128) {
+        named_bar_sync(1, kEpi);
+        for (int i = te; i < BN * 16; i += kEpi) {
           const int n = i >> 4, c8 = (i & 15) * 8;
           if (n < tl.nrows && tl.ft * 128 + c8 < p.n_feat)
             *reinterpret_cast<uint4*>(p.out + (long long)(tl.row0 + n) * p.ldo + tl.ft * 128 + c8) =
@@ -348,10 +403,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace w8
 
-// Shared memory of one CTA for token tile bn: ns stages of (8 KB weights +
-// bn x 64 B token rows), the epilogue buffers, barriers and the tile prefix.
+// Shared memory of one CTA for token tile bn: the epilogue buffers (combined
+// scales 2 KB, routing weights 512 B, up values and the output tile).
 uint32_t w8a8_epilogue_bytes(int bn, int gated) {
-  return 2048u + static_cast<uint32_t>(bn) * (gated ? 64u * 4u + 72u * 2u : 136u * 2u);
+  return 4096u + static_cast<uint32_t>(bn) * (gated ? 64u * 4u + 72u * 2u : 136u * 2u);
+}
+
+int w8a8_tmem_buffers(int bn) {
+  return bn <= 64 ? 4 : 2;
 }
 
 const void* w8a8_kernel_ptr(int bn) {
