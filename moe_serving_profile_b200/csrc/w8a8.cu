@@ -295,9 +295,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint16_t* ost = reinterpret_cast<uint16_t*>(ux + (p.gated ? BN * 64 : 0));
     const bool scaled = !p.gated && p.row_w != nullptr;
     int gc = 0;
+    // scales of group g are loaded one group ahead (the next tile's first
+    // group during the current tile's last), off the critical path
+    GroupScales nxt{};
+    Tile tl{};
+    if (blockIdx.x < total) {
+      tl = decode_tile<BN>(blockIdx.x, prefix, p);
+      if (te < BN)
+        nxt = load_scales(p, p.wblob + (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb * p.blob_bytes, tl, te,
+                          0);
+    }
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const Tile tl = decode_tile<BN>(t, prefix, p);
       const uint8_t* wb = p.wblob + (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb * p.blob_bytes;
+      const bool more = t + static_cast<int>(gridDim.x) < total;
+      Tile tn{};
+      if (more) tn = decode_tile<BN>(t + gridDim.x, prefix, p);
       if (scaled && te < tl.nrows) {
         const int src = p.row_src[tl.row0 + te];
         rowv[te] = p.row_w_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.row_w)[src])
@@ -307,49 +319,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int n = 0; n < CB; ++n) tot[n] = 0.f;
       bool ok = true;
-      // scales of group g are loaded one group ahead, off the critical path
-      GroupScales nxt{};
-      if (te < BN) nxt = load_scales(p, wb, tl, te, 0);
       for (int g = 0; g < p.ngroups; ++g, ++gc) {
         const int buf = gc % NB;
         float* sc = sc_s + (gc & 1) * 256;
         if (te < BN) {
           sc[te] = nxt.q * nxt.w0;
           sc[128 + te] = nxt.q * nxt.w1;
-          if (g + 1 < p.ngroups) nxt = load_scales(p, wb, tl, te, g + 1);
+          if (g + 1 < p.ngroups)
+            nxt = load_scales(p, wb, tl, te, g + 1);
+          else if (more)
+            nxt = load_scales(p, p.wblob + (long long)(tn.e * p.feat_tiles + tn.ft) * p.nkb * p.blob_bytes, tn,
+                              te, 0);
         }
         // publishes sc and lets the eight warps agree on success
         ok = named_bar_and(1, kEpi, wait_bounded(&acc_full[buf], (gc / NB) & 1, p.status, 64));
         if (!ok) break;
         tc_fence_after();
         const float4* s4 = reinterpret_cast<const float4*>(sc + half * 128 + n0);
+        // all of the group's TMEM loads are issued before one wait
+        uint32_t v[CB];
+        const uint32_t ta = tq + static_cast<uint32_t>(buf * BN + n0);
         if constexpr (CB % 16 == 0) {
 #pragma unroll
-          for (int c0 = 0; c0 < CB; c0 += 16) {
-            uint32_t v[16];
-            tmem_ld16(tq + static_cast<uint32_t>(buf * BN + n0 + c0), v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 s = s4[(c0 + j) >> 2];
-              tot[c0 + j] = fmaf(__uint_as_float(v[j]), s.x, tot[c0 + j]);
-              tot[c0 + j + 1] = fmaf(__uint_as_float(v[j + 1]), s.y, tot[c0 + j + 1]);
-              tot[c0 + j + 2] = fmaf(__uint_as_float(v[j + 2]), s.z, tot[c0 + j + 2]);
-              tot[c0 + j + 3] = fmaf(__uint_as_float(v[j + 3]), s.w, tot[c0 + j + 3]);
-            }
-          }
+          for (int c0 = 0; c0 < CB; c0 += 16)
+            tmem_ld16(ta + static_cast<uint32_t>(c0), *reinterpret_cast<uint32_t(*)[16]>(&v[c0]));
         } else {
-          uint32_t v[8];
-          tmem_ld8(tq + static_cast<uint32_t>(buf * BN + n0), v);
-          tmem_ld_wait();
+          tmem_ld8(ta, *reinterpret_cast<uint32_t(*)[8]>(&v[0]));
+        }
+        tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 8; j += 4) {
-            const float4 s = s4[j >> 2];
-            tot[j] = fmaf(__uint_as_float(v[j]), s.x, tot[j]);
-            tot[j + 1] = fmaf(__uint_as_float(v[j + 1]), s.y, tot[j + 1]);
-            tot[j + 2] = fmaf(__uint_as_float(v[j + 2]), s.z, tot[j + 2]);
-            tot[j + 3] = fmaf(__uint_as_float(v[j + 3]), s.w, tot[j + 3]);
-          }
+        for (int j = 0; j < CB; j += 4) {
+          const float4 s = s4[j >> 2];
+          tot[j] = fmaf(__uint_as_float(v[j]), s.x, tot[j]);
+          tot[j + 1] = fmaf(__uint_as_float(v[j + 1]), s.y, tot[j + 1]);
+          tot[j + 2] = fmaf(__uint_as_float(v[j + 2]), s.z, tot[j + 2]);
+          tot[j + 3] = fmaf(__uint_as_float(v[j + 3]), s.w, tot[j + 3]);
         }
         tc_fence_before();
         __syncwarp();
@@ -391,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<const uint4*>(ost + n * 136 + c8);
         }
       }
+      tl = tn;
     }
   }
   tc_fence_before();
