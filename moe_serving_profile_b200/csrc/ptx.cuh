@@ -209,6 +209,16 @@ B200_DEVI void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
                "r"(src_bytes)
                : "memory");
 }
+// 4- and 8-byte async copies global->shared (through L1); src_bytes == 0
+// zero-fills the destination.
+B200_DEVI void cp_async_4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+B200_DEVI void cp_async_8(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
 B200_DEVI void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 B200_DEVI void cp_async_wait() {

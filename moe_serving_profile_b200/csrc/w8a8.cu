@@ -127,21 +127,20 @@ __device__ __forceinline__ float swiglu_bf16(float g, float u) {
   return bf16_rn(bf16_rn(gb / (1.f + expf(-gb))) * ub);
 }
 
-// The promotion scales of one 128-column group: token scale qs[row, g] of
-// the tile's row `te` (0 past the tile's rows) and the weight block scales
-// of rows 0-63 and 64-127 (the blob of k-block 2g).
-struct GroupScales {
-  float q, w0, w1;
-};
+// Promotion scales of one 128-column group, staged per thread through a
+// 4-slot shared-memory ring by cp.async (issued 4 groups ahead): slot
+// [0, 128) token scales qs[row0 + te, g] (0 past the tile's rows),
+// [128, 384) the weight block scales of rows 0-63 and 64-127 (the blob of
+// k-block 2g), two per thread.
+constexpr int kScaleRing = 4;
+constexpr int kRingSlot = 384;   // floats
 
-__device__ __forceinline__ GroupScales load_scales(const W8A8Params& p, const uint8_t* wb, const Tile& tl,
-                                                   int te, int g) {
-  GroupScales s;
-  s.q = te < tl.nrows ? __ldg(p.qs + (long long)(tl.row0 + te) * p.qs_groups + g) : 0.f;
-  const float2 w = __ldg(reinterpret_cast<const float2*>(wb + (long long)(2 * g) * p.blob_bytes + kAStage));
-  s.w0 = w.x;
-  s.w1 = w.y;
-  return s;
+__device__ __forceinline__ void issue_scales(const W8A8Params& p, const uint8_t* wb, const Tile& tl, int te,
+                                             int g, float* ring) {
+  float* slot = ring + (g % kScaleRing) * kRingSlot;
+  cp_async_4(smem_u32(slot + te), p.qs + (long long)(tl.row0 + (te < tl.nrows ? te : 0)) * p.qs_groups + g,
+             te < tl.nrows ? 4u : 0u);
+  cp_async_8(smem_u32(slot + 128 + 2 * te), wb + (long long)(2 * g) * p.blob_bytes + kAStage, 8u);
 }
 
 template <int BN>
@@ -291,25 +290,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
     float* sc_s = reinterpret_cast<float*>(sbase + p.x_off);   // [2 slots][2 halves][128] combined scales
     float* rowv = sc_s + 512;                                   // [128] routing weights
-    float* ux = rowv + 128;                                     // gated: [BN][64] up values
+    float* ring = rowv + 128;                                   // [kScaleRing][kRingSlot] staged scales
+    float* ux = ring + kScaleRing * kRingSlot;                  // gated: [BN][64] up values
     uint16_t* ost = reinterpret_cast<uint16_t*>(ux + (p.gated ? BN * 64 : 0));
     const bool scaled = !p.gated && p.row_w != nullptr;
     int gc = 0;
-    // scales of group g are loaded one group ahead (the next tile's first
-    // group during the current tile's last), off the critical path
-    GroupScales nxt{};
-    Tile tl{};
-    if (blockIdx.x < total) {
-      tl = decode_tile<BN>(blockIdx.x, prefix, p);
-      if (te < BN)
-        nxt = load_scales(p, p.wblob + (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb * p.blob_bytes, tl, te,
-                          0);
-    }
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile tl = decode_tile<BN>(t, prefix, p);
       const uint8_t* wb = p.wblob + (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb * p.blob_bytes;
-      const bool more = t + static_cast<int>(gridDim.x) < total;
-      Tile tn{};
-      if (more) tn = decode_tile<BN>(t + gridDim.x, prefix, p);
+      if (te < BN) {
+#pragma unroll
+        for (int i = 0; i < kScaleRing; ++i) {
+          if (i < p.ngroups) issue_scales(p, wb, tl, te, i, ring);
+          cp_async_commit();
+        }
+      }
       if (scaled && te < tl.nrows) {
         const int src = p.row_src[tl.row0 + te];
         rowv[te] = p.row_w_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.row_w)[src])
@@ -323,13 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = gc % NB;
         float* sc = sc_s + (gc & 1) * 256;
         if (te < BN) {
-          sc[te] = nxt.q * nxt.w0;
-          sc[128 + te] = nxt.q * nxt.w1;
-          if (g + 1 < p.ngroups)
-            nxt = load_scales(p, wb, tl, te, g + 1);
-          else if (more)
-            nxt = load_scales(p, p.wblob + (long long)(tn.e * p.feat_tiles + tn.ft) * p.nkb * p.blob_bytes, tn,
-                              te, 0);
+          cp_async_wait<kScaleRing - 1>();   // group g's scales have landed
+          const float* slot = ring + (g % kScaleRing) * kRingSlot;
+          const float qv = slot[te];
+          sc[te] = qv * slot[128 + 2 * te];
+          sc[128 + te] = qv * slot[129 + 2 * te];
+          if (g + kScaleRing < p.ngroups) issue_scales(p, wb, tl, te, g + kScaleRing, ring);
+          cp_async_commit();
         }
         // publishes sc and lets the eight warps agree on success
         ok = named_bar_and(1, kEpi, wait_bounded(&acc_full[buf], (gc / NB) & 1, p.status, 64));
@@ -395,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<const uint4*>(ost + n * 136 + c8);
         }
       }
-      tl = tn;
     }
+    cp_async_wait<0>();   // no scale copy is still landing when the CTA exits
   }
   tc_fence_before();
   __syncthreads();
@@ -409,9 +404,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace w8
 
 // Shared memory of one CTA for token tile bn: the epilogue buffers (combined
-// scales 2 KB, routing weights 512 B, up values and the output tile).
+// scales 2 KB, routing weights 512 B, the scale ring 6 KB, up values and the
+// output tile).
 uint32_t w8a8_epilogue_bytes(int bn, int gated) {
-  return 4096u + static_cast<uint32_t>(bn) * (gated ? 64u * 4u + 72u * 2u : 136u * 2u);
+  return 8704u + static_cast<uint32_t>(bn) * (gated ? 64u * 4u + 72u * 2u : 136u * 2u);
 }
 
 int w8a8_tmem_buffers(int bn) {
