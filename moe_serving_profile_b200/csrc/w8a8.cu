@@ -80,11 +80,11 @@ constexpr int kThreads = kW8A8Threads;   // warp 0 copies, warp 1 MMA, warps 2-9
 constexpr int kEpi = kThreads - 64;      // promotion / epilogue threads
 constexpr uint32_t kAStage = 8192;       // 128 weight rows x 64 e4m3
 
-// Group accumulators in tensor memory: 4 for token tiles up to 64 rows, so
-// the MMAs run up to three groups ahead of the promotion; 2 for 128.
+// Group accumulators in tensor memory: 4 (512 columns at 128-row tiles), so
+// the MMAs run up to three groups ahead of the promotion.
 template <int BN>
 __host__ __device__ constexpr int tmem_bufs() {
-  return BN <= 64 ? 4 : 2;
+  return 4;
 }
 
 struct Tile {
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* wb = p.wblob + (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb * p.blob_bytes;
         for (int kb = 0; kb < p.nkb; ++kb, ring.next(), ++issued) {
           const int s = ring.idx;
-          if (!wait_bounded(&empty[s], ring.phase ^ 1u, p.status, 32)) {
+          if (!wait_bounded(&empty[s], ring.phase ^ 1u, p.status)) {
             ok = false;
             break;
           }
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int kb_end = min(2 * g + 2, p.nkb);
           for (int kb = 2 * g; kb < kb_end; ++kb, ring.next()) {
             const int s = ring.idx;
-            if (!wait_spin(&full[s], ring.phase, p.status)) {
+            if (!wait_bounded(&full[s], ring.phase, p.status)) {
               ok = false;
               break;
             }
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           cp_async_commit();
         }
         // publishes sc and lets the eight warps agree on success
-        ok = named_bar_and(1, kEpi, wait_bounded(&acc_full[buf], (gc / NB) & 1, p.status, 64));
+        ok = named_bar_and(1, kEpi, wait_bounded(&acc_full[buf], (gc / NB) & 1, p.status));
         if (!ok) break;
         tc_fence_after();
         const float4* s4 = reinterpret_cast<const float4*>(sc + half * 128 + n0);
@@ -411,7 +411,7 @@ uint32_t w8a8_epilogue_bytes(int bn, int gated) {
 }
 
 int w8a8_tmem_buffers(int bn) {
-  return bn <= 64 ? 4 : 2;
+  return 4;
 }
 
 const void* w8a8_kernel_ptr(int bn) {
