@@ -521,10 +521,10 @@ int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* a, cons
   p.out = static_cast<__nv_bfloat16*>(a->out);
   p.ldo = a->ldo;
   p.status = sp;
-  // shared memory: stages of (8 KB weights + bn x 64 B token rows) on 1024-byte
-  // boundaries, the epilogue buffers, barriers + tile prefix
+  // shared memory: stages of (two 8 KB weight blobs + bn x 128 B token rows) on
+  // 1024-byte boundaries, the epilogue buffers, barriers + tile prefix
   const uint32_t budget = 232448u - 2048u;
-  p.stage_bytes = (8192u + static_cast<uint32_t>(bn) * 64u + 1023u) & ~1023u;
+  p.stage_bytes = (16384u + static_cast<uint32_t>(bn) * 128u + 1023u) & ~1023u;   // one 128-column group
   const uint32_t xbytes = (b200::w8a8_epilogue_bytes(bn, p.gated) + 1023u) & ~1023u;
   const uint32_t nbuf = static_cast<uint32_t>(b200::w8a8_tmem_buffers(bn));
   // full/empty per stage, acc_full/acc_empty per TMEM buffer, mma_done; tmem
@@ -544,10 +544,10 @@ int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* a, cons
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->k_pad), static_cast<cuuint64_t>(a->b_rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a->k_pad)};
-    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(bn)};
+    const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(bn)};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "activation tensor map failed (%d)", (int)cr);
   }

@@ -15,7 +15,8 @@
 // exact-product fp32 MMA accumulation in tensor memory, the outer sum
 // ("promotion") in fp32 registers of the epilogue warps. Weights come
 // straight from the packed FP8 blobs (their rows already sit in the 64-byte
-// swizzled operand layout), token rows by a 64-byte-swizzled TMA box.
+// swizzled operand layout), a 128-column group of token rows by one
+// 128-byte-swizzled TMA box.
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -207,7 +208,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   const int total = *s_total;
-  constexpr uint32_t kBStage = BN * 64;
+  // One stage per 128-column group: the weight blobs of k-blocks 2g and
+  // 2g + 1 (64-byte-swizzled rows, 8 KB each) and the group's token rows as
+  // one 128-byte-swizzled TMA box of BN rows x 128 B.
+  constexpr uint32_t kBStage = BN * 128;
+  constexpr uint32_t kBOff = 2 * kAStage;
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -218,16 +223,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         const Tile tl = decode_tile<BN>(t, prefix, p);
         const uint8_t* wb = p.wblob + (long long)(tl.e * p.feat_tiles + tl.ft) * p.nkb * p.blob_bytes;
-        for (int kb = 0; kb < p.nkb; ++kb, ring.next(), ++issued) {
+        for (int g = 0; g < p.ngroups; ++g, ring.next(), ++issued) {
           const int s = ring.idx;
           if (!wait_bounded(&empty[s], ring.phase ^ 1u, p.status)) {
             ok = false;
             break;
           }
+          const int nblobs = min(2, p.nkb - 2 * g);
           uint8_t* st = sbase + s * p.stage_bytes;
-          mbar_arrive_expect_tx(&full[s], kAStage + kBStage);
-          bulk_load(st, wb + (long long)kb * p.blob_bytes, kAStage, &full[s]);
-          tma_load_2d(st + kAStage, &qmap, &full[s], kb * 64, tl.row0);
+          mbar_arrive_expect_tx(&full[s], nblobs * kAStage + kBStage);
+          for (int b = 0; b < nblobs; ++b)
+            bulk_load(st + b * kAStage, wb + (long long)(2 * g + b) * p.blob_bytes, kAStage, &full[s]);
+          tma_load_2d(st + kBOff, &qmap, &full[s], g * 128, tl.row0);
         }
       }
       // every issued copy has landed before the CTA may exit
@@ -236,38 +243,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
-    // Group g of a tile (k-blocks 2g, 2g + 1) accumulates into buffer
-    // gc % NB (gc counts the CTA's groups), which the promotion warps drain.
+    // Group g of a tile (one stage) accumulates into buffer gc % NB (gc
+    // counts the CTA's groups), which the promotion warps drain.
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
       Ring ring(p.ns);
       int gc = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        for (int g = 0; ok && g < p.ngroups; ++g, ++gc) {
+        for (int g = 0; g < p.ngroups; ++g, ++gc, ring.next()) {
           const int buf = gc % NB;
-          if (!wait_bounded(&acc_empty[buf], ((gc / NB) & 1) ^ 1, p.status)) {
+          const int s = ring.idx;
+          if (!wait_bounded(&acc_empty[buf], ((gc / NB) & 1) ^ 1, p.status) ||
+              !wait_bounded(&full[s], ring.phase, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
-          const int kb_end = min(2 * g + 2, p.nkb);
-          for (int kb = 2 * g; kb < kb_end; ++kb, ring.next()) {
-            const int s = ring.idx;
-            if (!wait_bounded(&full[s], ring.phase, p.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t st = base_u32 + s * p.stage_bytes;
-            const uint64_t adesc = sdesc_k_sw64(st);
-            const uint64_t bdesc = sdesc_k_sw64(st + kAStage);
-            umma_e4m3(d, adesc, bdesc, idesc, kb > 2 * g ? 1u : 0u);
-            umma_e4m3(d, adesc + 2, bdesc + 2, idesc, 1u);
-            umma_commit(&empty[s]);
-          }
-          if (!ok) break;
+          const uint32_t st = base_u32 + s * p.stage_bytes;
+          const uint64_t bdesc = sdesc_k_sw128(st + kBOff);
+          const int nk = 2 * min(2, p.nkb - 2 * g);   // K = 32 slices of this group
+#pragma unroll 1
+          for (int j = 0; j < nk; ++j)
+            umma_e4m3(d, sdesc_k_sw64(st + (j >> 1) * kAStage) + 2 * (j & 1), bdesc + 2 * j, idesc,
+                      j > 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
           umma_commit(&acc_full[buf]);
         }
       }
