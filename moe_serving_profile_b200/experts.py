@@ -28,13 +28,15 @@ def _sm_count(device: int) -> int:
     return torch.cuda.get_device_properties(device).multi_processor_count
 
 
-def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256) -> int:
+def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256, cover: float = 1.5) -> int:
     """Token tile (the MMA N) for one grouped GEMM launch: the smallest power
-    of two in [16, max_tile] covering 1.5x the mean rows per expert, so that
-    one tile usually holds an expert's rows (a second, nearly empty tile costs
-    a whole tile's k-block loop: 512 tokens with 32-token tiles took 2.3x
-    the time of 64-token tiles on B200)."""
-    rows = 1.5 * T * K / num_experts
+    of two in [16, max_tile] covering ``cover`` x the mean rows per expert, so
+    that one tile usually holds an expert's rows (a second, nearly empty tile
+    costs a whole tile's k-block loop: 512 tokens with 32-token tiles took
+    2.3x the time of 64-token tiles on B200). The W8A8 GEMM, whose per-group
+    cost grows with the tile, uses cover 1.0 (512 tokens: 32-token tiles
+    160 us, 64-token tiles 174 us)."""
+    rows = cover * T * K / num_experts
     bn = 16
     while bn < max_tile and bn < rows:
         bn *= 2
@@ -128,7 +130,7 @@ def run_experts_w8a8(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutati
         raise ValueError(f"hidden size {H} does not match the experts' {w.hidden}")
     R = perm.perm_src.numel()
     dev = hidden.device
-    bn = tile_policy(T, K, num_experts, 128)
+    bn = tile_policy(T, K, num_experts, 128, cover=1.0)
     div = K if b_map_div is None else b_map_div
     q, qs = ops.act_quant_fp8(hidden, k_pad=w.h_k, rows_src=perm.perm_src, src_div=div)
     act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16)

@@ -113,6 +113,13 @@ def test_tile_policy(T, K, E, bn):
     assert tile_policy(T, K, E, 160) == min(bn, 160)
 
 
+@pytest.mark.parametrize("T,bn", [(1, 16), (64, 16), (512, 32), (4096, 128), (16384, 128)])
+def test_w8a8_tile_policy(T, bn):
+    """The W8A8 launch covers 1.0x the mean rows per expert, capped at 128
+    (Qwen3-30B-A3B: top-8 of 128 experts)."""
+    assert tile_policy(T, 8, 128, 128, cover=1.0) == bn
+
+
 def test_fp8_layout_pads_with_zeros():
     E, I, H = 2, 136, 200
     g = torch.Generator().manual_seed(0)
