@@ -105,6 +105,42 @@ def test_wrappers_refuse_cpu_tensors():
         ops.gather_rows(torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(4, dtype=torch.int32), 1)
 
 
+def test_w8a8_paths_refuse_before_device_work():
+    """The efficient (W8A8) path checks its inputs on the host: CPU tensors,
+    a q that is not e4m3 of the padded width, and non-FP8 expert weights are
+    refused before anything is enqueued."""
+    from types import SimpleNamespace
+
+    from moe_serving_profile_b200 import experts as X
+    from moe_serving_profile_b200 import qwen3
+    from moe_serving_profile_b200.parallel import ParallelGroup
+
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.act_quant_fp8(torch.zeros(4, 128, dtype=torch.bfloat16))
+    kw = dict(offsets=torch.zeros(9, dtype=torch.int32), expert_begin=0, n_experts=8, max_rows=8, planes=2,
+              feat_pad=128, n_feat=128, k_pad=256, weight=torch.zeros(16, dtype=torch.uint8),
+              q=torch.zeros(8, 256, dtype=torch.float8_e4m3fn), q_scale=torch.zeros(8, 2),
+              epilogue=_lib.EPI_SWIGLU, out=torch.zeros(8, 128, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.w8a8_gemm(**kw)
+    g, u, d = (torch.zeros(2, 128, 256, dtype=torch.bfloat16), torch.zeros(2, 128, 256, dtype=torch.bfloat16),
+               torch.zeros(2, 256, 128, dtype=torch.bfloat16))
+    w = layout.bf16_experts(g, u, d)
+    perm = ops.Permutation(*(torch.zeros(n, dtype=torch.int32) for n in (2, 3, 8, 8)))
+    with pytest.raises(ValueError, match="FP8"):
+        X.run_experts_w8a8(w, torch.zeros(4, 256, dtype=torch.bfloat16), perm, None, K=2, num_experts=2,
+                           expert_begin=0)
+    m = qwen3.ParallelExperts(SimpleNamespace(num_experts=2, hidden_act="silu"), ParallelGroup(1), "efficient")
+    for e, mods in enumerate(m.local):
+        mods["gate_proj"] = qwen3.ExpertProjection(g[e])
+        mods["up_proj"] = qwen3.ExpertProjection(u[e])
+        mods["down_proj"] = qwen3.ExpertProjection(d[e])
+    with pytest.raises(ValueError, match="block FP8"):
+        m.prepare()
+    with pytest.raises(ValueError):
+        qwen3.ParallelExperts(SimpleNamespace(num_experts=2, hidden_act="silu"), ParallelGroup(1), "exact")
+
+
 @pytest.mark.parametrize("T,K,E,bn", [(1, 8, 128, 16), (64, 8, 128, 16), (512, 8, 128, 64),
                                       (4096, 8, 128, 256), (2048, 4, 32, 256), (16, 4, 32, 16),
                                       (64, 4, 32, 16), (256, 8, 128, 32), (1024, 8, 128, 128)])
