@@ -292,8 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* sc_s = reinterpret_cast<float*>(sbase + p.x_off);   // [2 slots][2 halves][128] combined scales
     float* rowv = sc_s + 512;                                   // [128] routing weights
     float* ring = rowv + 128;                                   // [kScaleRing][kRingSlot] staged scales
-    float* ux = ring + kScaleRing * kRingSlot;                  // gated: [BN][64] up values
-    uint16_t* ost = reinterpret_cast<uint16_t*>(ux + (p.gated ? BN * 64 : 0));
+    uint16_t* ux16 = reinterpret_cast<uint16_t*>(ring + kScaleRing * kRingSlot);   // gated: [BN][64] bf16 up values
     const bool scaled = !p.gated && p.row_w != nullptr;
     int gc = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -356,40 +355,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
       }
       if (!ok) break;
+      // Outputs go straight from registers: thread r writes feature r of its
+      // token columns, a warp 32 consecutive bf16 (64 B) per token row.
+      uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
       if (p.gated) {
+        // up rows (64..127) hand their bf16 values to the gate rows (0..63)
         if (half == 1) {
 #pragma unroll
-          for (int n = 0; n < CB; ++n) ux[(n0 + n) * 64 + (r - 64)] = tot[n];
-        }
-        named_bar_sync(1, kEpi);
-        if (half == 0) {
-#pragma unroll
           for (int n = 0; n < CB; ++n)
-            ost[(n0 + n) * 72 + r] =
-                static_cast<uint16_t>(__float_as_uint(swiglu_bf16(tot[n], ux[(n0 + n) * 64 + r])) >> 16);
+            ux16[(n0 + n) * 64 + (r - 64)] = static_cast<uint16_t>(__float_as_uint(bf16_rn(tot[n])) >> 16);
         }
         named_bar_sync(1, kEpi);
-        for (int i = te; i < BN * 8; i += kEpi) {
-          const int n = i >> 3, c8 = (i & 7) * 8;
-          if (n < tl.nrows && tl.ft * 64 + c8 < p.n_feat)
-            *reinterpret_cast<uint4*>(p.out + (long long)(tl.row0 + n) * p.ldo + tl.ft * 64 + c8) =
-                *reinterpret_cast<const uint4*>(ost + n * 72 + c8);
+        if (half == 0 && tl.ft * 64 + r < p.n_feat) {
+#pragma unroll
+          for (int n = 0; n < CB; ++n) {
+            if (n0 + n < tl.nrows) {
+              const float u = __uint_as_float(static_cast<uint32_t>(ux16[(n0 + n) * 64 + r]) << 16);
+              out16[(long long)(tl.row0 + n0 + n) * p.ldo + tl.ft * 64 + r] =
+                  static_cast<uint16_t>(__float_as_uint(swiglu_bf16(tot[n], u)) >> 16);
+            }
+          }
         }
+        // ux16 is next written after the next tile's group barriers
       } else {
         // rowv (written before the group barriers) is visible here
+        if (tl.ft * 128 + r < p.n_feat) {
 #pragma unroll
-        for (int n = 0; n < CB; ++n) {
-          float y = bf16_rn(tot[n]);
-          if (scaled) y = bf16_rn(y * rowv[n0 + n]);
-          ost[(n0 + n) * 136 + r] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
+          for (int n = 0; n < CB; ++n) {
+            if (n0 + n < tl.nrows) {
+              float y = bf16_rn(tot[n]);
+              if (scaled) y = bf16_rn(y * rowv[n0 + n]);
+              out16[(long long)(tl.row0 + n0 + n) * p.ldo + tl.ft * 128 + r] =
+                  static_cast<uint16_t>(__float_as_uint(y) >> 16);
+            }
+          }
         }
-        named_bar_sync(1, kEpi);
-        for (int i = te; i < BN * 16; i += kEpi) {
-          const int n = i >> 4, c8 = (i & 15) * 8;
-          if (n < tl.nrows && tl.ft * 128 + c8 < p.n_feat)
-            *reinterpret_cast<uint4*>(p.out + (long long)(tl.row0 + n) * p.ldo + tl.ft * 128 + c8) =
-                *reinterpret_cast<const uint4*>(ost + n * 136 + c8);
-        }
+        named_bar_sync(1, kEpi);   // every rowv read is done before the next tile rewrites it
       }
     }
     cp_async_wait<0>();   // no scale copy is still landing when the CTA exits
@@ -405,10 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace w8
 
 // Shared memory of one CTA for token tile bn: the epilogue buffers (combined
-// scales 2 KB, routing weights 512 B, the scale ring 6 KB, up values and the
-// output tile).
+// scales 2 KB, routing weights 512 B, the scale ring 6 KB and, for gated
+// tiles, the bf16 up values).
 uint32_t w8a8_epilogue_bytes(int bn, int gated) {
-  return 8704u + static_cast<uint32_t>(bn) * (gated ? 64u * 4u + 72u * 2u : 136u * 2u);
+  return 8704u + (gated ? static_cast<uint32_t>(bn) * 128u : 0u);
 }
 
 int w8a8_tmem_buffers(int bn) {
