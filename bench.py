@@ -214,7 +214,7 @@ def w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst):
         kw = dict(offsets=perm.offsets, expert_begin=0, n_experts=packed.n_experts, max_rows=R, planes=2,
                   feat_pad=packed.i_pad, n_feat=packed.inter, k_pad=packed.h_k, weight=packed.w1,
                   fp8_block=packed.block, q=q, q_scale=qs, epilogue=_lib.EPI_SWIGLU, out=act,
-                  token_tile=X.tile_policy(Tm, cfg.top_k, cfg.experts, 128, cover=1.0))
+                  token_tile=X.tile_policy(Tm, cfg.top_k, cfg.experts, 128))
         for _ in range(3):
             ops.w8a8_gemm(**kw)
         kms = 0.0

@@ -33,9 +33,8 @@ def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256, cover: fl
     of two in [16, max_tile] covering ``cover`` x the mean rows per expert, so
     that one tile usually holds an expert's rows (a second, nearly empty tile
     costs a whole tile's k-block loop: 512 tokens with 32-token tiles took
-    2.3x the time of 64-token tiles on B200). The W8A8 GEMM, whose per-group
-    cost grows with the tile, uses cover 1.0 (512 tokens: 32-token tiles
-    160 us, 64-token tiles 174 us)."""
+    2.3x the time of 64-token tiles on B200; the W8A8 gate/up GEMM at 512
+    tokens: 64-token tiles 138 us, 32-token tiles 150 us)."""
     rows = cover * T * K / num_experts
     bn = 16
     while bn < max_tile and bn < rows:
@@ -130,7 +129,7 @@ def run_experts_w8a8(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutati
         raise ValueError(f"hidden size {H} does not match the experts' {w.hidden}")
     R = perm.perm_src.numel()
     dev = hidden.device
-    bn = tile_policy(T, K, num_experts, 128, cover=1.0)
+    bn = tile_policy(T, K, num_experts, 128)
     div = K if b_map_div is None else b_map_div
     q, qs = ops.act_quant_fp8(hidden, k_pad=w.h_k, rows_src=perm.perm_src, src_div=div)
     act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16)

@@ -149,11 +149,13 @@ def test_tile_policy(T, K, E, bn):
     assert tile_policy(T, K, E, 160) == min(bn, 160)
 
 
-@pytest.mark.parametrize("T,bn", [(1, 16), (64, 16), (512, 32), (4096, 128), (16384, 128)])
+@pytest.mark.parametrize("T,bn", [(1, 16), (64, 16), (512, 64), (4096, 128), (16384, 128)])
 def test_w8a8_tile_policy(T, bn):
-    """The W8A8 launch covers 1.0x the mean rows per expert, capped at 128
-    (Qwen3-30B-A3B: top-8 of 128 experts)."""
-    assert tile_policy(T, 8, 128, 128, cover=1.0) == bn
+    """The W8A8 launch caps the tile at 128 rows (four 128-column TMEM group
+    buffers fill the 512 columns); Qwen3-30B-A3B: top-8 of 128 experts. A
+    smaller cover picks smaller tiles."""
+    assert tile_policy(T, 8, 128, 128) == bn
+    assert tile_policy(512, 8, 128, 128, cover=1.0) == 32
 
 
 def test_fp8_layout_pads_with_zeros():
