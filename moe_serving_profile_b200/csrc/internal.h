@@ -43,7 +43,7 @@ struct W8A8Params {
 };
 constexpr int kW8A8Threads = 320;   // copy warp, MMA warp, 8 promotion + epilogue warps
 uint32_t w8a8_epilogue_bytes(int bn, int gated);
-int w8a8_tmem_buffers(int bn);      // group accumulators in tensor memory (ping-pong or 4-deep)
+int w8a8_tmem_buffers(int bn);      // group accumulators in tensor memory (4: the MMAs run 3 groups ahead)
 const void* w8a8_kernel_ptr(int bn);   // token tile 16, 32, 64 or 128; else NULL
 
 size_t permute_workspace_bytes(int T, int K, int E);

@@ -83,10 +83,7 @@ constexpr uint32_t kAStage = 8192;       // 128 weight rows x 64 e4m3
 
 // Group accumulators in tensor memory: 4 (512 columns at 128-row tiles), so
 // the MMAs run up to three groups ahead of the promotion.
-template <int BN>
-__host__ __device__ constexpr int tmem_bufs() {
-  return 4;
-}
+constexpr int kTmemBufs = 4;
 
 struct Tile {
   int e, ft, row0, nrows;
@@ -153,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sbase = smem_raw + (base_u32 - raw_u32);
   if (*reinterpret_cast<volatile int*>(p.status) & kStatusWaitTimeout) return;
 
-  constexpr int NB = tmem_bufs<BN>();
+  constexpr int NB = kTmemBufs;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(sbase + p.bar_off);
@@ -412,8 +409,8 @@ uint32_t w8a8_epilogue_bytes(int bn, int gated) {
   return 8704u + (gated ? static_cast<uint32_t>(bn) * 128u : 0u);
 }
 
-int w8a8_tmem_buffers(int bn) {
-  return 4;
+int w8a8_tmem_buffers(int) {
+  return w8::kTmemBufs;
 }
 
 const void* w8a8_kernel_ptr(int bn) {
