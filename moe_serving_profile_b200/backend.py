@@ -39,10 +39,8 @@ def backend_metadata(family: str, numerics: str) -> dict:
     """Labels of the kernels one layer call runs (the reference's keys)."""
     if numerics not in NUMERICS:
         raise ValueError(f"numerics must be one of {NUMERICS}, got {numerics!r}")
-    if numerics == "efficient" and family == "gpt_oss":
-        raise NotImplementedError("b200 GPT-OSS experts run the weight-only MXFP4 path (reference, fast)")
     weights = "mxfp4_e2m1_ue8m0" if family == "gpt_oss" else "fp8_e4m3_block128"
-    kind = "w8a8_dynamic_act_128" if numerics == "efficient" else "weight_only"
+    kind = "w8a8_dynamic_act_128" if numerics == "efficient" and family == "qwen3" else "weight_only"
     return {
         "experts": f"b200_tcgen05_grouped_{weights}_{kind}",
         "router": "b200_fused_router",

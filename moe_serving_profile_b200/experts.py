@@ -174,8 +174,10 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     EP size, the contract of moe_serving/parallel_numerics.py:13-36).
     numerics "fast": each rank combines its own experts and the partial sums
     are all-reduced (moe_serving/qwen3_parallel.py:105-118).
-    numerics "efficient" (FP8 weights): the W8A8 experts of the reference's
-    grouped_fp8 (moe_serving/efficient_kernels.py:243-274), combined like "fast".
+    numerics "efficient": FP8 weights run the W8A8 experts of the reference's
+    grouped_fp8 (moe_serving/efficient_kernels.py:243-274), other formats the
+    weight-only experts (grouped_mxfp4's bf16 x upcast MXFP4, :157-206);
+    combined like "fast".
     """
     hidden, indices, weights = check_inputs(hidden, indices, weights)
     T, K = indices.shape
@@ -184,10 +186,13 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     perm = ops.permute(indices, num_experts)
     size = 1 if parallel is None else parallel.size
     if numerics == "efficient":
-        # W8A8 experts; the rank-local partial sums are all-reduced, the
-        # reference's efficient EP exchange (efficient_kernels.py:274)
-        contrib = run_experts_w8a8(w, hidden, perm, weights, K=K, num_experts=num_experts,
-                                   expert_begin=expert_begin)
+        # FP8: W8A8 experts (grouped_fp8). MXFP4 / BF16: the weight-only
+        # experts, as matmul_ogs multiplies bf16 activations with upcast
+        # MXFP4 weights (grouped_mxfp4, efficient_kernels.py:157-206). The
+        # rank-local partial sums are all-reduced, the reference's efficient
+        # EP exchange (efficient_kernels.py:206, 274).
+        run = run_experts_w8a8 if w.fmt == _lib.W_FP8 else run_experts
+        contrib = run(w, hidden, perm, weights, K=K, num_experts=num_experts, expert_begin=expert_begin)
         if size == 1:
             return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
         return parallel.combine_reduce(contrib, perm.inverse, indices, expert_begin,

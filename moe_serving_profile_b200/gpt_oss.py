@@ -24,7 +24,7 @@ from moe_serving_profile_b200 import experts as _experts
 from moe_serving_profile_b200 import layout
 from moe_serving_profile_b200.parallel import ParallelGroup
 
-NUMERICS = ("reference", "fast")
+NUMERICS = ("reference", "fast", "efficient")
 
 
 class ParallelExperts(nn.Module):
@@ -35,6 +35,8 @@ class ParallelExperts(nn.Module):
             raise ValueError(f"numerics must be one of {NUMERICS}, got {numerics!r}")
         if storage not in ("mxfp4", "bf16"):
             raise ValueError("expert_storage must be mxfp4 or bf16")
+        if numerics == "efficient" and storage != "mxfp4":
+            raise ValueError("efficient gpt_oss requires mxfp4 checkpoint storage")
         if config.num_local_experts % parallel.size:
             raise ValueError("Number of experts must be divisible by EP size")
         self.parallel, self.storage, self.numerics = parallel, storage, numerics

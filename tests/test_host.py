@@ -141,6 +141,33 @@ def test_w8a8_paths_refuse_before_device_work():
         qwen3.ParallelExperts(SimpleNamespace(num_experts=2, hidden_act="silu"), ParallelGroup(1), "exact")
 
 
+def test_efficient_numerics_dispatch(monkeypatch):
+    """numerics="efficient" runs the W8A8 experts for FP8 weights and the
+    weight-only experts for MXFP4 / BF16 (the reference's grouped_mxfp4
+    multiplies bf16 activations with upcast MXFP4 weights); GPT-OSS needs
+    MXFP4 storage for it, as the reference's check_runtime does."""
+    from types import SimpleNamespace
+
+    from moe_serving_profile_b200 import experts as X
+    from moe_serving_profile_b200 import gpt_oss
+    from moe_serving_profile_b200.parallel import ParallelGroup
+
+    calls = []
+    monkeypatch.setattr(X.ops, "permute", lambda idx, E: SimpleNamespace(inverse=None))
+    monkeypatch.setattr(X.ops, "combine", lambda contrib, inverse, idx, order: contrib)
+    monkeypatch.setattr(X, "run_experts", lambda *a, **k: calls.append("weight_only") or "rows")
+    monkeypatch.setattr(X, "run_experts_w8a8", lambda *a, **k: calls.append("w8a8") or "rows")
+    for fmt, want in ((_lib.W_FP8, "w8a8"), (_lib.W_MXFP4, "weight_only"), (_lib.W_BF16, "weight_only")):
+        out = X.layer_forward(SimpleNamespace(fmt=fmt, n_experts=4), torch.zeros(3, 64, dtype=torch.bfloat16),
+                              torch.zeros(3, 2, dtype=torch.int64), torch.zeros(3, 2), num_experts=4,
+                              expert_begin=0, numerics="efficient")
+        assert out == "rows" and calls[-1] == want
+    conf = SimpleNamespace(num_local_experts=4, swiglu_alpha=1.702, swiglu_limit=7.0)
+    gpt_oss.ParallelExperts(conf, ParallelGroup(1), "mxfp4", "efficient")
+    with pytest.raises(ValueError, match="mxfp4"):
+        gpt_oss.ParallelExperts(conf, ParallelGroup(1), "bf16", "efficient")
+
+
 @pytest.mark.parametrize("T,K,E,bn", [(1, 8, 128, 16), (64, 8, 128, 16), (512, 8, 128, 64),
                                       (4096, 8, 128, 256), (2048, 4, 32, 256), (16, 4, 32, 16),
                                       (64, 4, 32, 16), (256, 8, 128, 32), (1024, 8, 128, 128)])
@@ -248,8 +275,9 @@ def test_backend_checks_and_metadata():
     assert "mxfp4" in m["experts"] and "ordered" in m["expert_parallel"]
     assert "fp8" in backend.backend_metadata("qwen3", "fast")["experts"]
     assert "w8a8" in backend.backend_metadata("qwen3", "efficient")["experts"]
-    with pytest.raises(NotImplementedError):
-        backend.backend_metadata("gpt_oss", "efficient")
+    m = backend.backend_metadata("gpt_oss", "efficient")
+    assert "mxfp4" in m["experts"] and "weight_only" in m["experts"]
+    assert m["expert_parallel"] == "local_combine_then_all_reduce"
     with pytest.raises(ValueError):
         backend.backend_metadata("qwen3", "exact")
 
