@@ -15,6 +15,8 @@
  *   - the expert-contiguous permutation in (slot, token) order
  *     (moe_serving/parallel_numerics.py:21-26)
  *   - the ordered bf16 combine (parallel_numerics.py:26-35; moe.py:123-136)
+ *   - e4m3 encoding and the W8A8 per-(row, 128-column) activation
+ *     quantisation (efficient_kernels.py:243-274)
  * Compile with -ffp-contract=off so every float operation rounds as written.
  */
 #include <math.h>
@@ -225,4 +227,55 @@ void oracle_combine(const uint16_t* rows, long ld_rows, const int32_t* inverse,
   free(sel);
   free(key);
   free(acc);
+}
+
+/* fp32 -> e4m3fn code, round to nearest even, saturating to +-448 (the
+   largest finite value); NaN -> 0x7f. From the format: normal values
+   2^(e-7) * (1 + m/8) for exponent field e = 1..15 (e = 15, m = 7 is NaN),
+   subnormals 2^-6 * m/8. In each binade [2^p, 2^(p+1)) (p >= -6) the
+   representable values are 2^(p-3) apart, below 2^-6 they are 2^-9 apart, so
+   a value rounds to the nearest multiple of that quantum (ties to even). */
+uint8_t oracle_f32_to_e4m3(float f) {
+  const uint8_t sign = (f2u(f) >> 31) ? 0x80 : 0x00;
+  const float a = fabsf(f);
+  if (a != a) return 0x7f;
+  if (a >= 448.0f) return sign | 0x7e;
+  if (a == 0.0f) return sign;
+  int ex;
+  frexpf(a, &ex);                       /* a in [2^(ex-1), 2^ex) */
+  int p = ex - 1;
+  if (p < -6) p = -6;
+  const float step = ldexpf(1.0f, p - 3);
+  const float v = rintf(a / step) * step; /* exact scaling; rintf rounds half to even */
+  if (v == 0.0f) return sign;
+  frexpf(v, &ex);
+  p = ex - 1;                           /* v may have rounded up into the next binade */
+  if (p < -6) return sign | (uint8_t)(v / ldexpf(1.0f, -9));      /* subnormal: m = v / 2^-9 */
+  const int mant = (int)(v / ldexpf(1.0f, p - 3)) - 8;
+  return sign | (uint8_t)(((p + 7) << 3) | mant);
+}
+
+/* Dynamic FP8 activation quantisation of the W8A8 path (the activation side
+   of moe_serving/efficient_kernels.py:243-274): for row r and 128-column
+   group g, s[r,g] = amax / 448 over the group's bf16 values (1 if all are
+   zero) and q[r,c] = e4m3(x[src(r), c] / s[r,g]) for c < k_valid, 0 up to
+   k_pad. src(r) = map[r] / div, or r without a map. */
+void oracle_act_quant_fp8(const uint16_t* x, long ldx, const int32_t* map, int div, int rows,
+                          int k_valid, int k_pad, uint8_t* q, float* s) {
+  const int groups = (k_pad + 127) / 128;
+  for (int r = 0; r < rows; ++r) {
+    const long src = map ? map[r] / div : r;
+    const uint16_t* xr = x + src * ldx;
+    for (int g = 0; g < groups; ++g) {
+      float amax = 0.0f;
+      for (int c = g * 128; c < g * 128 + 128 && c < k_valid; ++c) {
+        const float v = fabsf(oracle_bf16_to_f32(xr[c]));
+        if (v > amax) amax = v;
+      }
+      const float sc = amax > 0.0f ? amax / 448.0f : 1.0f;
+      s[(long)r * groups + g] = sc;
+      for (int c = g * 128; c < g * 128 + 128 && c < k_pad; ++c)
+        q[(long)r * k_pad + c] = c < k_valid ? oracle_f32_to_e4m3(oracle_bf16_to_f32(xr[c]) / sc) : 0;
+    }
+  }
 }

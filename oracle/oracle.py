@@ -49,6 +49,9 @@ def _load() -> ctypes.CDLL:
     lib.oracle_permute.restype = c_int
     lib.oracle_combine.argtypes = [vp, c_long, vp, vp, c_int, c_int, c_int, c_int, c_int, c_int64,
                                    c_int64, c_int, vp, vp]
+    lib.oracle_f32_to_e4m3.argtypes = [ctypes.c_float]
+    lib.oracle_f32_to_e4m3.restype = ctypes.c_uint8
+    lib.oracle_act_quant_fp8.argtypes = [vp, c_long, vp, c_int, c_int, c_int, c_int, vp, vp]
     return lib
 
 
@@ -145,6 +148,31 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *,
                          lo, hi, int(weights is not None), _p(wa) if wa is not None else None,
                          _p(out))
     return _bf16_tensor(out, (T, H))
+
+
+def f32_to_e4m3_c(values: torch.Tensor) -> torch.Tensor:
+    """e4m3fn codes (uint8) of fp32 values from the C encoder (round to
+    nearest even, saturating at +-448)."""
+    f = lib().oracle_f32_to_e4m3
+    flat = values.detach().float().cpu().reshape(-1).tolist()
+    return torch.tensor([f(v) for v in flat], dtype=torch.uint8).reshape(values.shape)
+
+
+def act_quant_fp8_c(x: torch.Tensor, k_pad: int | None = None, rows_src: torch.Tensor | None = None,
+                    src_div: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+    """The C restatement of ``act_quant_fp8``: (e4m3 codes as uint8 [rows, k_pad],
+    fp32 scales [rows, ceil(k_pad / 128)])."""
+    k_valid = x.shape[1]
+    k_pad = k_valid if k_pad is None else k_pad
+    xa = _np(x.to(torch.bfloat16), torch.int16)
+    ma = _np(rows_src.to(torch.int32), torch.int32) if rows_src is not None else None
+    rows = rows_src.numel() if rows_src is not None else x.shape[0]
+    groups = -(-k_pad // 128)
+    q = np.empty(rows * k_pad, np.uint8)
+    sc = np.empty(rows * groups, np.float32)
+    lib().oracle_act_quant_fp8(_p(xa), k_valid, _p(ma) if ma is not None else None, src_div, rows, k_valid,
+                               k_pad, _p(q), _p(sc))
+    return torch.from_numpy(q.reshape(rows, k_pad)), torch.from_numpy(sc.reshape(rows, groups))
 
 
 # --------------------------------------------------------------------------- reference FP math (torch)

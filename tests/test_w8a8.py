@@ -47,6 +47,42 @@ def test_oracle_quant_properties():
     assert torch.equal(_codes(q2), _codes(q3)) and torch.equal(s2, s3)
 
 
+def test_e4m3_encoder_c_matches_torch():
+    """The C e4m3 encoder (written from the format's definition) agrees with
+    torch's float8_e4m3fn conversion on every code, the midpoints between
+    neighbouring codes (ties to even), values just off them, subnormals and
+    saturation."""
+    codes = torch.arange(256, dtype=torch.uint8)
+    vals = codes.view(torch.float8_e4m3fn).float()
+    finite = vals[vals.isfinite()].unique()
+    pos = finite[finite >= 0]
+    mids = (pos[1:] + pos[:-1]) / 2
+    probes = torch.cat([finite, mids, mids * (1 + 2 ** -20), mids * (1 - 2 ** -20), -mids,
+                        torch.tensor([447.9, 448.0, 460.0, 1e6, 2.0 ** -10, 2.0 ** -11, 3 * 2.0 ** -11]),
+                        torch.randn(4000, generator=torch.Generator().manual_seed(5)) * 100])
+    got = oracle.f32_to_e4m3_c(probes)
+    want = probes.clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+    # +-0 may differ only in sign for values that round to zero
+    zero = (want & 0x7f) == 0
+    assert torch.equal(got[~zero], want[~zero]) and ((got[zero] & 0x7f) == 0).all()
+
+
+def test_act_quant_oracles_agree():
+    """The torch oracle and the plain-C restatement of the activation
+    quantiser give the same codes and scales (gather, padding, all-zero
+    groups, one huge value flushing its neighbours)."""
+    g = torch.Generator().manual_seed(9)
+    x = (torch.randn(40, 300, generator=g) * torch.rand(40, 1, generator=g) * 30).to(torch.bfloat16)
+    x[3, :128] = 0
+    x[5, 7] = 3.0e38
+    src = torch.randint(0, 80, (57,), generator=g, dtype=torch.int32)
+    for rows_src, div in ((None, 1), (src, 2)):
+        qt, st = oracle.act_quant_fp8(x, k_pad=320, rows_src=rows_src, src_div=div)
+        qc, scc = oracle.act_quant_fp8_c(x, k_pad=320, rows_src=rows_src, src_div=div)
+        assert torch.equal(st, scc)
+        assert torch.equal(_codes(qt), qc)
+
+
 def test_act_quant_argument_checks():
     L = _lib.lib
     # no rows: nothing to enqueue, no pointer needed
