@@ -1,7 +1,7 @@
 """MoE expert-layer benchmark (router -> permute -> grouped GEMMs -> combine).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload qwen3-30b-a3b|gpt-oss-20b|qwen3-235b-a22b]
+                    [--workload qwen3-30b-a3b|gpt-oss-20b|gpt-oss-120b|qwen3-235b-a22b]
 
 One step runs the layer once for every batch size of the workload (decode and
 prefill batches of one layer shape) on seeded synthetic weights and tokens
@@ -16,17 +16,22 @@ copies run on their own streams and overlap other batches' compute.
 N > 1 (torchrun, one rank per GPU): replicated-token expert parallelism, the
 reference's record_* layout: every rank routes all tokens and runs its E/N
 experts, combines its own experts' contributions and the [T, H] partial sums
-are all-reduced over NCCL ("fast" numerics, the reference's efficient EP
-exchange). Work per step is fixed (strong scaling).
+are summed over the group ("fast" numerics, the reference's efficient EP
+exchange, through the fused NVLink combine). Work per step is fixed (strong
+scaling). Before timing, every rank checks the EP layer against the
+single-GPU layer on one decode and one prefill batch ("parity").
 
 ``--impl reference`` times the reference algorithm on the host CPU (the
-torch restatement in oracle/, reference numerics), rank 0 only.
+oracle's torch restatement of the reference numerics), rank 0 only, with no
+library code loaded: step i runs batch i mod (number of batches), each batch
+timed whole.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -42,10 +47,8 @@ import torch.distributed as dist
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from moe_serving_profile_b200 import _lib, experts as X, layout, ops  # noqa: E402
+# plain torch: loads no library (the reference arm imports nothing else of the package)
 from moe_serving_profile_b200 import synthetic as S  # noqa: E402
-from moe_serving_profile_b200.parallel import ParallelGroup  # noqa: E402
-from moe_serving_profile_b200.router import GptOssRouter, Qwen3Router  # noqa: E402
 
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 L2_FLUSH_BYTES = 256 << 20
@@ -112,8 +115,17 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- workload
+def workload_config(cfg, world: int) -> dict:
+    """The workload's shape, identical in the line of both arms."""
+    return {"workload": cfg.name, "batches": list(cfg.batches), "hidden": cfg.hidden,
+            "experts": cfg.experts, "top_k": cfg.top_k, "intermediate": cfg.inter,
+            "weights": cfg.storage, "parallelism": f"ep{world} replicated-token"}
+
+
 def build_layer(cfg, dev, ep: int, rank: int, seed: int = 1):
     """Router module + rank-local packed experts for one synthetic layer."""
+    from moe_serving_profile_b200 import layout
+    from moe_serving_profile_b200.router import GptOssRouter, Qwen3Router
     epr = cfg.experts // ep
     sl = slice(rank * epr, (rank + 1) * epr)
     if cfg.family == "qwen3":
@@ -148,11 +160,12 @@ def numerics_for(ep: int) -> str:
     return "reference" if ep == 1 else "fast"
 
 
-def layer_call(cfg, router, packed, x, parallel, rank, ep):
+def layer_call(cfg, router, packed, x, parallel, rank, ep, numerics=None):
+    from moe_serving_profile_b200 import experts as X
     _, scores, idx = router(x)
     return X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts,
                            expert_begin=rank * (cfg.experts // ep), parallel=parallel,
-                           numerics=numerics_for(ep))
+                           numerics=numerics or numerics_for(ep))
 
 
 def w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst):
@@ -160,6 +173,8 @@ def w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst):
     ``numerics="efficient"``), reported beside the weight-only headline:
     per-batch CUDA-graph replays after an L2 flush, and the W8A8 gate/up GEMM
     of the largest batch timed alone."""
+    from moe_serving_profile_b200 import _lib, ops
+    from moe_serving_profile_b200 import experts as X
     def call(x):
         _, scores, idx = router(x)
         return X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts, expert_begin=0,
@@ -239,10 +254,12 @@ def w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst):
 
 
 def kernel_launches(T: int, K: int, E: int) -> int:
-    """Our kernels per layer call: router (2) + permute (1 or 3) + row gather
-    (large token tiles only) + 2 GEMMs + combine."""
+    """Our kernels per layer call: router selection (1; the logits are the
+    reference's own F.linear) + permute (1 or 3) + row gather (large token
+    tiles only) + 2 GEMMs + combine."""
+    from moe_serving_profile_b200 import experts as X
     gather = 1 if X.tile_policy(T, K, E) >= 64 else 0
-    return 2 + (1 if T * K <= 8192 else 3) + gather + 2 + 1
+    return 1 + (1 if T * K <= 8192 else 3) + gather + 2 + 1
 
 
 # --------------------------------------------------------------------------- CPU leg
@@ -270,58 +287,152 @@ def cpu_layer_time(cfg, T: int, seed: int = 1) -> float:
         return time.perf_counter() - t0
 
 
-def cpu_sweep(cfg, budget_s: float):
-    """tokens/s of the reference path on the host over the workload's batches.
-    Batches up to 64 tokens run whole; larger ones run a 64- or 512-token
-    sample and are scaled linearly by tokens (at >= 64 tokens nearly every
-    expert is in use, so the per-token cost is close to flat; linear scaling
-    slightly understates the CPU at the largest batches). Returns
-    (tokens/s, sample text)."""
+def cpu_batches(cfg, budget_s: float):
+    """The reference path on the host over the workload's batches, each batch
+    timed whole (no extrapolation), in increasing size until ``budget_s`` of
+    CPU time is spent. Returns (tokens/s over the measured batches, {T: s},
+    sample text)."""
     torch.set_num_threads(os.cpu_count() or 1)
-    total_t, total_s, parts = 0, 0.0, []
-    sample_T = 512 if budget_s >= 30 else 64
-    measured = {}
-    for T in cfg.batches:
-        run = T if T <= 64 else sample_T
-        if run not in measured:
-            measured[run] = cpu_layer_time(cfg, run)
-        sec = measured[run] * (T / run)
-        total_t += T
-        total_s += sec
-        parts.append(f"T={T}" + ("" if run == T else f" (scaled from {run})"))
-    return total_t / total_s, ", ".join(parts)
+    secs, spent = {}, 0.0
+    for T in sorted(cfg.batches):
+        if secs and spent > budget_s:
+            break
+        secs[T] = cpu_layer_time(cfg, T)
+        spent += secs[T]
+    value = sum(secs) / sum(secs.values())
+    skipped = [T for T in cfg.batches if T not in secs]
+    sample = ("reference numerics on host CPU, each batch timed whole: "
+              + ", ".join(f"T={T} {secs[T]:.2f} s" for T in sorted(secs))
+              + (f"; not measured (budget): {skipped}" if skipped else ""))
+    return value, secs, sample
 
 
 def reference_arm(args, cfg):
+    """The reference's CPU path, timed on the host cores (rank 0 only). With
+    at least as many steps as batches, step i runs batch i mod n_batches
+    (every batch timed whole at least once); with fewer, every step runs all
+    of them. value = sum of batch tokens / sum of the batches' mean times, the
+    GPU arm's metric."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    budget = 150.0 / max(1, args.steps + args.warmup)
-    for _ in range(args.warmup):
-        cpu_sweep(cfg, budget)
-    vals = []
-    for _ in range(args.steps):
-        v, sample = cpu_sweep(cfg, budget)
-        vals.append(v)
-    value = statistics.median(vals)
+    torch.set_num_threads(os.cpu_count() or 1)
+    batches = list(cfg.batches)
+    rotate = args.steps >= len(batches)
+
+    def step(i):
+        return [batches[i % len(batches)]] if rotate else batches
+
+    for i in range(args.warmup):
+        for T in step(i):
+            cpu_layer_time(cfg, T)
+    times = {T: [] for T in batches}
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        for T in step(args.warmup + i):
+            times[T].append(cpu_layer_time(cfg, T))
+    wall = time.perf_counter() - t0
+    mean = {T: statistics.mean(v) for T, v in times.items() if v}
+    value = sum(mean) / sum(mean.values())
     cores = torch.get_num_threads()
+    sample = (("step i runs batch i mod %d" % len(batches)) if rotate else "every step runs all batches") + \
+        ", each batch timed whole: " + ", ".join(f"T={T} {mean[T] * 1e3:.1f} ms (x{len(times[T])})"
+                                                 for T in batches if T in mean)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sum(cfg.batches) / value * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": cfg.name, "batches": list(cfg.batches), "path": "reference numerics "
-                   "(dequantise-then-BF16 per expert, ordered merge) on host CPU"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "ms_per_step": round(wall / max(1, args.steps) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, quantised like the checkpoints)",
+        "config": workload_config(cfg, args.gpus),
+        "reference_path": "the reference numerics (dequantise-then-BF16 per expert, ordered bf16 merge; "
+                          "the oracle's torch restatement) on the host CPU, one process",
+        "per_batch_ms": {str(T): round(mean[T] * 1e3, 3) for T in batches if T in mean},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": sample},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------------------- GPU arm
+def ep_parity(cfg, router, packed, parallel, rank, world, dev):
+    """EP layer against the single-GPU layer on every rank, on the smallest
+    and the largest batch: "reference" numerics must be bitwise equal (the
+    ordered global-expert combine is EP-invariant), "fast" numerics within
+    the layer tolerance (rel. L2 <= 1e-2). Every rank builds the whole layer
+    for the comparison; the result is reduced over the group (max error,
+    AND of bitwise)."""
+    from moe_serving_profile_b200 import experts as X
+    _, packed1 = build_layer(cfg, dev, 1, 0)
+    res = {}
+    for T in (min(cfg.batches), max(cfg.batches)):
+        x = S.make_hidden(T, cfg.hidden, seed=7000 + T, device=dev)
+        _, scores, idx = router(x)
+        one = X.layer_forward(packed1, x, idx, scores, num_experts=cfg.experts, expert_begin=0)
+        for num in ("reference", "fast"):
+            out = X.layer_forward(packed, x, idx, scores, num_experts=cfg.experts,
+                                  expert_begin=rank * (cfg.experts // world), parallel=parallel,
+                                  numerics=num)
+            d = (out.float() - one.float())
+            stats = torch.tensor([float(d.abs().max()), float(d.norm() / one.float().norm().clamp_min(1e-30)),
+                                  0.0 if torch.equal(out, one) else 1.0], device=dev, dtype=torch.float64)
+            dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+            res[f"{num}_T{T}"] = {"max_abs": float(stats[0]), "rel_l2": float(stats[1]),
+                                  "bitwise": bool(stats[2] == 0.0)}
+    del packed1
+    torch.cuda.empty_cache()
+    res["ok"] = all(v["bitwise"] for k, v in res.items() if k.startswith("reference")) and \
+        all(v["rel_l2"] <= 1e-2 for k, v in res.items() if k.startswith("fast"))
+    return res
+
+
+def stage_breakdown(cfg, router, packed, xs, parallel, rank, world, stream, reps=5):
+    """Per-stage device time (ms, warm L2, eager) of one layer call per batch:
+    router, permute, row gather + gate/up GEMM, down GEMM, combine (+ the EP
+    exchange at N > 1). Every rank runs the same sequence, so the collective
+    steps line up."""
+    from moe_serving_profile_b200 import _lib, ops
+    from moe_serving_profile_b200 import experts as X
+    lo = rank * (cfg.experts // world)
+    out = {}
+    for T, x in xs.items():
+        acc = [0.0] * 5
+        for it in range(reps + 2):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            with torch.cuda.stream(stream):
+                ev[0].record(stream)
+                _, scores, idx = router(x)
+                ev[1].record(stream)
+                perm = ops.permute(idx, cfg.experts)
+                ev[2].record(stream)
+                act = X.gate_up(packed, x, perm, K=cfg.top_k, num_experts=cfg.experts, expert_begin=lo,
+                                tokens=T)
+                ev[3].record(stream)
+                contrib = X.down(packed, act, perm, scores, K=cfg.top_k, num_experts=cfg.experts,
+                                 expert_begin=lo, tokens=T)
+                ev[4].record(stream)
+                if parallel is None:
+                    ops.combine(contrib, perm.inverse, idx, order=_lib.ORDER_EXPERT)
+                else:
+                    parallel.combine_reduce(contrib, perm.inverse, idx, lo, lo + packed.n_experts)
+                ev[5].record(stream)
+            ev[5].synchronize()
+            if it >= 2:
+                for j in range(5):
+                    acc[j] += ev[j].elapsed_time(ev[j + 1]) / reps
+        t = torch.tensor(acc, device=x.device, dtype=torch.float64)
+        if parallel is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        names = ("router", "permute", "gather+gate_up", "down", "combine" if parallel is None else "exchange")
+        out[str(T)] = {n: round(float(v), 4) for n, v in zip(names, t.tolist())}
+    return out
+
+
 def profile_calls(args, cfg):
     """Three eager layer calls per batch size, nothing timed (an ncu target)."""
+    from moe_serving_profile_b200 import _lib
+    from moe_serving_profile_b200 import experts as X
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     router, packed = build_layer(cfg, dev, 1, 0)
@@ -359,6 +470,10 @@ def main():
     if args.profile:
         return profile_calls(args, cfg)
 
+    from moe_serving_profile_b200 import _lib, ops  # noqa: F401  (loads the library)
+    from moe_serving_profile_b200 import experts as X
+    from moe_serving_profile_b200.parallel import ParallelGroup
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -371,9 +486,8 @@ def main():
     hbm, tf_burst, tf_sust, peak_kind = peaks()
 
     router, packed = build_layer(cfg, dev, world, rank)
-    if parallel is not None:
-        router.shard_over(parallel)   # large batches: each rank routes a slice, one all-gather
     batches = list(cfg.batches)
+    parity = ep_parity(cfg, router, packed, parallel, rank, world, dev) if world > 1 else None
     xs = {T: S.make_hidden(T, cfg.hidden, seed=1000 + T, device=dev) for T in batches}
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(device=dev)
@@ -452,7 +566,9 @@ def main():
         tfs = flops / (ms / 1e3) / 1e12
         per_batch.append({"tokens": T, "ms": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
                           "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                          "hbm_frac_per_gpu": round(gbs / (hbm * world), 4),
                           "tflops": round(tfs, 2), "tensor_frac": round(tfs / tf_burst, 4),
+                          "tensor_frac_per_gpu": round(tfs / (tf_burst * world), 4),
                           "used_experts": int((counts > 0).sum()),
                           "expert_load_cv": round(S.expert_load_cv(counts), 3)})
 
@@ -542,11 +658,13 @@ def main():
     if world == 1 and cfg.storage == "fp8" and not args.no_w8a8:
         w8a8 = w8a8_leg(args, cfg, router, packed, xs, flush, stream, dev, hbm, tf_burst)
 
+    stages = stage_breakdown(cfg, router, packed, xs, parallel, rank, world, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, sample = cpu_sweep(cfg, budget_s=20.0)
+        v, _, sample = cpu_batches(cfg, budget_s=25.0)
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
-               "kind": "port", "sample": f"reference numerics on host CPU: {sample}"}
+               "kind": "port", "sample": sample}
 
     launches = args.steps * sum(kernel_launches(T, cfg.top_k, cfg.experts) for T in batches)
     if rank == 0:
@@ -555,19 +673,19 @@ def main():
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(step_ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, quantised like the checkpoints)",
-            "config": {"workload": cfg.name, "batches": batches, "hidden": cfg.hidden,
-                       "experts": cfg.experts, "top_k": cfg.top_k, "intermediate": cfg.inter,
-                       "weights": cfg.storage, "parallelism": f"ep{world} replicated-token",
-                       "numerics": numerics_for(world),
-                       "l2": "flushed (256 MiB write) before every batch", "timing": "CUDA graph "
-                       "replay per batch, CUDA events"},
-            "per_batch": per_batch, "roofline": roofline,
+            "config": workload_config(cfg, world),
+            "numerics": numerics_for(world), "routing": "exact (F.linear logits, fused selection)",
+            "l2": "flushed (256 MiB write) before every batch",
+            "timing": "CUDA graph replay per batch, CUDA events",
+            "per_batch": per_batch, "roofline": roofline, "stages_ms": stages,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches, "clocks": clocks.summary(), "cpu_baseline": cpu,
         }
         if w8a8 is not None:
             line["w8a8"] = w8a8
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     for g in graphs.values():
         del g

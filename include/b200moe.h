@@ -102,9 +102,14 @@ int b200moe_route_record(int device, void* stream, const long long* indices, con
  * x: bf16 rows of stride ldx elements; src(r) = map[r] / map_div when map is
  * given (the permuted-row gather perm_src / K), else r. q: e4m3 [rows, k_pad];
  * s: fp32 [rows, ceil(k_pad / 128)]. Needs k_valid % 4 == 0, ldx % 4 == 0,
- * k_pad % 16 == 0 and k_valid <= k_pad. */
+ * k_pad % 16 == 0 and k_valid <= k_pad.
+ * row_offsets (device int32 [E+1], b200moe_permute's offsets) or NULL: when
+ * given, only rows r in [row_offsets[expert_lo], row_offsets[expert_hi]) are
+ * quantised (the rows of one rank's experts; the others are left unwritten,
+ * as the rank's GEMM never reads them). */
 int b200moe_act_quant_fp8(int device, void* stream, const void* x, long long ldx, const int* map,
-                          int map_div, int rows, int k_valid, int k_pad, void* q, float* s);
+                          int map_div, int rows, int k_valid, int k_pad, void* q, float* s,
+                          const int* row_offsets, int expert_lo, int expert_hi);
 
 /* ------------------------------------------------------------ permutation
  * Expert-contiguous permutation of the T*K (token, slot) assignments.

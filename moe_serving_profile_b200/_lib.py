@@ -109,7 +109,7 @@ def _load() -> ctypes.CDLL:
                                          c_void_p, c_void_p]
     lib.b200moe_act_quant_fp8.restype = c_int
     lib.b200moe_act_quant_fp8.argtypes = [c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int,
-                                          c_int, c_int, c_void_p, c_void_p]
+                                          c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int]
     lib.b200moe_permute_workspace.restype = c_int
     lib.b200moe_permute_workspace.argtypes = [c_int, c_int, c_int, POINTER(c_size_t)]
     lib.b200moe_permute.restype = c_int

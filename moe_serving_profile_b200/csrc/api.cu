@@ -162,13 +162,15 @@ int b200moe_route_record(int device, void* stream, const long long* indices, con
 }
 
 int b200moe_act_quant_fp8(int device, void* stream, const void* x, long long ldx, const int* map,
-                          int map_div, int rows, int k_valid, int k_pad, void* q, float* s) {
+                          int map_div, int rows, int k_valid, int k_pad, void* q, float* s,
+                          const int* row_offsets, int expert_lo, int expert_hi) {
   B200_CHECK(rows >= 0 && k_valid >= 0 && k_pad >= k_valid, "bad sizes rows=%d k_valid=%d k_pad=%d", rows,
              k_valid, k_pad);
   B200_CHECK(k_valid % 4 == 0 && k_pad % 16 == 0 && ldx % 4 == 0 && ldx >= k_valid,
              "need k_valid %% 4 == 0, k_pad %% 16 == 0, ldx %% 4 == 0 and ldx >= k_valid");
   B200_CHECK(map == nullptr || map_div >= 1, "map_div must be >= 1");
   B200_CHECK((long long)rows * ((k_pad + 127) / 128) < (1ll << 40), "too many groups");
+  B200_CHECK(row_offsets == nullptr || (expert_lo >= 0 && expert_hi >= expert_lo), "bad expert range");
   if (rows == 0 || k_pad == 0) return B200MOE_OK;
   B200_CHECK(x && q && s, "x, q and s are required");
   B200_CHECK(reinterpret_cast<uintptr_t>(x) % 8 == 0 && reinterpret_cast<uintptr_t>(q) % 4 == 0,
@@ -176,7 +178,7 @@ int b200moe_act_quant_fp8(int device, void* stream, const void* x, long long ldx
   int rc = use_device(device, nullptr);
   if (rc) return rc;
   B200_CUDA(b200::launch_act_quant(static_cast<cudaStream_t>(stream), x, ldx, map, map_div, rows, k_valid,
-                                   k_pad, q, s));
+                                   k_pad, q, s, row_offsets, expert_lo, expert_hi));
   return B200MOE_OK;
 }
 

@@ -21,7 +21,8 @@ cudaError_t launch_route_record(cudaStream_t st, const long long* indices, const
 
 // Per-(row, 128-column) FP8 activation quantisation (w8a8.cu).
 cudaError_t launch_act_quant(cudaStream_t st, const void* x, long long ldx, const int* map, int div,
-                             int rows, int k_valid, int k_pad, void* q, float* s);
+                             int rows, int k_valid, int k_pad, void* q, float* s, const int* range_offsets,
+                             int expert_lo, int expert_hi);
 
 // W8A8 grouped GEMM (w8a8.cu): kernel parameters, filled by the host.
 struct W8A8Params {

@@ -292,9 +292,38 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// torch's descending comparator: a NaN is larger than any number.
+__device__ __forceinline__ bool gt_nan(float a, float b) {
+  return (a != a && b == b) || a > b;
+}
+
 constexpr int kMaxPerLane = 16;  // E <= 512
 
-// One warp per token.
+// Sum over lanes 0 .. K-1 (lanes K .. P-1 contribute 0, P = the power of two
+// >= K) by xor-butterfly: lane 0 gets ((v0 + v4) + (v2 + v6)) + ((v1 + v5) +
+// (v3 + v7)) at K = 8. This is the order of torch's CUDA sum over a row of K
+// values and of the warp reduction of its softmax over K values.
+__device__ __forceinline__ float butterfly_sum(float v, int K) {
+  int p = 1;
+  while (p < K) p <<= 1;
+  for (int o = p >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// One warp per token. The selection reproduces torch.topk on CUDA for
+// k <= 32 bit for bit, including the slot order of equal values:
+//   1. the k selected experts are those with a key above the k-th largest
+//      key, plus the lowest-index experts whose key equals it;
+//   2. they are laid out in index order, the above-the-k-th ones first, in
+//      32 slots (slots k .. 31 invalid);
+//   3. a 32-slot bitonic sorting network orders them: comparator (a, b) with
+//      a at the lower slot swaps when "not (a valid and a > b) and b valid"
+//      equals the stage's direction, so equal keys are exchanged whenever the
+//      direction is ascending (the final merge is descending throughout).
+// Keys: the fp32 softmax probabilities (QWEN3, NATIVE; the softmax is
+// torch's warp softmax: lane-sequential sums over e = lane + 32 i, then a
+// xor-butterfly across lanes, probs = exp(x - max) / sum) or the bf16 logits
+// (GPT_OSS). Sums over the k selected values use butterfly_sum.
 __global__ void __launch_bounds__(256) router_select_kernel(const void* __restrict__ logits,
                                                              int T, int E, int K, int mode,
                                                              int normalize, float* probs,
@@ -305,7 +334,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
 
-  float val[kMaxPerLane];
+  float key[kMaxPerLane];
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const int e = lane + 32 * i;
@@ -316,13 +345,36 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
       else
         v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[(long long)t * E + e]);
     }
-    val[i] = v;
+    key[i] = v;
   }
 
-  // ---- top-k on the logits: value descending, ties by ascending expert id.
+  if (mode != kGptOss) {
+    // ---- softmax over all E (fp32): the keys become the probabilities
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) mx = fmaxf(mx, key[i]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    float lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      key[i] = (lane + 32 * i < E) ? expf(key[i] - mx) : 0.f;
+      lsum += key[i];
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      key[i] = key[i] / lsum;
+      if (mode == kQwen3 && probs != nullptr && e < E) probs[(long long)t * E + e] = key[i];
+    }
+  }
+
+  // ---- 1. the selected set: K rounds of (key descending, index ascending)
   uint32_t taken = 0;
-  int my_idx = -1;      // lane k < K holds slot k
-  float my_val = 0.f;
+  int sidx = -1;        // lane k < K: the k-th selected expert
+  float skey = 0.f;
   for (int k = 0; k < K; ++k) {
     unsigned long long best = 0ull;
 #pragma unroll
@@ -330,7 +382,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
       const int e = lane + 32 * i;
       if (e < E && !((taken >> i) & 1u)) {
         const unsigned long long c =
-            (static_cast<unsigned long long>(order_key(val[i])) << 32) | (0xffffffffu - e);
+            (static_cast<unsigned long long>(order_key(key[i])) << 32) | (0xffffffffu - e);
         best = c > best ? c : best;
       }
     }
@@ -341,74 +393,87 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
     }
     const int e_sel = static_cast<int>(0xffffffffu - static_cast<uint32_t>(best));
     if ((e_sel & 31) == lane) taken |= 1u << (e_sel >> 5);
-    // the selected value, recovered from the winning lane
     float vsel = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i)
-      if (lane + 32 * i == e_sel) vsel = val[i];
+      if (lane + 32 * i == e_sel) vsel = key[i];
     vsel = __shfl_sync(kFull, vsel, e_sel & 31);
     if (lane == k) {
-      my_idx = e_sel;
-      my_val = vsel;
+      sidx = e_sel;
+      skey = vsel;
     }
   }
-  const float top = __shfl_sync(kFull, my_val, 0);
 
+  // ---- 2. index order, keys above the k-th first
+  const float kth = __shfl_sync(kFull, skey, K - 1);
+  const int grp = lane < K ? (order_key(skey) > order_key(kth) ? 0 : 1) : 2;
+  int pos = 0;
+  for (int j = 0; j < K; ++j) {
+    const int gj = __shfl_sync(kFull, grp, j);
+    const int ij = __shfl_sync(kFull, sidx, j);
+    if (lane < K && (gj < grp || (gj == grp && ij < sidx))) ++pos;
+  }
+  float okey = 0.f;
+  int oidx = -1;
+  for (int j = 0; j < K; ++j) {
+    const int pj = __shfl_sync(kFull, pos, j);
+    const float kj = __shfl_sync(kFull, skey, j);
+    const int ij = __shfl_sync(kFull, sidx, j);
+    if (lane == pj) {
+      okey = kj;
+      oidx = ij;
+    }
+  }
+  bool valid = lane < K;
+
+  // ---- 3. the 32-slot bitonic network (lane = slot)
+  auto step = [&](int stride, bool dir) {
+    const float pk = __shfl_xor_sync(kFull, okey, stride);
+    const int pi = __shfl_xor_sync(kFull, oidx, stride);
+    const bool pv = __shfl_xor_sync(kFull, valid ? 1 : 0, stride) != 0;
+    const bool is_a = (lane & stride) == 0;
+    const float ka = is_a ? okey : pk, kb = is_a ? pk : okey;
+    const bool va = is_a ? valid : pv, vb = is_a ? pv : valid;
+    const bool swap = (gt_nan(ka, kb) && va) || !vb;
+    if (swap == dir) {
+      okey = pk;
+      oidx = pi;
+      valid = pv;
+    }
+  };
+#pragma unroll
+  for (int size = 2; size < 32; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) step(stride, (lane & size) != 0);
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) step(stride, false);
+
+  // lanes 0 .. K-1 now hold the slots in torch's order
+  const bool mine = lane < K;
   if (mode == kGptOss) {
-    // softmax over the k selected bf16 logits, result rounded to bf16
-    const float ex = (lane < K) ? expf(my_val - top) : 0.f;
-    float s = 0.f;
-    for (int k = 0; k < K; ++k) s += __shfl_sync(kFull, ex, k);
-    if (lane < K) {
-      reinterpret_cast<__nv_bfloat16*>(scores)[(long long)t * K + lane] = __float2bfloat16_rn(ex / s);
-      indices[(long long)t * K + lane] = my_idx;
-      if (counts) atomicAdd(&counts[my_idx], 1);
+    // softmax over the k selected bf16 logits (fp32 arithmetic, bf16 result)
+    const float top = __shfl_sync(kFull, okey, 0);
+    const float ex = mine ? expf(okey - top) : 0.f;
+    const float s = __shfl_sync(kFull, butterfly_sum(ex, K), 0);
+    if (mine) reinterpret_cast<__nv_bfloat16*>(scores)[(long long)t * K + lane] = __float2bfloat16_rn(ex / s);
+  } else {
+    const float p = mine ? okey : 0.f;
+    float wv = p;
+    if (normalize) {
+      float s = __shfl_sync(kFull, butterfly_sum(p, K), 0);
+      if (mode == kNative) s = fmaxf(s, 1e-20f);
+      wv = p / s;
     }
-    return;
-  }
-
-  // ---- softmax over all E (fp32); QWEN3 writes the probabilities
-  float lsum = 0.f;
-  float ex[kMaxPerLane];
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
-    ex[i] = (lane + 32 * i < E) ? expf(val[i] - top) : 0.f;
-    lsum += ex[i];
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
-  if (mode == kQwen3 && probs != nullptr) {
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) probs[(long long)t * E + e] = ex[i] / lsum;
+    if (mine) {
+      if (mode == kQwen3)
+        reinterpret_cast<float*>(scores)[(long long)t * K + lane] = wv;
+      else
+        reinterpret_cast<__nv_bfloat16*>(scores)[(long long)t * K + lane] = __float2bfloat16_rn(wv);
     }
   }
-  // probability of my slot
-  float psel = 0.f;
-  for (int k = 0; k < K; ++k) {
-    const int e = __shfl_sync(kFull, my_idx, k);
-    float pe = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
-      if (lane + 32 * i == e) pe = ex[i] / lsum;
-    pe = __shfl_sync(kFull, pe, e & 31);
-    if (lane == k) psel = pe;
-  }
-  float denom = 1.f;
-  if (normalize) {
-    float s = 0.f;
-    for (int k = 0; k < K; ++k) s += __shfl_sync(kFull, psel, k);
-    denom = (mode == kNative) ? fmaxf(s, 1e-20f) : s;
-  }
-  if (lane < K) {
-    const float wv = normalize ? psel / denom : psel;
-    if (mode == kQwen3)
-      reinterpret_cast<float*>(scores)[(long long)t * K + lane] = wv;
-    else
-      reinterpret_cast<__nv_bfloat16*>(scores)[(long long)t * K + lane] = __float2bfloat16_rn(wv);
-    indices[(long long)t * K + lane] = my_idx;
-    if (counts) atomicAdd(&counts[my_idx], 1);
+  if (mine) {
+    indices[(long long)t * K + lane] = oidx;
+    if (counts && oidx >= 0 && oidx < E) atomicAdd(&counts[oidx], 1);
   }
 }
 

@@ -36,12 +36,17 @@ __device__ __forceinline__ uint32_t e4m3x2(float x0, float x1) {
 __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
                                                         const int* __restrict__ map, int div, int rows,
                                                         int k_valid, int k_pad, uint8_t* __restrict__ q,
-                                                        float* __restrict__ s) {
+                                                        float* __restrict__ s,
+                                                        const int* __restrict__ range_offsets, int lo,
+                                                        int hi) {
   const int groups = (k_pad + 127) / 128;
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= (long long)rows * groups) return;
   const int r = static_cast<int>(w / groups), g = static_cast<int>(w - (long long)r * groups);
+  // only the rows [offsets[lo], offsets[hi]) of one rank's experts (the
+  // others are never read by that rank's GEMM)
+  if (range_offsets != nullptr && (r < range_offsets[lo] || r >= range_offsets[hi])) return;
   const long long src = map ? map[r] / div : r;
   const int c = g * 128 + lane * 4;
   float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -66,11 +71,13 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
 }  // namespace
 
 cudaError_t launch_act_quant(cudaStream_t st, const void* x, long long ldx, const int* map, int div,
-                             int rows, int k_valid, int k_pad, void* q, float* s) {
+                             int rows, int k_valid, int k_pad, void* q, float* s, const int* range_offsets,
+                             int expert_lo, int expert_hi) {
   if (rows == 0) return cudaSuccess;
   const long long warps = (long long)rows * ((k_pad + 127) / 128);
   act_quant_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, map, div, rows, k_valid, k_pad, static_cast<uint8_t*>(q), s);
+      static_cast<const __nv_bfloat16*>(x), ldx, map, div, rows, k_valid, k_pad, static_cast<uint8_t*>(q), s,
+      range_offsets, expert_lo, expert_hi);
   return cudaGetLastError();
 }
 

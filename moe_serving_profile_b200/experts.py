@@ -131,13 +131,16 @@ def run_experts_w8a8(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutati
     dev = hidden.device
     bn = tile_policy(T, K, num_experts, 128)
     div = K if b_map_div is None else b_map_div
-    q, qs = ops.act_quant_fp8(hidden, k_pad=w.h_k, rows_src=perm.perm_src, src_div=div)
+    # only this rank's rows are quantised (other ranks' rows are never read)
+    lo, hi = expert_begin, expert_begin + w.n_experts
+    local = dict(offsets=perm.offsets, expert_lo=lo, expert_hi=hi) if (lo, hi) != (0, num_experts) else {}
+    q, qs = ops.act_quant_fp8(hidden, k_pad=w.h_k, rows_src=perm.perm_src, src_div=div, **local)
     act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16)
     ops.w8a8_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts, max_rows=R,
                   planes=2, feat_pad=w.i_pad, n_feat=w.inter, k_pad=w.h_k, weight=w.w1,
                   fp8_block=w.block, q=q, q_scale=qs, epilogue=_lib.EPI_SWIGLU, out=act,
                   token_tile=bn)
-    q2, qs2 = ops.act_quant_fp8(act[:, :w.inter], k_pad=w.i_pad)
+    q2, qs2 = ops.act_quant_fp8(act[:, :w.inter], k_pad=w.i_pad, **local)
     if contrib is None:
         contrib = torch.empty(R, w.hidden, device=dev, dtype=torch.bfloat16)
     ops.w8a8_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts, max_rows=R,

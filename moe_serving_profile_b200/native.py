@@ -303,8 +303,11 @@ class MoELayer(torch.nn.Module):
 
     def __init__(self, gate_weight: torch.Tensor, experts: LocalSwiGLUExperts, plan: ExpertPlan,
                  top_k: int, renormalize: bool = True, shared: SharedSwiGLU | None = None,
-                 collective: Collective | None = None, layer_id: int = 0):
+                 collective: Collective | None = None, layer_id: int = 0, logits: str = "exact"):
         super().__init__()
+        if logits not in ("exact", "fused"):
+            raise ValueError(f"logits must be 'exact' or 'fused', got {logits!r}")
+        self.logits_mode = logits   # "exact": fp32 F.linear as moe.route does; "fused": fixed-order kernel
         self.gate_weight = torch.nn.Parameter(gate_weight, requires_grad=False)
         self.experts = experts
         self.shared = shared
@@ -315,8 +318,13 @@ class MoELayer(torch.nn.Module):
         self.layer_id = layer_id
 
     def forward(self, hidden: torch.Tensor) -> tuple[torch.Tensor, RoutingStats]:
-        out = ops.router(_lib.ROUTER_NATIVE, hidden, self.gate_weight, None, self.top_k,
-                         self.renormalize)
+        if self.logits_mode == "exact":
+            lg = torch.nn.functional.linear(hidden.float(), self.gate_weight.float()).contiguous()
+            out = ops.router(_lib.ROUTER_NATIVE, None, self.gate_weight, None, self.top_k,
+                             self.renormalize, logits=lg)
+        else:
+            out = ops.router(_lib.ROUTER_NATIVE, hidden, self.gate_weight, None, self.top_k,
+                             self.renormalize)
         output = routed_forward(hidden, out.indices, out.scores, self.experts, self.plan,
                                 self.collective)
         if self.shared is not None:

@@ -118,11 +118,14 @@ def route_record(indices: torch.Tensor, scores: torch.Tensor,
 
 
 def act_quant_fp8(x: torch.Tensor, k_pad: int | None = None, rows_src: torch.Tensor | None = None,
-                  src_div: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+                  src_div: int = 1, offsets: torch.Tensor | None = None, expert_lo: int = 0,
+                  expert_hi: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
     """Dynamic FP8 activation quantisation of the W8A8 FP8 path: e4m3 ``q``
     [rows, k_pad] and fp32 ``scales`` [rows, ceil(k_pad / 128)], one scale per
     row and 128-column group (amax / 448). With ``rows_src`` (int32), row r
-    quantises ``x[rows_src[r] // src_div]`` (the permuted-row gather)."""
+    quantises ``x[rows_src[r] // src_div]`` (the permuted-row gather). With
+    ``offsets`` (the permutation's device offsets), only the rows
+    [offsets[expert_lo], offsets[expert_hi]) are written."""
     device = _dev(x, "x")
     if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("x must be a 2-D bfloat16 tensor with unit column stride")
@@ -134,11 +137,16 @@ def act_quant_fp8(x: torch.Tensor, k_pad: int | None = None, rows_src: torch.Ten
         if rows_src.dtype != torch.int32 or not rows_src.is_contiguous() or rows_src.dim() != 1:
             raise ValueError("rows_src must be contiguous 1-D int32")
         rows = rows_src.numel()
+    if offsets is not None:
+        _dev(offsets, "offsets")
+        if offsets.dtype != torch.int32 or not 0 <= expert_lo <= expert_hi < offsets.numel():
+            raise ValueError("offsets must be int32 with 0 <= expert_lo <= expert_hi < offsets.numel()")
     q = torch.empty((rows, k_pad), device=x.device, dtype=torch.float8_e4m3fn)
     s = torch.empty((rows, -(-k_pad // 128)), device=x.device, dtype=torch.float32)
     check(
         lib.b200moe_act_quant_fp8(device, _stream(device), _ptr(x), x.stride(0), _ptr(rows_src),
-                                  int(src_div), rows, k_valid, k_pad, _ptr(q), _ptr(s)),
+                                  int(src_div), rows, k_valid, k_pad, _ptr(q), _ptr(s), _ptr(offsets),
+                                  int(expert_lo), int(expert_hi)),
         "act_quant_fp8",
     )
     return q, s

@@ -62,6 +62,11 @@ class ParallelExperts(nn.Module):
         g, u, d = projs
         if any(len(p) != self.num_experts for p in projs):
             raise ValueError("every local expert needs gate_proj, up_proj and down_proj")
+        # checked before anything is packed or released, so every forward of
+        # a misconfigured module raises (prepare_fp8 refuses the same case,
+        # moe_serving/efficient_kernels.py:228-231)
+        if self.numerics == "efficient" and any(p.scales is None for p in g + u + d):
+            raise ValueError("efficient Qwen mode requires block FP8 expert weights")
         gw = torch.stack([p.weight for p in g])
         uw = torch.stack([p.weight for p in u])
         dw = torch.stack([p.weight for p in d])
@@ -76,8 +81,6 @@ class ParallelExperts(nn.Module):
             self.packed = layout.bf16_experts(gw.to(torch.bfloat16), uw.to(torch.bfloat16),
                                               dw.to(torch.bfloat16))
         self.local = None
-        if self.numerics == "efficient" and self.packed.fmt != layout._lib.W_FP8:
-            raise ValueError("efficient Qwen mode requires block FP8 expert weights")
         return self.packed
 
     def forward(self, hidden, indices, weights):

@@ -11,7 +11,10 @@
  *     moe_serving/gpt_oss_parallel.py:183-193; transformers 5.5.0
  *     integrations/mxfp4.py:279-330 is the readable proxy)
  *   - router logits in the library's documented fixed fp32 order, and the
- *     top-k selection (value descending, ties by ascending expert id)
+ *     top-k selection of torch.topk on CUDA (k <= 32) with its slot order
+ *     for equal values, the selection the reference's routers run
+ *     (transformers qwen3_moe/modeling_qwen3_moe.py:266 and
+ *     gpt_oss/modeling_gpt_oss.py:129 call torch.topk; moe_serving/moe.py:104)
  *   - the expert-contiguous permutation in (slot, token) order
  *     (moe_serving/parallel_numerics.py:21-26)
  *   - the ordered bf16 combine (parallel_numerics.py:26-35; moe.py:123-136)
@@ -139,9 +142,24 @@ static int greater(float a, int ia, float b, int ib) {
   return ia < ib;
 }
 
-/* top-k of each row of values [T, E]: value descending, ties by index */
+/* torch's descending comparator: a NaN is larger than any number */
+static int key_gt(float a, float b) { return (a != a && b == b) || a > b; }
+
+/* top-k of each row of values [T, E] in the slot order torch.topk gives on
+   CUDA for k <= 32 (pinned against torch's outputs by the fixtures of
+   tests/golden/make_router_golden.py):
+     1. the selected set: keys above the k-th largest key, then the
+        lowest-index keys equal to it;
+     2. laid out in index order, keys above the k-th first, in 32 slots
+        (slots k..31 invalid);
+     3. sorted by a 32-slot bitonic network whose comparator (a at the lower
+        slot, b at the upper) exchanges the pair when
+        ((a valid and a > b) or b invalid) equals the stage's direction
+        (direction = bit `size` of the slot in the building stages, 0 in the
+        final merge), so equal keys trade places on every ascending stage. */
 void oracle_topk(const float* values, int T, int E, int K, int64_t* indices) {
   char* taken = (char*)malloc((size_t)E);
+  int sel[32];
   for (int t = 0; t < T; ++t) {
     memset(taken, 0, (size_t)E);
     const float* row = values + (long)t * E;
@@ -152,8 +170,43 @@ void oracle_topk(const float* values, int T, int E, int K, int64_t* indices) {
         if (best < 0 || greater(row[e], e, row[best], best)) best = e;
       }
       taken[best] = 1;
-      indices[(long)t * K + k] = best;
+      sel[k] = best;
     }
+    const float kth = row[sel[K - 1]];
+    float key[32];
+    int idx[32], valid[32];
+    int n = 0;
+    for (int pass = 0; pass < 2; ++pass)          /* above the k-th, then equal to it */
+      for (int e = 0; e < E; ++e) {
+        if (!taken[e]) continue;
+        const int above = key_gt(row[e], kth) || (row[e] != row[e] && kth == kth);
+        if (above == (pass == 0)) {
+          key[n] = row[e];
+          idx[n] = e;
+          valid[n] = 1;
+          ++n;
+        }
+      }
+    for (int i = n; i < 32; ++i) {
+      key[i] = 0.f;
+      idx[i] = -1;
+      valid[i] = 0;
+    }
+    for (int size = 2; size <= 32; size <<= 1)
+      for (int stride = size >> 1; stride > 0; stride >>= 1)
+        for (int a = 0; a < 32; ++a) {
+          if (a & stride) continue;
+          const int b = a + stride;
+          const int dir = size < 32 ? (a & size) != 0 : 0;
+          const int swap = (key_gt(key[a], key[b]) && valid[a]) || !valid[b];
+          if (swap == dir) {
+            const float tk = key[a];
+            const int ti = idx[a], tv = valid[a];
+            key[a] = key[b], idx[a] = idx[b], valid[a] = valid[b];
+            key[b] = tk, idx[b] = ti, valid[b] = tv;
+          }
+        }
+    for (int k = 0; k < K; ++k) indices[(long)t * K + k] = idx[k];
   }
   free(taken);
 }

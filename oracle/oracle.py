@@ -113,12 +113,43 @@ def router_logits(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, m
 
 
 def topk(values: torch.Tensor, k: int) -> torch.Tensor:
-    """Top-k indices: value descending, equal values by ascending index."""
+    """torch.topk(values, k).indices as computed on CUDA (k <= 32), including
+    the slot order of equal values (oracle.c states the rule)."""
     T, E = values.shape
     va = np.ascontiguousarray(values.detach().float().cpu().numpy())
     out = np.empty(T * k, np.int64)
     lib().oracle_topk(_p(va), T, E, k, _p(out))
     return torch.from_numpy(out.reshape(T, k))
+
+
+def butterfly_sum(v: torch.Tensor) -> torch.Tensor:
+    """Row sums of v [T, K] (float32) in the order torch's CUDA sum over a row
+    of K values uses (xor-butterfly over the next power of two, zero padded):
+    ((v0 + v4) + (v2 + v6)) + ((v1 + v5) + (v3 + v7)) at K = 8. Pinned against
+    torch's outputs by tests/golden/router_torch_cuda.pt for K = 2 and 8."""
+    T, K = v.shape
+    P = 1
+    while P < K:
+        P <<= 1
+    lanes = torch.zeros(T, P, dtype=torch.float32)
+    lanes[:, :K] = v.float()
+    ids = torch.arange(P)
+    o = P >> 1
+    while o >= 1:
+        lanes = lanes + lanes[:, ids ^ o]
+        o >>= 1
+    return lanes[:, 0]
+
+
+def qwen_select(probs: torch.Tensor, k: int, normalize: bool):
+    """torch.topk of the fp32 probabilities on CUDA (slot order of ties
+    included) and the renormalised scores (transformers
+    qwen3_moe/modeling_qwen3_moe.py:266-269)."""
+    idx = topk(probs, k)
+    top = torch.gather(probs.float().cpu(), 1, idx)
+    if normalize:
+        top = top / butterfly_sum(top)[:, None]
+    return idx, top
 
 
 def permute(indices: torch.Tensor, num_experts: int):

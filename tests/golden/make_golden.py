@@ -23,6 +23,7 @@ The fixtures are small (.pt, tens of KB each).
 from __future__ import annotations
 
 import hashlib
+import os
 import sys
 from pathlib import Path
 from types import SimpleNamespace
@@ -192,4 +193,7 @@ def main(reference_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOE_SERVING_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set MOE_SERVING_REFERENCE)")
+    main(root)

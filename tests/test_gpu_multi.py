@@ -149,9 +149,9 @@ def _worker(rank: int, port: int, q):
         from moe_serving_profile_b200.router import Qwen3Router
         rconf = SimpleNamespace(num_experts_per_tok=8, num_experts=128, norm_topk_prob=True,
                                 hidden_size=2048)
-        whole = Qwen3Router(rconf).to(dev)
+        whole = Qwen3Router(rconf, logits="fused").to(dev)
         whole.weight.data = w.router
-        shard = Qwen3Router(rconf).to(dev).shard_over(pg)
+        shard = Qwen3Router(rconf, logits="fused").to(dev).shard_over(pg)
         shard.weight.data = w.router
         xr = S.make_hidden(2048, 2048, seed=9, device=dev)
         a, b = whole(xr), shard(xr)

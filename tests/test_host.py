@@ -137,6 +137,12 @@ def test_w8a8_paths_refuse_before_device_work():
         mods["down_proj"] = qwen3.ExpertProjection(d[e])
     with pytest.raises(ValueError, match="block FP8"):
         m.prepare()
+    # the refusal repeats on every call: nothing was packed or released by the first
+    x, idx, wts = torch.zeros(3, 256, dtype=torch.bfloat16), torch.zeros(3, 2, dtype=torch.int64), torch.zeros(3, 2)
+    for _ in range(2):
+        with pytest.raises(ValueError, match="block FP8"):
+            m(x, idx, wts)
+    assert m.packed is None and m.local is not None
     with pytest.raises(ValueError):
         qwen3.ParallelExperts(SimpleNamespace(num_experts=2, hidden_act="silu"), ParallelGroup(1), "exact")
 

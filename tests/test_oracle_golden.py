@@ -4,7 +4,7 @@ by the reference's own modules (tests/golden/make_golden.py). CPU only."""
 import pytest
 import torch
 
-from tests.conftest import load_golden, tie_free_rows
+from tests.conftest import GOLDEN, load_golden, tie_free_rows
 from moe_serving_profile_b200 import synthetic as S
 from oracle import oracle
 from tests.golden.make_golden import GPT_CASES, QWEN_CASES, checksum, gpt_inputs, qwen_inputs
@@ -119,3 +119,22 @@ def test_synthetic_quantisers_roundtrip():
     b, sc = S.quantize_mxfp4(w)
     dec = oracle.decode_mxfp4(b, sc).float()
     assert float((dec - w).norm() / w.norm()) < 0.15
+
+
+def test_oracle_selection_matches_torch_cuda():
+    """The oracle's top-k (slot order of equal values included) and its
+    butterfly sum reproduce torch's CUDA topk / sum, recorded on a B200 by
+    tests/golden/make_router_golden.py on tie-heavy logits: rows of repeated
+    values, all-equal rows and a coarse value grid."""
+    g = torch.load(GOLDEN / "router_torch_cuda.pt", weights_only=False)
+    for name, c in g["cases"].items():
+        K = c["K"]
+        keys = c["logits"].float() if c["kind"] == "gpt" else c["probs"]
+        idx = oracle.topk(keys, K)
+        assert torch.equal(idx, c["indices"]), name
+        if c["kind"] != "gpt":
+            top = torch.gather(c["probs"], 1, idx)
+            s = oracle.butterfly_sum(top)
+            if K & (K - 1) == 0:   # pinned for powers of two
+                assert torch.equal(s, c["sums"]), name
+                assert torch.equal(top / s[:, None], c["scores"]), name

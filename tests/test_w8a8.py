@@ -86,13 +86,15 @@ def test_act_quant_oracles_agree():
 def test_act_quant_argument_checks():
     L = _lib.lib
     # no rows: nothing to enqueue, no pointer needed
-    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 0, 128, 128, None, None) == _lib.OK
+    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 0, 128, 128, None, None, None, 0, 0) == _lib.OK
     # k_pad not a multiple of 16, k_valid not a multiple of 4, k_valid > k_pad, ldx < k_valid
-    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 4, 128, 120, None, None) == _lib.ERR_INVALID
-    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 4, 126, 128, None, None) == _lib.ERR_INVALID
-    assert L.b200moe_act_quant_fp8(0, None, None, 256, None, 1, 4, 256, 128, None, None) == _lib.ERR_INVALID
-    assert L.b200moe_act_quant_fp8(0, None, None, 64, None, 1, 4, 128, 128, None, None) == _lib.ERR_INVALID
-    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 0, 4, 128, 128, 1, 1) == _lib.ERR_INVALID
+    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 4, 128, 120, None, None, None, 0, 0) == _lib.ERR_INVALID
+    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 4, 126, 128, None, None, None, 0, 0) == _lib.ERR_INVALID
+    assert L.b200moe_act_quant_fp8(0, None, None, 256, None, 1, 4, 256, 128, None, None, None, 0, 0) == _lib.ERR_INVALID
+    assert L.b200moe_act_quant_fp8(0, None, None, 64, None, 1, 4, 128, 128, None, None, None, 0, 0) == _lib.ERR_INVALID
+    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 0, 4, 128, 128, 1, 1, None, 0, 0) == _lib.ERR_INVALID
+    # a row range that runs backwards
+    assert L.b200moe_act_quant_fp8(0, None, None, 128, None, 1, 4, 128, 128, 1, 1, 1, 3, 2) == _lib.ERR_INVALID
 
 
 CASES = [  # rows, k_valid, k_pad, gather divisor (0 = no gather)
