@@ -296,14 +296,16 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   int bn = a->token_tile;
   if (bn == 0) {
     // quantised weights: at most 160 tokens, the largest tile with two
-    // accumulator slots beside the tensor-memory A stages (a 256-token tile
-    // would get one slot, which measured slower)
+    // accumulator slots beside the tensor-memory A stages
     const int max_auto = a->wfmt == B200MOE_W_BF16 ? 256 : 160;
     // 1.5x the mean rows per expert, so that one tile usually holds an
     // expert's rows
     const long long avg = (3ll * a->max_rows + 2ll * a->n_experts - 1) / (2ll * a->n_experts);
     bn = std::min(max_auto, std::max(16, pow2_ceil(static_cast<int>(std::min(avg, 1ll << 20)))));
   }
+  // quantised weights at 256-row tiles: converted weights in shared-memory A
+  // stages (the tensor-memory A stages leave room for one 256-column slot)
+  const bool a_smem = a->wfmt != B200MOE_W_BF16 && bn == 256 && a->b_map == nullptr;
   const int feat_tile = gated ? 64 : 128;
   const int feat_tiles = a->feat_pad / feat_tile;
   const long long tiles_ub =
@@ -328,7 +330,16 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   // columns 256..511, beside the two accumulator slots of at most 128 columns
   // each), nb token-row stages and as many raw stages as fit (even, <= 24).
   int na = 0, nb = 0, nr = 0;
-  if (rpb == 0) {
+  if (a_smem) {
+    // A and token-row stages in step (one commit releases both), then as
+    // many raw stages as fit, at most 8
+    na = nb = 3;
+    const uint32_t fixed = na * a_stage + nb * b_stage + xbytes + barbytes;
+    nr = fixed < budget ? static_cast<int>((budget - fixed) / rpb) : 0;
+    nr = std::min(8, nr);
+    if (nr < 3)
+      return fail(B200MOE_ERR_UNSUPPORTED, "shared memory plan does not fit (token_tile=%d)", bn);
+  } else if (rpb == 0) {
     na = 8;
     nb = 6;
     auto total = [&](int a_, int b_) { return a_ * a_stage + b_ * b_stage + xbytes + barbytes; };
@@ -392,7 +403,7 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.raw_off = off;
   off += nr * rpb;
   p.a_off = off;
-  if (rpb == 0) off += na * a_stage;
+  if (rpb == 0 || a_smem) off += na * a_stage;
   p.b_off = off;
   off += nb * b_stage;
   p.x_off = off;
@@ -406,12 +417,14 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   p.nbanks = std::min(p.nacc, p.nkb);
   // quantised weights keep their A stages in TMEM columns 256..511, so a
   // 256-token tile gets a single accumulator slot
-  p.acc_slots = (rpb && bn > 160) ? 1 : 2;
+  p.acc_slots = (rpb && bn > 160 && !a_smem) ? 1 : 2;
+  p.a_smem = a_smem ? 1 : 0;
   p.joint_ab = na == nb ? 1 : 0;
   // two MMA issuers when there are banks for both and the A / B rings split
   // evenly between them
   p.n_issuers = (p.nacc % 2 == 0 && na % 2 == 0 && nb % 2 == 0) ? 2 : 1;
-  p.tmem_cols = rpb ? 512u : static_cast<uint32_t>(std::max(32, pow2_ceil(p.acc_slots * p.nacc * bn)));
+  p.tmem_cols = (rpb && !a_smem) ? 512u
+                                 : static_cast<uint32_t>(std::max(32, pow2_ceil(p.acc_slots * p.nacc * bn)));
   p.a_col0 = (rpb && bn == 160) ? 320u : 256u;
 
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
@@ -437,7 +450,7 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->k_valid), static_cast<cuuint64_t>(a->b_rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a->ldb) * 2};
-    const cuuint32_t box[2] = {64, a->b_map ? 1u : static_cast<cuuint32_t>(bn)};
+    const cuuint32_t box[2] = {64, a->b_map ? 1u : (a_smem ? 64u : static_cast<cuuint32_t>(bn))};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a->b_src), dims,
                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

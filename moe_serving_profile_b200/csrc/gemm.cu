@@ -76,6 +76,16 @@ struct Ring {
   }
 };
 
+// Rows per token tile of an expert with cnt rows: bn, or (a_smem) the
+// expert's ceil(cnt / bn) tiles cut evenly, rounded up to 16 rows; when the
+// rounding would leave the last tile empty, bn.
+__device__ __forceinline__ int chunk_rows(int cnt, const GemmParams& p) {
+  if (!p.a_smem || cnt <= 0) return p.bn;
+  const int nt = (cnt + p.bn - 1) / p.bn;
+  const int cs = ((cnt + nt - 1) / nt + 15) & ~15;
+  return (nt - 1) * cs < cnt ? cs : p.bn;
+}
+
 // prefix[e] = token tiles of local experts < e (prefix[n_experts] = total).
 __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const GemmParams& p) {
   Tile r;
@@ -90,9 +100,15 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const Gemm
   const int sub = u - prefix[lo];
   const int start = p.offsets[p.expert_begin + lo];
   const int cnt = p.offsets[p.expert_begin + lo + 1] - start;
-  r.row0 = start + sub * p.bn;
-  r.nrows = min(p.bn, cnt - sub * p.bn);
+  const int cs = chunk_rows(cnt, p);
+  r.row0 = start + sub * cs;
+  r.nrows = min(cs, cnt - sub * cs);
   return r;
+}
+
+// MMA N of a tile: its rows rounded up to 16 (a_smem), else the launch's bn.
+__device__ __forceinline__ int tile_n(const Tile& tl, const GemmParams& p) {
+  return p.a_smem ? ((tl.nrows + 15) & ~15) : p.bn;
 }
 
 // 2^(s-127) as the fp32 value torch's ldexp multiplies by (exact, including
@@ -243,8 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 32 * kWarpTma) {
     // quantised weights: a raw stage is drained, and an A stage filled, by
-    // the four warps of one converter group
-    const uint32_t group = p.wfmt == kWBf16 ? 1u : 4u;
+    // the four warps of one converter group (a_smem: by all eight)
+    const uint32_t group = p.wfmt == kWBf16 ? 1u : (p.a_smem ? 8u : 4u);
     for (int i = 0; i < p.nr; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], group);
@@ -327,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const int step = p.n_issuers;
       const int j = warp == kWarpMma ? 0 : 1;
-      const uint32_t idesc = idesc_bf16_f32(128, p.bn);
+      uint32_t idesc = idesc_bf16_f32(128, p.bn);
       Ring ra(p.na / step), rb(p.nb / step);
       int tc = 0;
       int i0 = 0;   // CTA-wide index of the tile's first k-block
@@ -337,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // loop of tile t + 1) or one when a 256-token tile fills them both
         const int slot = p.acc_slots == 2 ? (tc & 1) : 0;
         const uint32_t use = p.acc_slots == 2 ? static_cast<uint32_t>(tc >> 1) : static_cast<uint32_t>(tc);
+        if (p.a_smem) idesc = idesc_bf16_f32(128, tile_n(decode_tile(t, prefix, p), p));
         if (!wait_bounded(&acc_empty[slot], (use & 1u) ^ 1u, p.status)) break;
         tc_fence_after();
         // tile slot `slot` owns accumulator banks slot * nacc .. + nacc - 1.
@@ -365,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           nb_.next();
           const bool more = kb + step < p.nkb;
           const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + sb * p.bn * 128);
-          if (p.wfmt == kWBf16) {
+          if (p.wfmt == kWBf16 || p.a_smem) {
             ready = more && mbar_test_wait(&a_full[j + step * na_.idx], na_.phase) &&
                     mbar_test_wait(&b_full[j + step * nb_.idx], nb_.phase);
             const uint64_t adesc = sdesc_k_sw128(base_u32 + p.a_off + sa * kATile);
@@ -392,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++npend;
           ra.next();
           rb.next();
-          if (npend == 2 || kb + step >= p.nkb) {
+          if (npend == 2 || p.a_smem || kb + step >= p.nkb) {
             umma_commit(&a_empty[pa0]);
             if (npend == 2) umma_commit(&a_empty[pa1]);
             if (!p.joint_ab) {
@@ -448,6 +465,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         uint8_t* dst = sbase + p.b_off + s * p.bn * 128;
+        if (p.a_smem) {
+          // 64-row boxes covering the tile's MMA N (rows past the tile are
+          // read but never stored; past the tensor they are zero-filled)
+          const int nbox = (tile_n(tl, p) + 63) >> 6;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&b_full[s], static_cast<uint32_t>(nbox) * 64u * 128u);
+            for (int j = 0; j < nbox; ++j)
+              tma_load_2d(dst + j * 64 * 128, &bmap, &b_full[s], kb * 64, tl.row0 + j * 64);
+          }
+          __syncwarp();
+          continue;
+        }
         if (lane == 0) mbar_arrive_expect_tx(&b_full[s], p.bn * 128);
         __syncwarp();
         if (p.b_gather) {
@@ -583,6 +612,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[slot]);
+    }
+  } else if (warp >= kWarpConv && p.a_smem) {
+    // ------------------------------------------------ converters (a_smem)
+    // All eight warps convert every k-block: lane l of converter warp c takes
+    // weight row 16 c + l / 2, half h = l & 1 (32 of its 64 values), and
+    // writes the four 16-byte bf16 chunks 4h .. 4h + 3 of that row into the
+    // shared-memory A stage at their 128-byte-swizzle positions (eight
+    // consecutive lanes hit eight distinct 16-byte bank groups, so each
+    // store is four wavefronts). Raw rows are read through the packing's
+    // chunk permutation, also without conflicts.
+    const int row = (warp - kWarpConv) * 16 + (lane >> 1);
+    const int h = lane & 1;
+    const int half = row >> 6;                           // gate/up plane or down half
+    Ring rr(p.nr), ar(p.na);
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      for (int kb = 0; kb < p.nkb; ++kb) {
+        if (!wait_spin(&raw_full[rr.idx], rr.phase, p.status, 32) ||
+            !wait_spin(&a_empty[ar.idx], ar.phase ^ 1u, p.status, 32)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* stage = sbase + p.raw_off + rr.idx * p.stage_bytes;
+        uint32_t o[16];
+        if (p.wfmt == kWFp8) {
+          const uint8_t* raw = stage + row * 64;
+          const float* sc = reinterpret_cast<const float*>(stage + kRawFp8);
+          const int sw = (row >> 1) & 3;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int c = 2 * h + j;
+            const uint4 qv = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
+            const float scale = p.scale_form == kScaleHalf ? sc[half] : sc[row * 4 + c];
+            fp8x16_cvt(qv, scale, *reinterpret_cast<uint32_t(*)[8]>(o + 8 * j));
+          }
+        } else {
+          const uint8_t* raw = stage + row * 32;
+          const int sw = (row >> 2) & 1;
+          const uint32_t sx = *reinterpret_cast<const unsigned short*>(stage + kRawMx + row * 2);
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + ((h ^ sw) << 4));
+          mx32_cvt(qv, (sx >> (8 * h)) & 0xffu, o);
+        }
+        // the raw bytes and scales are in registers: release the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rr.idx]);
+        uint8_t* a = sbase + p.a_off + ar.idx * kATile;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(a + swz(row, 4 * h + j)) =
+              make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[ar.idx]);
+        rr.next();
+        ar.next();
+      }
     }
   } else if (warp >= kWarpConv && p.wfmt != kWBf16) {
     // ------------------------------------------------ converters

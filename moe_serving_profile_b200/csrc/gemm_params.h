@@ -54,6 +54,15 @@ struct GemmParams {
   // uses stage i % na of both, so one commit to a_empty releases both (the
   // token-row producer waits on a_empty; b_empty is unused)
   int joint_ab;
+  // a_smem (quantised weights, token tiles up to 256): the converters write
+  // the bf16 weight tile into shared-memory A stages (128-byte-swizzled
+  // K-major, the layout a TMA SWIZZLE_128B load produces), all eight
+  // converter warps share every k-block, and tensor memory holds two
+  // accumulator slots of bn columns. An expert's rows are cut into
+  // ceil(rows / bn) chunks of equal size (rounded up to 16, the MMA's N
+  // granule), each chunk one tile whose MMA N is its row count rounded up
+  // to 16; token rows arrive as 64-row TMA boxes.
+  int a_smem;
   uint32_t raw_off, a_off, b_off, x_off, bar_off, tmem_cols, a_col0;
 };
 

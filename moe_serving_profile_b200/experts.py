@@ -45,8 +45,10 @@ def tile_policy(T: int, K: int, num_experts: int, max_tile: int = 256, cover: fl
 def _max_tile(w: ExpertWeights) -> int:
     # quantised weights: at most 160 tokens, the largest tile whose two
     # accumulator slots fit beside the converted-weight stages in tensor
-    # memory (a 256-token tile would get a single slot); 160 keeps an expert
-    # with up to 320 rows at two tiles (4096 tokens: 18 % faster than 128)
+    # memory. (256-row tiles exist, with the converted weights in shared
+    # memory instead, but measured no faster: both operands then come from
+    # shared memory, whose operand bandwidth holds a 128 x 256 x 16 MMA to
+    # 171 cycles against 138 with the weights in tensor memory.)
     return 256 if w.fmt == _lib.W_BF16 else 160
 
 

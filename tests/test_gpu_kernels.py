@@ -438,10 +438,12 @@ def test_gated_gemm_integer_exact(cuda, fmt, tile, split):
 
 
 @pytest.mark.parametrize("planes", [1, 2])
-def test_fp8_per_chunk_scales_exact(cuda, planes):
+@pytest.mark.parametrize("tile", [0, 256])
+def test_fp8_per_chunk_scales_exact(cuda, planes, tile):
     """FP8 scale blocks that do not cover whole 64 x 64 halves (32 x 32 here)
     travel as per-(row, 16-column chunk) scales inside each blob; with
-    power-of-two scales every dequantised weight and partial sum is exact."""
+    power-of-two scales every dequantised weight and partial sum is exact.
+    tile 256: contiguous permuted rows through the shared-memory A stages."""
     E, feat, K, T, topk, (br, bc) = 3, 200, 320, 90, 2, (32, 32)
     g, wv, x, idx = _int_case(_lib.W_FP8, E, planes * feat, K, T, topk, seed=31 + planes)
     wv = wv.reshape(E, planes, feat, K)
@@ -457,12 +459,54 @@ def test_fp8_per_chunk_scales_exact(cuda, planes):
     e_of_row = torch.repeat_interleave(torch.arange(E), counts.long())
     xr = x[(perm // topk).long()]
     out = torch.zeros(R, Fp if planes == 2 else feat, dtype=torch.bfloat16, device=cuda)
+    if tile == 256:
+        rows = torch.zeros(R, Kp, dtype=torch.bfloat16)
+        rows[:, :K] = xr.bfloat16()
+        src = dict(b_src=rows.to(cuda), token_tile=256)
+    else:
+        src = dict(b_src=x.bfloat16().to(cuda), b_map=perm.to(cuda), b_div=topk)
     ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R,
                     wfmt=_lib.W_FP8, planes=planes, feat_pad=Fp, n_feat=feat, k_pad=Kp,
-                    weight=blobs.to(cuda), fp8_block=(br, bc),
-                    b_src=x.bfloat16().to(cuda), k_valid=K, b_map=perm.to(cuda), b_div=topk,
-                    epilogue=_lib.EPI_SWIGLU if planes == 2 else _lib.EPI_DOWN, out=out)
+                    weight=blobs.to(cuda), fp8_block=(br, bc), k_valid=K,
+                    epilogue=_lib.EPI_SWIGLU if planes == 2 else _lib.EPI_DOWN, out=out, **src)
     pre = torch.einsum("rk,rpfk->rpf", xr.double(), weff.double()[e_of_row])   # [R, planes, feat]
+    got = out.cpu()[:, :feat]
+    if planes == 1:
+        assert torch.equal(got, pre[:, 0].bfloat16())
+    else:
+        ref = torch.nn.functional.silu(pre[:, 0].bfloat16()) * pre[:, 1].bfloat16()
+        assert float((got != ref).float().mean()) < 1e-3
+        assert float((got.float() - ref.float()).abs().max()) <= float(ref.float().abs().max()) * 2 ** -7
+    _status_clean(cuda)
+
+
+@pytest.mark.parametrize("fmt", [_lib.W_FP8, _lib.W_MXFP4])
+@pytest.mark.parametrize("planes", [1, 2])
+def test_256_row_tiles_cut_evenly_integer_exact(cuda, fmt, planes):
+    """Quantised weights at 256-row token tiles (weights converted into
+    shared-memory operand stages): an expert with more rows than one tile is
+    cut into equal tiles rounded up to 16 rows (700 rows -> 240 + 240 + 220),
+    each tile's MMA N its own row count; other experts get one tile each.
+    Contiguous permuted rows, integer data, exact results."""
+    E, feat, K, T, topk = 4, 200, 320, 700, 2
+    g, wv, x, _ = _int_case(fmt, E, planes * feat, K, T, topk, seed=7 + planes + fmt)
+    # every token routes to expert 0 and one of experts 1..3
+    idx = torch.stack([torch.zeros(T, dtype=torch.long), torch.randint(1, E, (T,), generator=g)], 1)
+    w, Fp = _pack_weight(fmt, wv.reshape(E * planes, feat, K), planes=planes)
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    assert int(counts[0]) == T
+    R = T * topk
+    Kp = -(-K // 64) * 64
+    xr = x[(perm // topk).long()]
+    rows = torch.zeros(R, Kp, dtype=torch.bfloat16)
+    rows[:, :K] = xr.bfloat16()
+    out = torch.zeros(R, Fp if planes == 2 else feat, dtype=torch.bfloat16, device=cuda)
+    ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R, wfmt=fmt,
+                    planes=planes, feat_pad=Fp, n_feat=feat, k_pad=Kp, weight=w.to(cuda),
+                    b_src=rows.to(cuda), k_valid=K,
+                    epilogue=_lib.EPI_SWIGLU if planes == 2 else _lib.EPI_DOWN, out=out, token_tile=256)
+    e_of_row = torch.repeat_interleave(torch.arange(E), counts.long())
+    pre = torch.einsum("rk,rpfk->rpf", xr.double(), wv.reshape(E, planes, feat, K).double()[e_of_row])
     got = out.cpu()[:, :feat]
     if planes == 1:
         assert torch.equal(got, pre[:, 0].bfloat16())
