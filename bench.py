@@ -88,6 +88,13 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, limit_s: float) -> None:
+        """Wait (at most limit_s) until nvidia-smi has printed its first sample:
+        it takes a moment to start, and a short timed region could pass first."""
+        t0 = time.perf_counter()
+        while self.proc is not None and not self.lines and time.perf_counter() - t0 < limit_s:
+            time.sleep(0.05)
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -429,6 +436,118 @@ def stage_breakdown(cfg, router, packed, xs, parallel, rank, world, stream, reps
     return out
 
 
+# --------------------------------------------------------------------------- EP workloads
+# Expert-parallel legs reported beside the headline: (workload, mode). "a2a":
+# token all-to-all (moe.py:110-137), each rank routes its 1/N of the tokens
+# and the rows move over NVLink peer memory (native.PeerCollective);
+# "replicated": every rank routes all tokens, runs its experts and the
+# contribution rows are gathered over NVLink for the ordered global-expert
+# combine (reference numerics, parallel_numerics.py:13-36).
+EP_LEGS = (("qwen3-235b-a22b", "a2a"), ("gpt-oss-120b", "a2a"), ("gpt-oss-120b", "replicated"))
+
+
+def ep_leg(args, name, mode, world, rank, dev, stream, flush, pg):
+    """Tokens/s of one expert-parallel workload over its batches (CUDA-graph
+    replays, L2 flushed before each batch, max over ranks), with each batch
+    checked on every rank against the single-GPU computation of the same
+    tokens (bitwise: the same combine order, expert outputs independent of
+    where they run)."""
+    from moe_serving_profile_b200 import _lib, native, ops
+    from moe_serving_profile_b200 import experts as X
+    cfg = S.CONFIGS[name]
+    E, K, el = cfg.experts, cfg.top_k, cfg.experts // world
+    router, packed = build_layer(cfg, dev, world, rank)
+    _, full = build_layer(cfg, dev, 1, 0) if world > 1 else (None, packed)
+    local = SimpleNamespace(num_experts=el, weights=packed)
+    plan = native.ExpertPlan(E, world, rank)
+    a2a = mode == "a2a"
+    shard = {T: (T // world if a2a else T) for T in cfg.batches}
+    coll = native.PeerCollective(max_tokens=max(shard.values())) if (a2a and world > 1) else native.SingleRank()
+    xs = {}
+    for T in cfg.batches:
+        x = S.make_hidden(T, cfg.hidden, seed=2000 + T, device=dev)
+        xs[T] = x[rank * shard[T]:(rank + 1) * shard[T]].contiguous() if a2a else x
+
+    def call(T):
+        _, scores, idx = router(xs[T])
+        if a2a:
+            return native.routed_forward(xs[T], idx, scores, local, plan, coll)
+        return X.layer_forward(packed, xs[T], idx, scores, num_experts=E, expert_begin=rank * el,
+                               parallel=pg, numerics="reference")
+
+    # parity against one GPU (full layer) on every batch, and the global load cv
+    parity, cvs = {}, {}
+    with torch.cuda.stream(stream):
+        for T in cfg.batches:
+            out = call(T)
+            _, scores, idx = router(xs[T])
+            if a2a:
+                perm = ops.permute(idx, E)
+                y = X.run_experts(full, xs[T], perm, None, K=K, num_experts=E, expert_begin=0)
+                ref = ops.combine(y, perm.inverse, idx, order=_lib.ORDER_RANK_SLOT, experts_per_rank=el,
+                                  weights=scores.to(torch.bfloat16).contiguous())
+            else:
+                ref = X.layer_forward(full, xs[T], idx, scores, num_experts=E, expert_begin=0)
+            d = (out.float() - ref.float())
+            st = torch.tensor([float(d.abs().max()) if d.numel() else 0.0,
+                               float(d.norm() / ref.float().norm().clamp_min(1e-30)) if d.numel() else 0.0,
+                               0.0 if torch.equal(out, ref) else 1.0], device=dev, dtype=torch.float64)
+            counts = torch.bincount(idx.flatten(), minlength=E).to(dev)
+            if world > 1:
+                dist.all_reduce(st, op=dist.ReduceOp.MAX)
+                dist.all_reduce(counts)
+            parity[str(T)] = {"max_abs": float(st[0]), "rel_l2": float(st[1]), "bitwise": bool(st[2] == 0)}
+            cvs[T] = S.expert_load_cv(counts.cpu())
+    del full
+    torch.cuda.synchronize(dev)
+    graphs = {}
+    with torch.cuda.stream(stream):
+        for T in cfg.batches:
+            call(T)
+    torch.cuda.synchronize(dev)
+    for T in cfg.batches:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            call(T)
+        graphs[T] = g
+    if world > 1:
+        dist.barrier()
+    recs = []
+    with torch.cuda.stream(stream):
+        for it in range(max(3, args.warmup) + args.steps):
+            for T in cfg.batches:
+                flush.fill_(T & 0xff)
+                s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_.record(stream)
+                graphs[T].replay()
+                e_.record(stream)
+                if it >= max(3, args.warmup):
+                    recs.append((T, s_, e_))
+    torch.cuda.synchronize(dev)
+    ms = {T: 0.0 for T in cfg.batches}
+    for T, s_, e_ in recs:
+        ms[T] += s_.elapsed_time(e_) / args.steps
+    t = torch.tensor([ms[T] for T in cfg.batches], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = dict(zip(cfg.batches, t.tolist()))
+    for g in graphs.values():
+        del g
+    graphs.clear()
+    torch.cuda.synchronize(dev)
+    if world > 1 and a2a:
+        coll.close()
+    total = sum(ms.values())
+    per_batch = [{"tokens": T, "ms": round(ms[T], 4), "tokens_per_s": round(T / (ms[T] / 1e3), 1),
+                  "expert_load_cv": round(cvs[T], 3),
+                  "tflops": round(S.algorithmic_flops(cfg, T) / (ms[T] / 1e3) / 1e12, 2)}
+                 for T in cfg.batches]
+    return {"workload": name, "mode": mode + (" (NVLink peer memory)" if world > 1 else ""),
+            "value": round(sum(cfg.batches) / (total / 1e3), 1), "unit": "tokens/s",
+            "ms_per_step": round(total, 4), "per_batch": per_batch, "parity": parity,
+            "parity_ok": all(v["bitwise"] for v in parity.values())}
+
+
 def profile_calls(args, cfg):
     """Three eager layer calls per batch size, nothing timed (an ncu target)."""
     from moe_serving_profile_b200 import _lib
@@ -458,6 +577,9 @@ def main():
     ap.add_argument("--workload", default="qwen3-30b-a3b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-w8a8", action="store_true", help="skip the W8A8 (efficient FP8) report")
+    ap.add_argument("--no-ep-legs", action="store_true",
+                    help="skip the expert-parallel workloads (qwen3-235b-a22b all-to-all, gpt-oss-120b "
+                         "all-to-all and replicated-token)")
     ap.add_argument("--profile", action="store_true",
                     help="eager layer calls only (for ncu): 3 calls per --tokens batch")
     ap.add_argument("--tokens", type=int, nargs="*", default=None)
@@ -522,14 +644,21 @@ def main():
 
     per_batch_ms = {T: 0.0 for T in batches}
     with ClockSampler(local) as clocks:
-        # warm-up (at least W steps and ~0.5 s, so the clock sampler sees load)
+        clocks.wait_first(5.0)
+        # warm-up: at least W steps and ~0.5 s, so the clock sampler sees load.
+        # Every rank must replay the same collectives, so the count is agreed
+        # over the group (max) from the time of the first W steps.
         t0 = time.perf_counter()
-        n = 0
-        # (ranks > 1 run a fixed count: every rank must replay the same collectives)
-        while n < max(3, args.warmup) or (world == 1 and time.perf_counter() - t0 < 0.5):
+        for _ in range(max(3, args.warmup)):
             step(False)
-            torch.cuda.synchronize(dev)
-            n += 1
+        torch.cuda.synchronize(dev)
+        per = (time.perf_counter() - t0) / max(3, args.warmup)
+        extra = torch.tensor([max(0, math.ceil((0.5 - (time.perf_counter() - t0)) / max(per, 1e-6)))],
+                             device=dev, dtype=torch.int64)
+        if world > 1:
+            dist.all_reduce(extra, op=dist.ReduceOp.MAX)
+        for _ in range(int(extra)):
+            step(False)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
@@ -660,6 +789,15 @@ def main():
 
     stages = stage_breakdown(cfg, router, packed, xs, parallel, rank, world, stream)
 
+    legs = []
+    if not args.no_ep_legs:
+        for name, mode in EP_LEGS:
+            pg = ParallelGroup(world) if (world > 1 and mode == "replicated") else None
+            legs.append(ep_leg(args, name, mode, world, rank, dev, stream, flush, pg))
+            if pg is not None:
+                pg.close()   # its NVLink gather buffers (collective)
+            torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, _, sample = cpu_batches(cfg, budget_s=25.0)
@@ -686,6 +824,8 @@ def main():
             line["w8a8"] = w8a8
         if parity is not None:
             line["parity"] = parity
+        if legs:
+            line["ep_workloads"] = legs
         print(json.dumps(line), flush=True)
     for g in graphs.values():
         del g

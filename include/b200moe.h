@@ -369,6 +369,72 @@ int b200moe_a2a_recv_plan(int device, void* stream, const int* counts, int ep,
                           int experts_per_rank, int rows, int* offsets, int* map_in,
                           int* map_back);
 
+/* ------------------------------------------------------------ peer-memory row exchanges
+ * The token all-to-all of moe_serving/moe.py:110-137 (replacing the three
+ * ProcessGroupCollective.exchange calls of distributed.py:33-46, each an
+ * NCCL count exchange, a host read of the split sizes and an
+ * all_to_all_single) and the replicated-token exact gather of
+ * moe_serving/parallel_numerics.py:13-36 (every expert's contribution rows on
+ * every rank), over NVLink peer memory.
+ *
+ * Every rank of the group owns one buffer of b200moe_peer_rows_bytes(H,
+ * cap_a, cap_b) bytes from b200moe_p2p_alloc (zeroed), exported and imported
+ * with b200moe_p2p_export / b200moe_p2p_import like the combine buffers;
+ * peers[world] are the buffers' addresses in this process, peers[rank] the
+ * local one. A buffer is a 64 KB header (flags, the count board, placements),
+ * area A [cap_a][H] bf16 at byte offset 65536 and area B [cap_b][H] bf16
+ * after it. All ranks call the same sequence of functions with the same E,
+ * H, world and caps; each waits (bounded, timeout_ns, 0: 2 s) for the other
+ * ranks of its phase and sets B200MOE_STATUS_PEER_TIMEOUT when one does not
+ * arrive. A row that would fall outside an area is skipped and sets
+ * B200MOE_STATUS_BAD_TILE. world <= 8, E <= 1024, E % world == 0, H % 8 == 0.
+ *
+ * Token all-to-all, per layer call (rank r holds its own tokens):
+ *   b200moe_a2a_counts    counts: int32 [E], this rank's rows per global
+ *                         expert (b200moe_permute's counts). Exchanges them
+ *                         with every rank and writes recv_offsets (int32
+ *                         [E / world + 1], device): the receive-area segment
+ *                         starts of this rank's experts. Area A of rank d will
+ *                         hold d's experts' rows in (expert, source rank,
+ *                         source's permuted order) order; cap_a bounds the
+ *                         received rows (world * max tokens per rank * K),
+ *                         cap_b this rank's own rows (tokens * K).
+ *   b200moe_a2a_dispatch  pushes row j of this rank's permutation (hidden row
+ *                         perm_src[j] / K, expert indices[perm_src[j]]) into
+ *                         its owner's area A; returns once every rank's rows
+ *                         for this rank have landed. The grouped GEMMs then
+ *                         read area A in place with recv_offsets.
+ *   b200moe_a2a_return    y: [cap_a][ldy] bf16, the expert outputs in receive
+ *                         order; pushes every row back to its source's area B
+ *                         at the source's own permuted position, and returns
+ *                         once this rank's rows have all come back. Area B
+ *                         rows [0, T * K) are then the returned rows in this
+ *                         rank's permuted order (combine them with
+ *                         b200moe_combine, order RANK_SLOT, as moe.py:134-136
+ *                         adds them).
+ * Replicated-token exact gather:
+ *   b200moe_ep_gather     rows [offsets[expert_lo], offsets[expert_hi]) of
+ *                         this rank's area A (its experts' contribution rows,
+ *                         written there by the down GEMM) are copied to the
+ *                         same rows of every other rank's area A; returns once
+ *                         every rank's rows have landed here, so area A holds
+ *                         all rows_total rows for the ordered combine.
+ */
+size_t b200moe_peer_rows_bytes(int H, long long cap_a, long long cap_b);
+int b200moe_a2a_counts(int device, void* stream, void* const* peers, int world, int rank, int E,
+                       const int* counts, int* recv_offsets, long long cap_a, long long cap_b,
+                       unsigned long long timeout_ns);
+int b200moe_a2a_dispatch(int device, void* stream, void* const* peers, int world, int rank, int E,
+                         const void* hidden, long long ldh, int H, const long long* indices,
+                         const int* perm_src, const int* offsets, int rows, int K,
+                         long long cap_a, unsigned long long timeout_ns);
+int b200moe_a2a_return(int device, void* stream, void* const* peers, int world, int rank, int E,
+                       const void* y, long long ldy, int H, long long cap_a, long long cap_b,
+                       unsigned long long timeout_ns);
+int b200moe_ep_gather(int device, void* stream, void* const* peers, int world, int rank, int H,
+                      const int* offsets, int expert_lo, int expert_hi, int rows_total,
+                      long long cap_a, unsigned long long timeout_ns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,6 +48,11 @@ EXPORTED = (
     "b200moe_p2p_import",
     "b200moe_p2p_close",
     "b200moe_combine_allreduce",
+    "b200moe_peer_rows_bytes",
+    "b200moe_a2a_counts",
+    "b200moe_a2a_dispatch",
+    "b200moe_a2a_return",
+    "b200moe_ep_gather",
 )
 
 
@@ -161,6 +166,28 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_gather_rows_range.argtypes = [
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int, c_int, c_void_p,
         c_longlong, c_void_p, c_int, c_int,
+    ]
+    lib.b200moe_peer_rows_bytes.restype = c_size_t
+    lib.b200moe_peer_rows_bytes.argtypes = [c_int, c_longlong, c_longlong]
+    lib.b200moe_a2a_counts.restype = c_int
+    lib.b200moe_a2a_counts.argtypes = [
+        c_int, c_void_p, POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_void_p, c_longlong,
+        c_longlong, ctypes.c_ulonglong,
+    ]
+    lib.b200moe_a2a_dispatch.restype = c_int
+    lib.b200moe_a2a_dispatch.argtypes = [
+        c_int, c_void_p, POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_longlong, c_int,
+        c_void_p, c_void_p, c_void_p, c_int, c_int, c_longlong, ctypes.c_ulonglong,
+    ]
+    lib.b200moe_a2a_return.restype = c_int
+    lib.b200moe_a2a_return.argtypes = [
+        c_int, c_void_p, POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_longlong, c_int,
+        c_longlong, c_longlong, ctypes.c_ulonglong,
+    ]
+    lib.b200moe_ep_gather.restype = c_int
+    lib.b200moe_ep_gather.argtypes = [
+        c_int, c_void_p, POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_int, c_int, c_int,
+        c_longlong, ctypes.c_ulonglong,
     ]
     lib.b200moe_a2a_recv_plan.restype = c_int
     lib.b200moe_a2a_recv_plan.argtypes = [

@@ -735,6 +735,100 @@ int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_
   return B200MOE_OK;
 }
 
+// ---------------------------------------------------------------- peer-memory row exchanges
+size_t b200moe_peer_rows_bytes(int H, long long cap_a, long long cap_b) {
+  if (H < 8 || cap_a < 0 || cap_b < 0) return 0;
+  return b200::kPeerRowsHeaderBytes + static_cast<size_t>(cap_a + cap_b) * static_cast<size_t>(H) * 2ull;
+}
+
+static int check_peers(void* const* peers, int world, int rank) {
+  if (world < 1 || world > b200::kP2PMaxRanks)
+    return fail(B200MOE_ERR_UNSUPPORTED, "peer exchanges support 1..%d ranks", b200::kP2PMaxRanks);
+  B200_CHECK(rank >= 0 && rank < world, "rank %d outside [0, %d)", rank, world);
+  B200_CHECK(peers != nullptr, "peers are required");
+  for (int i = 0; i < world; ++i)
+    B200_CHECK(peers[i] != nullptr && aligned16(peers[i]), "peer buffer %d missing or unaligned", i);
+  return B200MOE_OK;
+}
+
+int b200moe_a2a_counts(int device, void* stream, void* const* peers, int world, int rank, int E,
+                       const int* counts, int* recv_offsets, long long cap_a, long long cap_b,
+                       unsigned long long timeout_ns) {
+  int rc = check_peers(peers, world, rank);
+  if (rc) return rc;
+  B200_CHECK(E >= 1 && cap_a >= 0 && cap_b >= 0, "bad sizes");
+  if (E > 1024 || E % world != 0)
+    return fail(B200MOE_ERR_UNSUPPORTED, "the all-to-all needs E <= 1024 and E %% world == 0");
+  B200_CHECK(counts != nullptr, "counts are required");
+  int* sp = nullptr;
+  rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_a2a_counts(static_cast<cudaStream_t>(stream), peers, world, rank, E, counts,
+                                    recv_offsets, cap_a, cap_b,
+                                    timeout_ns ? timeout_ns : b200::kWaitLimitNs, sp));
+  return B200MOE_OK;
+}
+
+int b200moe_a2a_dispatch(int device, void* stream, void* const* peers, int world, int rank, int E,
+                         const void* hidden, long long ldh, int H, const long long* indices,
+                         const int* perm_src, const int* offsets, int rows, int K,
+                         long long cap_a, unsigned long long timeout_ns) {
+  int rc = check_peers(peers, world, rank);
+  if (rc) return rc;
+  B200_CHECK(E >= 1 && rows >= 0 && K >= 1 && cap_a >= 0, "bad sizes");
+  if (E > 1024 || E % world != 0 || H % 8 != 0 || H < 8)
+    return fail(B200MOE_ERR_UNSUPPORTED, "the all-to-all needs E <= 1024, E %% world == 0, H %% 8 == 0");
+  B200_CHECK(offsets != nullptr, "offsets are required");
+  if (rows > 0) {
+    B200_CHECK(hidden && indices && perm_src, "hidden, indices and perm_src are required");
+    B200_CHECK(aligned16(hidden) && ldh % 8 == 0 && ldh >= H, "hidden rows must be 16-byte aligned");
+  }
+  int* sp = nullptr;
+  rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_a2a_dispatch(static_cast<cudaStream_t>(stream), peers, world, rank, E, hidden,
+                                      ldh, H, indices, perm_src, offsets, rows, K, cap_a,
+                                      g_sm_count[device], timeout_ns ? timeout_ns : b200::kWaitLimitNs,
+                                      sp));
+  return B200MOE_OK;
+}
+
+int b200moe_a2a_return(int device, void* stream, void* const* peers, int world, int rank, int E,
+                       const void* y, long long ldy, int H, long long cap_a, long long cap_b,
+                       unsigned long long timeout_ns) {
+  int rc = check_peers(peers, world, rank);
+  if (rc) return rc;
+  B200_CHECK(E >= 1 && cap_a >= 0 && cap_b >= 0, "bad sizes");
+  if (E > 1024 || E % world != 0 || H % 8 != 0 || H < 8)
+    return fail(B200MOE_ERR_UNSUPPORTED, "the all-to-all needs E <= 1024, E %% world == 0, H %% 8 == 0");
+  if (cap_a > 0) B200_CHECK(y && aligned16(y) && ldy % 8 == 0 && ldy >= H, "y rows must be 16-byte aligned");
+  int* sp = nullptr;
+  rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_a2a_return(static_cast<cudaStream_t>(stream), peers, world, rank, E, y, ldy, H,
+                                    cap_a, cap_b, g_sm_count[device],
+                                    timeout_ns ? timeout_ns : b200::kWaitLimitNs, sp));
+  return B200MOE_OK;
+}
+
+int b200moe_ep_gather(int device, void* stream, void* const* peers, int world, int rank, int H,
+                      const int* offsets, int expert_lo, int expert_hi, int rows_total,
+                      long long cap_a, unsigned long long timeout_ns) {
+  int rc = check_peers(peers, world, rank);
+  if (rc) return rc;
+  B200_CHECK(expert_lo >= 0 && expert_hi >= expert_lo && rows_total >= 0 && cap_a >= 0, "bad sizes");
+  if (H % 8 != 0 || H < 8) return fail(B200MOE_ERR_UNSUPPORTED, "the gather needs H %% 8 == 0");
+  B200_CHECK(offsets != nullptr, "offsets are required");
+  B200_CHECK(rows_total <= cap_a, "rows_total %d exceeds area A's %lld rows", rows_total, cap_a);
+  int* sp = nullptr;
+  rc = use_device(device, &sp);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_ep_gather(static_cast<cudaStream_t>(stream), peers, world, rank, H, offsets,
+                                   expert_lo, expert_hi, rows_total, cap_a, g_sm_count[device],
+                                   timeout_ns ? timeout_ns : b200::kWaitLimitNs, sp));
+  return B200MOE_OK;
+}
+
 int b200moe_a2a_recv_plan(int device, void* stream, const int* counts, int ep,
                           int experts_per_rank, int rows, int* offsets, int* map_in,
                           int* map_back) {

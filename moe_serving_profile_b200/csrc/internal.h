@@ -97,6 +97,37 @@ cudaError_t launch_combine_allreduce(cudaStream_t st, const void* rows, long lon
                                      void* const* peers, int t_cap, void* out, long long ld_out,
                                      unsigned long long timeout_ns, int* status);
 
+// Row-exchange buffer of the peer-memory all-to-all and gather (a2a_p2p.cu):
+// this header, then area A [cap_a][H] bf16 and area B [cap_b][H] bf16.
+struct PeerRowsHeader {
+  uint32_t flags[5][kP2PMaxRanks];   // [phase][source]: epoch of the source's last signal
+  uint32_t a2a_epoch, gather_epoch, ctr_dispatch, ctr_return, ctr_gather;
+  int recv_total;                    // rows received by the last all-to-all
+  uint32_t pad[18];
+  int board[kP2PMaxRanks][1024];     // [source][expert]: row counts of the last all-to-all
+  int dst_base[1024];                // [expert]: first row of my rows of it in its owner's area A
+  int seg_start[1025];               // [my expert * world + source]: first receive row
+  int ret_base[1024];                // [my expert * world + source]: source's permuted offset
+  int recv_offsets[1025];            // [my expert]: first receive row (expert-major)
+};
+constexpr size_t kPeerRowsHeaderBytes = 65536;
+static_assert(sizeof(PeerRowsHeader) <= kPeerRowsHeaderBytes, "peer rows header");
+
+cudaError_t launch_a2a_counts(cudaStream_t st, void* const* peers, int world, int rank, int E,
+                              const int* counts, int* recv_offsets, long long cap_a, long long cap_b,
+                              unsigned long long timeout_ns, int* status);
+cudaError_t launch_a2a_dispatch(cudaStream_t st, void* const* peers, int world, int rank, int E,
+                                const void* hidden, long long ldh, int H, const long long* indices,
+                                const int* perm_src, const int* offsets, int rows_cap, int K,
+                                long long cap_a, int sm_count, unsigned long long timeout_ns,
+                                int* status);
+cudaError_t launch_a2a_return(cudaStream_t st, void* const* peers, int world, int rank, int E,
+                              const void* y, long long ldy, int H, long long cap_a, long long cap_b,
+                              int sm_count, unsigned long long timeout_ns, int* status);
+cudaError_t launch_ep_gather(cudaStream_t st, void* const* peers, int world, int rank, int H,
+                             const int* offsets, int lo, int hi, long long rows_cap, long long cap_a,
+                             int sm_count, unsigned long long timeout_ns, int* status);
+
 cudaError_t launch_gather_rows_range(cudaStream_t st, const void* src, long long ld_src,
                                      const int* map, int div, int n, int H, void* dst,
                                      long long ld_dst, const int* offsets, int expert_lo,

@@ -207,6 +207,16 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
                               expert_begin=expert_begin)
         return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
     if numerics == "reference":
+        g = parallel.gather_rows_buffer(hidden.device, hidden.shape[1], T * K)
+        if g is not None:
+            # The down GEMM writes this rank's experts' rows into its gather
+            # area; every rank copies them to the same rows of the others'
+            # areas over NVLink, then combines all rows in global expert order.
+            contrib = g.area_a[:T * K]
+            run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
+                        expert_begin=expert_begin, contrib=contrib)
+            ops.ep_gather(g, perm.offsets, expert_begin, expert_begin + w.n_experts, T * K)
+            return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
         # Rows of other ranks' experts start at zero, so a SUM all-reduce is an
         # exact gather of every expert's contribution rows.
         contrib = torch.zeros(T * K, hidden.shape[1], device=hidden.device, dtype=torch.bfloat16)

@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 from moe_serving_profile_b200 import _lib, ops
-from moe_serving_profile_b200.experts import check_inputs, run_experts, tile_policy
+from moe_serving_profile_b200.experts import _max_tile, check_inputs, run_experts, tile_policy
 from moe_serving_profile_b200.layout import bf16_experts
 from moe_serving_profile_b200.router import native_route
 
@@ -80,6 +80,46 @@ class ProcessGroupCollective(Collective):
         dist.all_to_all_single(out, rows.contiguous(), output_split_sizes=recv_list,
                                input_split_sizes=send_list, group=self.group)
         return out, recv_out
+
+
+class PeerCollective(ProcessGroupCollective):
+    """ProcessGroupCollective whose ``routed_forward`` exchange runs over
+    NVLink peer memory (b200moe_a2a_counts / dispatch / return): counts, rows
+    out and rows back each move in one kernel with no host read, the rows
+    landing in the receiver's expert-major order. ``max_tokens`` bounds the
+    tokens any rank routes in one call (the buffers hold world x max_tokens x
+    top-k received rows per rank). ``exchange`` is inherited (NCCL)."""
+
+    def __init__(self, group=None, max_tokens: int = 8192, timeout_ns: int = 0):
+        super().__init__(group)
+        self.max_tokens = max_tokens
+        self.timeout_ns = timeout_ns
+        self.rank = dist.get_rank(group)
+        self._rows = None
+
+    def peer_rows(self, device: torch.device, hidden: int, top_k: int):
+        """The exchange buffers for (hidden, top_k), created collectively by
+        the first eager call (not under CUDA graph capture)."""
+        from moe_serving_profile_b200.parallel import PeerRows
+        b = self._rows
+        if b is None or b.hidden != hidden or b.top_k != top_k or b.device != device:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the NVLink exchange buffers are created by an eager call "
+                                   "before CUDA graph capture")
+            if b is not None:
+                b.close()
+            cap_b = self.max_tokens * top_k
+            b = PeerRows(self.group, self.rank, self.world_size, device, hidden,
+                         self.world_size * cap_b, cap_b, self.timeout_ns)
+            b.top_k = top_k
+            self._rows = b
+        return b
+
+    def close(self) -> None:
+        """Release the exchange buffers (collective)."""
+        if self._rows is not None:
+            self._rows.close()
+            self._rows = None
 
 
 def exchange_inplace(payloads: list[torch.Tensor], splits: list) -> list[tuple[torch.Tensor, torch.Tensor]]:
@@ -259,6 +299,48 @@ def _combine(send: _Send, returned: torch.Tensor, experts_per_rank: int) -> torc
                        experts_per_rank=experts_per_rank, weights=send.weight)
 
 
+def run_experts_received(w, rows: torch.Tensor, offsets: torch.Tensor, *, tile_tokens: int, K: int,
+                         num_experts: int) -> torch.Tensor:
+    """Expert outputs y = down(SwiGLU(gate/up(row))) (no routing weight) of
+    rows already in expert-major order, ``offsets`` (device, int32 [local
+    experts + 1]) their segments; every row of ``rows`` is an upper bound.
+    The token tile follows the global batch (``tile_tokens`` tokens routed
+    to ``num_experts`` experts, ``K`` each), as on one GPU."""
+    R = rows.shape[0]
+    bn = tile_policy(tile_tokens, K, num_experts, _max_tile(w))
+    act = torch.empty(R, w.i_pad, device=rows.device, dtype=torch.bfloat16)
+    ops.expert_gemm(offsets=offsets, expert_begin=0, n_experts=w.n_experts, max_rows=R, wfmt=w.fmt,
+                    planes=2, feat_pad=w.i_pad, n_feat=w.inter, k_pad=w.h_k, weight=w.w1,
+                    fp8_block=w.block, b_src=rows, k_valid=rows.shape[1], epilogue=w.gated_epilogue,
+                    bias=w.b1, alpha=w.alpha, limit=w.limit, out=act, token_tile=bn)
+    y = torch.empty(R, w.hidden, device=rows.device, dtype=torch.bfloat16)
+    ops.expert_gemm(offsets=offsets, expert_begin=0, n_experts=w.n_experts, max_rows=R, wfmt=w.fmt,
+                    planes=1, feat_pad=w.h_f, n_feat=w.hidden, k_pad=w.i_pad, weight=w.w2,
+                    fp8_block=w.block, b_src=act, k_valid=w.inter, epilogue=_lib.EPI_DOWN, bias=w.b2,
+                    out=y, token_tile=bn)
+    return y
+
+
+def _routed_forward_peer(hidden, index, weight, w, plan: ExpertPlan, collective: PeerCollective):
+    """routed_forward over NVLink peer memory: count exchange, dispatch into
+    the owners' receive areas, grouped GEMMs in place, return into the
+    sources' areas, combine in (rank, slot) order."""
+    T, K = index.shape
+    if T > collective.max_tokens:
+        raise ValueError(f"{T} tokens exceed the exchange buffers' {collective.max_tokens}")
+    E, el = plan.num_experts, plan.experts_per_rank
+    buf = collective.peer_rows(hidden.device, hidden.shape[1], K)
+    perm = ops.permute(index, E)
+    recv_offsets = torch.empty(el + 1, device=hidden.device, dtype=torch.int32)
+    ops.a2a_counts(buf, perm.counts, recv_offsets, E)
+    ops.a2a_dispatch(buf, hidden, index, perm, E)
+    y = run_experts_received(w, buf.area_a, recv_offsets, tile_tokens=T * plan.ep_size, K=K,
+                             num_experts=E)
+    ops.a2a_return(buf, y, E)
+    return ops.combine(buf.area_b[:T * K], perm.inverse, index, order=_lib.ORDER_RANK_SLOT,
+                       experts_per_rank=el, weights=weight.to(hidden.dtype).contiguous())
+
+
 def routed_forward(hidden: torch.Tensor, expert_index: torch.Tensor, expert_weight: torch.Tensor,
                    experts: LocalSwiGLUExperts, plan: ExpertPlan, collective: Collective) -> torch.Tensor:
     """Dispatch local tokens, run the owned experts, combine (moe_serving/moe.py:110-137)."""
@@ -267,6 +349,10 @@ def routed_forward(hidden: torch.Tensor, expert_index: torch.Tensor, expert_weig
     if experts.num_experts != plan.experts_per_rank:
         raise ValueError(f"rank holds {experts.num_experts} experts, plan expects {plan.experts_per_rank}")
     ep, el = plan.ep_size, plan.experts_per_rank
+    if ep > 1 and isinstance(collective, PeerCollective) and hidden.is_cuda:
+        # every rank takes part in each exchange, also with no tokens
+        h, idx, wt = check_inputs(hidden, expert_index, expert_weight)
+        return _routed_forward_peer(h, idx, wt, experts.weights, plan, collective)
     send = _prepare(hidden, expert_index, expert_weight, plan.num_experts)
     if ep == 1:
         # no exchange: the experts read the tokens through the permutation

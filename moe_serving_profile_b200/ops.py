@@ -349,6 +349,57 @@ def combine_allreduce(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.
     return out
 
 
+# --------------------------------------------------------------------------- peer-memory row exchanges
+def _peer_array(buf):
+    return (ctypes.c_void_p * len(buf.peers))(*buf.peers)
+
+
+def a2a_counts(buf, counts: torch.Tensor, recv_offsets: torch.Tensor, E: int) -> torch.Tensor:
+    """Exchange this rank's per-expert row counts (int32 [E]) with every rank
+    of ``buf`` (a parallel.PeerRows) and write the receive segments of this
+    rank's experts into ``recv_offsets`` (int32 [E / world + 1])."""
+    device = _dev(counts, "counts")
+    if counts.dtype != torch.int32 or counts.numel() != E or not counts.is_contiguous():
+        raise ValueError(f"counts must be contiguous int32 [{E}]")
+    if recv_offsets.dtype != torch.int32 or recv_offsets.numel() != E // buf.world + 1:
+        raise ValueError(f"recv_offsets must be int32 [{E // buf.world + 1}]")
+    check(lib.b200moe_a2a_counts(device, _stream(device), _peer_array(buf), buf.world, buf.rank, E,
+                                 _ptr(counts), _ptr(recv_offsets), buf.cap_a, buf.cap_b,
+                                 buf.timeout_ns), "a2a_counts")
+    return recv_offsets
+
+
+def a2a_dispatch(buf, hidden: torch.Tensor, indices: torch.Tensor, perm: "Permutation", E: int) -> None:
+    """Push every routed row of this rank into its expert owner's receive area."""
+    device = _dev(hidden, "hidden")
+    _bf16_rows(hidden, "hidden")
+    T, K = indices.shape
+    if indices.dtype != torch.int64 or not indices.is_contiguous():
+        raise ValueError("indices must be contiguous int64")
+    check(lib.b200moe_a2a_dispatch(device, _stream(device), _peer_array(buf), buf.world, buf.rank, E,
+                                   _ptr(hidden), hidden.stride(0), hidden.shape[1], _ptr(indices),
+                                   _ptr(perm.perm_src), _ptr(perm.offsets), T * K, K, buf.cap_a,
+                                   buf.timeout_ns), "a2a_dispatch")
+
+
+def a2a_return(buf, y: torch.Tensor, E: int) -> None:
+    """Push every computed row (receive order, [cap_a, H]) back to its source."""
+    device = _dev(y, "y")
+    _bf16_rows(y, "y")
+    check(lib.b200moe_a2a_return(device, _stream(device), _peer_array(buf), buf.world, buf.rank, E,
+                                 _ptr(y), y.stride(0), y.shape[1], buf.cap_a, buf.cap_b,
+                                 buf.timeout_ns), "a2a_return")
+
+
+def ep_gather(buf, offsets: torch.Tensor, expert_lo: int, expert_hi: int, rows_total: int) -> None:
+    """Copy rows [offsets[expert_lo], offsets[expert_hi]) of this rank's area A
+    to the same rows of every other rank's area A."""
+    device = _dev(offsets, "offsets")
+    check(lib.b200moe_ep_gather(device, _stream(device), _peer_array(buf), buf.world, buf.rank,
+                                buf.hidden, _ptr(offsets), expert_lo, expert_hi, rows_total,
+                                buf.cap_a, buf.timeout_ns), "ep_gather")
+
+
 def gather_rows(src: torch.Tensor, index_map: torch.Tensor, div: int = 1,
                 out: torch.Tensor | None = None, offsets: torch.Tensor | None = None,
                 expert_lo: int = 0, expert_hi: int = 0) -> torch.Tensor:

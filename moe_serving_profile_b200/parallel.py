@@ -21,20 +21,16 @@ P2P_MAX_ROWS = 8192
 P2P_ONE_SHOT_BYTES = 16 << 20
 
 
-class PeerExchange:
-    """Exchange buffers of the fused combine + all-reduce
-    (b200moe_combine_allreduce): one cudaMalloc'd buffer per rank of an
-    expert-parallel group, mapped into the other ranks with CUDA IPC (plain
-    peer loads and stores over NVLink). Created collectively, outside CUDA
-    graph capture; ``close`` is collective too."""
+class _IpcBuffers:
+    """One cudaMalloc'd buffer per rank of a group, mapped into the other
+    ranks with CUDA IPC (plain peer loads and stores over NVLink). Created
+    collectively, outside CUDA graph capture; ``close`` is collective too."""
 
-    def __init__(self, group, rank: int, size: int, device: torch.device, t_cap: int, hidden: int):
+    def __init__(self, group, rank: int, size: int, device: torch.device, nbytes: int):
         from moe_serving_profile_b200._lib import check, lib
 
-        self.group, self.rank, self.size = group, rank, size
-        self.device, self.t_cap, self.hidden = device, t_cap, hidden
+        self.group, self.rank, self.size, self.device = group, rank, size, device
         dev = device.index
-        nbytes = lib.b200moe_p2p_buffer_bytes(t_cap, hidden, size)
         ptr = ctypes.c_void_p()
         check(lib.b200moe_p2p_alloc(dev, nbytes, ctypes.byref(ptr)), "p2p_alloc")
         self.local = ptr.value
@@ -67,6 +63,53 @@ class PeerExchange:
         self.peers = None
 
 
+class PeerExchange(_IpcBuffers):
+    """Exchange buffers of the fused combine + all-reduce
+    (b200moe_combine_allreduce)."""
+
+    def __init__(self, group, rank: int, size: int, device: torch.device, t_cap: int, hidden: int):
+        from moe_serving_profile_b200._lib import lib
+
+        self.t_cap, self.hidden = t_cap, hidden
+        super().__init__(group, rank, size, device, lib.b200moe_p2p_buffer_bytes(t_cap, hidden, size))
+
+
+class _DeviceRows:
+    """A device address range seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, rows: int, cols: int):
+        self.__cuda_array_interface__ = {"shape": (rows, cols), "typestr": "<i2",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+PEER_ROWS_HEADER_BYTES = 65536   # b200moe_peer_rows_bytes's header (include/b200moe.h)
+
+
+class PeerRows(_IpcBuffers):
+    """Row-exchange buffers of the peer-memory token all-to-all and the
+    replicated-token exact gather (b200moe_a2a_* / b200moe_ep_gather): per
+    rank a header, area A [cap_a, hidden] (received / gathered rows) and
+    area B [cap_b, hidden] (returned rows), both exposed as bf16 tensors that
+    alias the buffer (valid until ``close``)."""
+
+    def __init__(self, group, rank: int, size: int, device: torch.device, hidden: int, cap_a: int,
+                 cap_b: int, timeout_ns: int = 0):
+        from moe_serving_profile_b200._lib import lib
+
+        self.world, self.hidden, self.cap_a, self.cap_b = size, hidden, cap_a, cap_b
+        self.timeout_ns = timeout_ns
+        super().__init__(group, rank, size, device, lib.b200moe_peer_rows_bytes(hidden, cap_a, cap_b))
+        base = self.local + PEER_ROWS_HEADER_BYTES
+        with torch.cuda.device(device):
+            self.area_a = torch.as_tensor(_DeviceRows(base, cap_a, hidden), device=device).view(torch.bfloat16)
+            self.area_b = torch.as_tensor(_DeviceRows(base + cap_a * hidden * 2, cap_b, hidden),
+                                          device=device).view(torch.bfloat16)
+
+    def close(self) -> None:
+        self.area_a = self.area_b = None
+        super().close()
+
+
 class ParallelGroup:
     def __init__(self, size: int):
         world = dist.get_world_size() if dist.is_initialized() else 1
@@ -78,6 +121,7 @@ class ParallelGroup:
         self.start_rank = grank - self.rank
         self.group = None
         self._exchange = None
+        self._gather = None
         if size > 1:
             for first in range(0, world, size):
                 g = dist.new_group(list(range(first, first + size)))
@@ -108,6 +152,26 @@ class ParallelGroup:
                               expert_lo=expert_lo, expert_hi=expert_hi, weights=weights)
         return self.reduce(partial)
 
+    def gather_rows_buffer(self, device: torch.device, hidden: int, rows: int):
+        """This rank's exact-gather buffers (a PeerRows for b200moe_ep_gather)
+        when ``rows`` contribution rows fit them and the NVLink path is on,
+        else None. They hold P2P_MAX_ROWS tokens x 8 slots of rows."""
+        if (self.size == 1 or self.size > 8 or device.type != "cuda"
+                or os.environ.get("B200MOE_P2P", "1") == "0"):
+            return None
+        cap = P2P_MAX_ROWS * 8
+        if rows > cap:
+            return None
+        g = self._gather
+        if g is None or g.hidden != hidden or g.device != device:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the NVLink exchange buffers are created by an eager call "
+                                   "before CUDA graph capture")
+            if g is not None:
+                g.close()
+            g = self._gather = PeerRows(self.group, self.rank, self.size, device, hidden, cap, 0)
+        return g
+
     def _peer_exchange(self, device: torch.device, hidden: int, T: int):
         if (self.size == 1 or self.size > 8 or device.type != "cuda"
                 or os.environ.get("B200MOE_P2P", "1") == "0"):
@@ -132,6 +196,9 @@ class ParallelGroup:
         if self._exchange is not None:
             self._exchange.close()
             self._exchange = None
+        if self._gather is not None:
+            self._gather.close()
+            self._gather = None
 
     def broadcast(self, tensor: torch.Tensor, owner: int = 0) -> torch.Tensor:
         if self.size > 1:

@@ -4,9 +4,13 @@
   reference's --ep-size layout): with numerics="reference" the output on
   every rank equals the one-GPU layer bit for bit; numerics="fast" stays
   within the BF16 layer tolerance;
-* token all-to-all (native.routed_forward with ProcessGroupCollective): each
-  rank's output equals native.simulate_routed (all ranks in one process, the
-  same kernels) bit for bit;
+* replicated-token EP with numerics="reference" runs the exact NVLink gather
+  of contribution rows (b200moe_ep_gather) and must equal the one-GPU layer
+  on two calls in a row;
+* token all-to-all (native.routed_forward with ProcessGroupCollective, NCCL,
+  and with PeerCollective, NVLink peer memory, eager and in CUDA graph
+  replays): each rank's output equals native.simulate_routed (all ranks in
+  one process, the same kernels) bit for bit;
 * the fused NVLink combine + all-reduce (ParallelGroup.combine_reduce) equals
   its definition, bf16(fp32(partial_0) + fp32(partial_1)), bit for bit, in
   eager calls and in CUDA graph replays, for the one-shot exchange (T = 200)
@@ -78,9 +82,11 @@ def _worker(rank: int, port: int, q):
         scores, idx = scores.to(dev), idx.to(dev)
         one = _qwen_module(cfg, w, dev, ParallelGroup(1), "reference")(x, idx, scores)
         pg = ParallelGroup(WORLD)
-        ref_ep = _qwen_module(cfg, w, dev, pg, "reference")(x, idx, scores)
+        ref_mod = _qwen_module(cfg, w, dev, pg, "reference")
+        ref_ep = [ref_mod(x, idx, scores) for _ in range(2)]   # the exact NVLink gather, twice
         fast_ep = _qwen_module(cfg, w, dev, pg, "fast")(x, idx, scores)
-        res["reference_equal"] = bool(torch.equal(ref_ep, one))
+        res["gather_used"] = pg._gather is not None
+        res["reference_equal"] = all(bool(torch.equal(o, one)) for o in ref_ep)
         diff = (fast_ep.float() - one.float())
         res["fast_rel_l2"] = float(diff.norm() / one.float().norm())
         # ---- token all-to-all
@@ -100,6 +106,26 @@ def _worker(rank: int, port: int, q):
         out = native.routed_forward(hiddens[rank], routes[rank][0], routes[rank][1], banks[rank], plan,
                                     native.ProcessGroupCollective())
         res["a2a_equal"] = bool(torch.equal(out, sim[rank]))
+        # ---- token all-to-all over NVLink peer memory: two eager calls, then
+        # CUDA graph replays
+        pc = native.PeerCollective(max_tokens=64)
+        outs = [native.routed_forward(hiddens[rank], routes[rank][0], routes[rank][1], banks[rank],
+                                      plan, pc) for _ in range(2)]
+        res["a2a_peer_equal"] = all(bool(torch.equal(o, sim[rank])) for o in outs)
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            gout = native.routed_forward(hiddens[rank], routes[rank][0], routes[rank][1], banks[rank],
+                                         plan, pc)
+        ok = True
+        for _ in range(2):
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            ok = ok and bool(torch.equal(gout, sim[rank]))
+        del graph
+        res["a2a_peer_graph_equal"] = ok
+        pc.close()
         # ---- fused NVLink combine + all-reduce
         from moe_serving_profile_b200 import _lib, ops
         T2, K2, E2, H2 = 200, 8, 128, 2048
@@ -184,6 +210,8 @@ def test_expert_parallel_over_nccl():
         assert res["reference_equal"], f"rank {r}: replicated-token EP differs from one GPU"
         assert res["fast_rel_l2"] < 1e-2, res
         assert res["a2a_equal"], f"rank {r}: all-to-all differs from the one-process run"
+        assert res["a2a_peer_equal"] and res["a2a_peer_graph_equal"], res
+        assert res["gather_used"], res
         assert res["p2p_used"] and res["p2p_equal"] and res["p2p_graph_equal"], res
         assert res["nccl_close"] and res["status"] == 0, res
         assert res["router_shard_equal"], res
