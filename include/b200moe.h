@@ -369,6 +369,49 @@ int b200moe_a2a_recv_plan(int device, void* stream, const int* counts, int ep,
                           int experts_per_rank, int rows, int* offsets, int* map_in,
                           int* map_back);
 
+/* ------------------------------------------------------------ one call per expert layer
+ * The whole single-GPU expert layer of ParallelExperts.forward
+ * (moe_serving/qwen3_parallel.py:96-118, gpt_oss_parallel.py:206-244 with
+ * ParallelGroup(1); parallel_numerics.ordered_expert_merge, :13-36) in one
+ * call: b200moe_permute of the routing, the row gather (token tiles of 64 or
+ * more), the gate/up and down grouped GEMMs (b200moe_expert_gemm with the
+ * automatic token tile of 1.5x the mean rows per expert, at most 160 for
+ * quantised weights) and b200moe_combine in ascending global expert order.
+ * Results are those of the separate calls, bit for bit. The weights are the
+ * packed stacks b200moe_expert_gemm takes (w1 gate/up, planes 2, feat_pad =
+ * ceil(I/128)*128, k_pad = ceil(H/64)*64; w2 down, feat_pad = ceil(H/128)*128,
+ * k_pad = feat_pad of w1; optional bf16 biases b1 / b2). workspace:
+ * b200moe_layer_workspace(args) bytes of device memory the call may
+ * overwrite, 256-byte aligned; it must not be in use by another call that
+ * may run at the same time. out: bf16 [T][ldo].
+ */
+typedef struct b200moe_layer_args {
+  const long long* indices;   /* [T][K] global expert ids (device) */
+  const void* weights;        /* [T][K] routing weights, fp32 or bf16 (device) */
+  int weights_bf16;
+  int T, K, E;                /* tokens, top-k, global experts */
+  int expert_begin;           /* global id of the stack's first expert */
+  const void* hidden;         /* bf16 [T][ldh] */
+  long long ldh;
+  int H, I;                   /* hidden and intermediate sizes */
+  int wfmt, n_experts;        /* B200MOE_W_*, experts in the stacks */
+  const void* w1;
+  const void* w2;
+  const void* b1;
+  const void* b2;
+  int sc_br, sc_bc;           /* FP8 scale block */
+  int gated_epilogue;         /* B200MOE_EPI_SWIGLU or B200MOE_EPI_CLAMP_SWIGLU */
+  float alpha, limit;
+  void* out;
+  long long ldo;
+} b200moe_layer_args;
+
+size_t b200moe_layer_workspace(const b200moe_layer_args* args);
+int b200moe_expert_layer(int device, void* stream, const b200moe_layer_args* args, void* workspace,
+                         size_t workspace_bytes);
+/* sizeof(b200moe_layer_args), so foreign bindings can check their mirror. */
+size_t b200moe_layer_args_size(void);
+
 /* ------------------------------------------------------------ peer-memory row exchanges
  * The token all-to-all of moe_serving/moe.py:110-137 (replacing the three
  * ProcessGroupCollective.exchange calls of distributed.py:33-46, each an

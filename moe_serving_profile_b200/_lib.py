@@ -48,6 +48,9 @@ EXPORTED = (
     "b200moe_p2p_import",
     "b200moe_p2p_close",
     "b200moe_combine_allreduce",
+    "b200moe_layer_workspace",
+    "b200moe_expert_layer",
+    "b200moe_layer_args_size",
     "b200moe_peer_rows_bytes",
     "b200moe_a2a_counts",
     "b200moe_a2a_dispatch",
@@ -87,6 +90,37 @@ class GemmArgs(ctypes.Structure):
         ("row_weight", c_void_p),
         ("row_weight_bf16", c_int),
         ("row_src", c_void_p),
+        ("out", c_void_p),
+        ("ldo", c_longlong),
+    ]
+
+
+class LayerArgs(ctypes.Structure):
+    """Mirror of ``b200moe_layer_args``."""
+
+    _fields_ = [
+        ("indices", c_void_p),
+        ("weights", c_void_p),
+        ("weights_bf16", c_int),
+        ("T", c_int),
+        ("K", c_int),
+        ("E", c_int),
+        ("expert_begin", c_int),
+        ("hidden", c_void_p),
+        ("ldh", c_longlong),
+        ("H", c_int),
+        ("I", c_int),
+        ("wfmt", c_int),
+        ("n_experts", c_int),
+        ("w1", c_void_p),
+        ("w2", c_void_p),
+        ("b1", c_void_p),
+        ("b2", c_void_p),
+        ("sc_br", c_int),
+        ("sc_bc", c_int),
+        ("gated_epilogue", c_int),
+        ("alpha", c_float),
+        ("limit", c_float),
         ("out", c_void_p),
         ("ldo", c_longlong),
     ]
@@ -167,6 +201,14 @@ def _load() -> ctypes.CDLL:
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_int, c_int, c_int, c_void_p,
         c_longlong, c_void_p, c_int, c_int,
     ]
+    lib.b200moe_layer_args_size.restype = c_size_t
+    lib.b200moe_layer_args_size.argtypes = []
+    if lib.b200moe_layer_args_size() != ctypes.sizeof(LayerArgs):
+        raise ImportError("b200moe_layer_args layout differs between the library and _lib.LayerArgs")
+    lib.b200moe_layer_workspace.restype = c_size_t
+    lib.b200moe_layer_workspace.argtypes = [POINTER(LayerArgs)]
+    lib.b200moe_expert_layer.restype = c_int
+    lib.b200moe_expert_layer.argtypes = [c_int, c_void_p, POINTER(LayerArgs), c_void_p, c_size_t]
     lib.b200moe_peer_rows_bytes.restype = c_size_t
     lib.b200moe_peer_rows_bytes.argtypes = [c_int, c_longlong, c_longlong]
     lib.b200moe_a2a_counts.restype = c_int

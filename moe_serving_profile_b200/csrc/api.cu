@@ -735,6 +735,153 @@ int b200moe_gather_rows(int device, void* stream, const void* src, long long ld_
   return B200MOE_OK;
 }
 
+// ---------------------------------------------------------------- one call per expert layer
+namespace {
+
+struct LayerPlan {
+  int bn, R;
+  size_t off_counts, off_offsets, off_perm, off_inv, off_scratch, off_rows, off_act, off_contrib, total;
+  size_t scratch;
+  bool gather;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+// Token tile of the separate-call path (experts.tile_policy): the smallest
+// power of two from 16 covering 1.5x the mean rows per expert, capped at
+// 256 (BF16) or 160 (quantised weights).
+int layer_tile(int T, int K, int E, int wfmt) {
+  const int max_tile = wfmt == B200MOE_W_BF16 ? 256 : 160;
+  const double rows = 1.5 * static_cast<double>(T) * K / E;
+  int bn = 16;
+  while (bn < max_tile && bn < rows) bn *= 2;
+  return std::min(bn, max_tile);
+}
+
+LayerPlan layer_plan(const b200moe_layer_args* a) {
+  LayerPlan p{};
+  p.R = a->T * a->K;
+  p.bn = layer_tile(a->T, a->K, a->E, a->wfmt);
+  p.gather = p.bn >= 64;
+  const size_t R = static_cast<size_t>(p.R);
+  const size_t i_pad = static_cast<size_t>((a->I + 127) / 128 * 128);
+  const size_t h_k = static_cast<size_t>((a->H + 63) / 64 * 64);
+  p.scratch = b200::permute_workspace_bytes(a->T, a->K, a->E);
+  size_t off = 0;
+  p.off_counts = off;  off = align256(off + 4ull * a->E);
+  p.off_offsets = off; off = align256(off + 4ull * (a->E + 1));
+  p.off_perm = off;    off = align256(off + 4ull * R);
+  p.off_inv = off;     off = align256(off + 4ull * R);
+  p.off_scratch = off; off = align256(off + p.scratch);
+  p.off_rows = off;    off = align256(off + (p.gather ? 2ull * R * h_k : 0));
+  p.off_act = off;     off = align256(off + 2ull * R * i_pad);
+  p.off_contrib = off; off = align256(off + 2ull * R * static_cast<size_t>(a->H));
+  p.total = off;
+  return p;
+}
+
+}  // namespace
+
+size_t b200moe_layer_args_size(void) { return sizeof(b200moe_layer_args); }
+
+size_t b200moe_layer_workspace(const b200moe_layer_args* a) {
+  if (!a || a->T < 0 || a->K < 1 || a->E < 1 || a->H < 8 || a->I < 8) return 0;
+  return layer_plan(a).total;
+}
+
+int b200moe_expert_layer(int device, void* stream, const b200moe_layer_args* a, void* workspace,
+                         size_t workspace_bytes) {
+  B200_CHECK(a != nullptr, "args is NULL");
+  B200_CHECK(a->T >= 0 && a->K >= 1 && a->E >= 1 && a->H >= 8 && a->I >= 8, "bad sizes");
+  B200_CHECK(a->n_experts >= 1 && a->expert_begin >= 0 && a->expert_begin + a->n_experts <= a->E,
+             "bad expert range");
+  B200_CHECK(a->gated_epilogue == B200MOE_EPI_SWIGLU || a->gated_epilogue == B200MOE_EPI_CLAMP_SWIGLU,
+             "bad gated epilogue");
+  if (a->T == 0) return B200MOE_OK;
+  B200_CHECK((long long)a->T * a->K < (1ll << 30), "T*K too large");
+  B200_CHECK(a->indices && a->weights && a->hidden && a->out && a->w1 && a->w2,
+             "indices, weights, hidden, out, w1 and w2 are required");
+  const LayerPlan p = layer_plan(a);
+  B200_CHECK(workspace != nullptr && workspace_bytes >= p.total && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+             "workspace must be 256-byte aligned and hold %zu bytes (got %zu)", p.total, workspace_bytes);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(ws + p.off_counts);
+  int* offsets = reinterpret_cast<int*>(ws + p.off_offsets);
+  int* perm = reinterpret_cast<int*>(ws + p.off_perm);
+  int* inv = reinterpret_cast<int*>(ws + p.off_inv);
+  __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(ws + p.off_rows);
+  __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(ws + p.off_act);
+  __nv_bfloat16* contrib = reinterpret_cast<__nv_bfloat16*>(ws + p.off_contrib);
+  const int i_pad = (a->I + 127) / 128 * 128;
+  const int h_k = (a->H + 63) / 64 * 64;
+  const int h_f = (a->H + 127) / 128 * 128;
+  int rc = b200moe_permute(device, stream, a->indices, a->T, a->K, a->E, counts, offsets, perm, inv,
+                           ws + p.off_scratch, p.scratch);
+  if (rc) return rc;
+  const int lo = a->expert_begin, hi = a->expert_begin + a->n_experts;
+  if (p.gather) {
+    rc = b200moe_gather_rows_range(device, stream, a->hidden, a->ldh, perm, a->K, p.R, a->H, rows, h_k,
+                                   offsets, lo, hi);
+    if (rc) return rc;
+  }
+  b200moe_gemm_args g{};
+  g.offsets = offsets;
+  g.expert_begin = lo;
+  g.n_experts = a->n_experts;
+  g.max_rows = p.R;
+  g.token_tile = p.bn;
+  g.wfmt = a->wfmt;
+  g.sc_br = a->sc_br;
+  g.sc_bc = a->sc_bc;
+  g.alpha = a->alpha;
+  g.limit = a->limit;
+  // gate / up
+  g.planes = 2;
+  g.feat_pad = i_pad;
+  g.n_feat = a->I;
+  g.k_pad = h_k;
+  g.weight = a->w1;
+  g.b_src = p.gather ? static_cast<const void*>(rows) : a->hidden;
+  g.ldb = p.gather ? h_k : a->ldh;
+  g.b_rows = p.gather ? p.R : a->T;
+  g.k_valid = a->H;
+  g.b_map = p.gather ? nullptr : perm;
+  g.b_div = p.gather ? 1 : a->K;
+  g.epilogue = a->gated_epilogue;
+  g.bias = a->b1;
+  g.out = act;
+  g.ldo = i_pad;
+  rc = b200moe_expert_gemm(device, stream, &g);
+  if (rc) return rc;
+  // down, scaled by the routing weights
+  g.planes = 1;
+  g.feat_pad = h_f;
+  g.n_feat = a->H;
+  g.k_pad = i_pad;
+  g.weight = a->w2;
+  g.b_src = act;
+  g.ldb = i_pad;
+  g.b_rows = p.R;
+  g.k_valid = a->I;
+  g.b_map = nullptr;
+  g.b_div = 1;
+  g.epilogue = B200MOE_EPI_DOWN;
+  g.bias = a->b2;
+  g.row_weight = a->weights;
+  g.row_weight_bf16 = a->weights_bf16;
+  g.row_src = perm;
+  g.out = contrib;
+  g.ldo = a->H;
+  rc = b200moe_expert_gemm(device, stream, &g);
+  if (rc) return rc;
+  // a stack holding every expert combines every assignment, as the separate
+  // combine call does (expert range [0, 2^30))
+  const bool all = lo == 0 && hi == a->E;
+  return b200moe_combine(device, stream, contrib, a->H, inv, a->indices, a->T, a->K, a->H,
+                         B200MOE_ORDER_EXPERT, 1, all ? 0 : lo, all ? (1 << 30) : hi, 0, nullptr, 0,
+                         a->out, a->ldo);
+}
+
 // ---------------------------------------------------------------- peer-memory row exchanges
 size_t b200moe_peer_rows_bytes(int H, long long cap_a, long long cap_b) {
   if (H < 8 || cap_a < 0 || cap_b < 0) return 0;

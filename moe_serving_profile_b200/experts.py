@@ -188,8 +188,14 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     T, K = indices.shape
     if T == 0:
         return torch.empty_like(hidden)
-    perm = ops.permute(indices, num_experts)
     size = 1 if parallel is None else parallel.size
+    if size == 1 and numerics in ("reference", "fast") or (
+            size == 1 and numerics == "efficient" and w.fmt != _lib.W_FP8):
+        # one library call: permutation, gather, both GEMMs and the ordered
+        # combine (the same kernels and results as the separate calls)
+        return ops.expert_layer(w, hidden, indices, weights, num_experts=num_experts,
+                                expert_begin=expert_begin)
+    perm = ops.permute(indices, num_experts)
     if numerics == "efficient":
         # FP8: W8A8 experts (grouped_fp8). MXFP4 / BF16: the weight-only
         # experts, as matmul_ogs multiplies bf16 activations with upcast
@@ -202,10 +208,6 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
             return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
         return parallel.combine_reduce(contrib, perm.inverse, indices, expert_begin,
                                        expert_begin + w.n_experts)
-    if size == 1:
-        contrib = run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
-                              expert_begin=expert_begin)
-        return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
     if numerics == "reference":
         g = parallel.gather_rows_buffer(hidden.device, hidden.shape[1], T * K)
         if g is not None:

@@ -255,6 +255,42 @@ def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max
     return out
 
 
+def expert_layer(w, hidden: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor, *,
+                 num_experts: int, expert_begin: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The single-GPU expert layer in one call (b200moe_expert_layer):
+    permutation, row gather, gate/up and down grouped GEMMs and the
+    global-expert-order combine of the experts in ``w`` (a
+    layout.ExpertWeights). The workspace is one allocation of the caching
+    allocator per call."""
+    device = _dev(hidden, "hidden")
+    _bf16_rows(hidden, "hidden")
+    T, K = indices.shape
+    if out is None:
+        out = torch.empty(T, w.hidden, device=hidden.device, dtype=torch.bfloat16)
+    _bf16_rows(out, "output")
+    a = _lib.LayerArgs()
+    a.indices = _ptr(indices)
+    a.weights = _ptr(weights)
+    a.weights_bf16 = int(weights.dtype == torch.bfloat16)
+    a.T, a.K, a.E = T, K, num_experts
+    a.expert_begin = expert_begin
+    a.hidden = _ptr(hidden)
+    a.ldh = hidden.stride(0)
+    a.H, a.I = w.hidden, w.inter
+    a.wfmt, a.n_experts = w.fmt, w.n_experts
+    a.w1, a.w2, a.b1, a.b2 = _ptr(w.w1), _ptr(w.w2), _ptr(w.b1), _ptr(w.b2)
+    a.sc_br, a.sc_bc = w.block
+    a.gated_epilogue = w.gated_epilogue
+    a.alpha, a.limit = w.alpha, w.limit
+    a.out = _ptr(out)
+    a.ldo = out.stride(0)
+    nbytes = lib.b200moe_layer_workspace(ctypes.byref(a))
+    ws = torch.empty(max(nbytes, 256), device=hidden.device, dtype=torch.uint8)
+    check(lib.b200moe_expert_layer(device, _stream(device), ctypes.byref(a), _ptr(ws), nbytes),
+          "expert_layer")
+    return out
+
+
 def w8a8_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max_rows: int,
               planes: int, feat_pad: int, n_feat: int, k_pad: int, weight: torch.Tensor,
               fp8_block: tuple[int, int] = (128, 128), q: torch.Tensor, q_scale: torch.Tensor,

@@ -181,3 +181,42 @@ def test_expert_parallel_split_is_bitwise_invariant(cuda):
         contrib += c
     out = ops.combine(contrib, perm.inverse, idx, order=_lib.ORDER_EXPERT)
     assert torch.equal(out, base)
+
+
+@pytest.mark.parametrize("name,T", [("qwen3-30b-a3b", 1), ("qwen3-30b-a3b", 64), ("qwen3-30b-a3b", 512),
+                                    ("qwen3-30b-a3b", 4096), ("gpt-oss-20b", 16), ("gpt-oss-20b", 2048),
+                                    ("qwen3-30b-a3b-bf16", 512)])
+def test_expert_layer_one_call_equals_separate_calls(cuda, name, T):
+    """b200moe_expert_layer (one C-ABI call: permutation, gather, both
+    GEMMs, ordered combine) against the same kernels called one by one:
+    bit for bit."""
+    from moe_serving_profile_b200 import experts as X
+    from moe_serving_profile_b200 import layout, ops
+    bf16 = name.endswith("-bf16")
+    cfg = S.CONFIGS[name.removesuffix("-bf16")]
+    if cfg.family == "qwen3":
+        w = S.make_qwen(cfg, seed=3, device=cuda)
+        if bf16:
+            def dq(q, s):
+                E = q.shape[0]
+                return torch.stack([oracle.dequant_fp8(q[e].cpu(), s[e].cpu(), cfg.block) for e in range(E)]).to(cuda)
+            packed = layout.bf16_experts(dq(w.gate, w.gate_scale), dq(w.up, w.up_scale), dq(w.down, w.down_scale))
+        else:
+            packed = layout.fp8_experts(w.gate, w.gate_scale, w.up, w.up_scale, w.down, w.down_scale, cfg.block)
+        router = w.router
+    else:
+        w = S.make_gpt_oss(cfg, seed=3, device=cuda)
+        packed = layout.gpt_oss_mxfp4_experts(w.gu_blocks, w.gu_scales, w.gu_bias, w.dn_blocks, w.dn_scales,
+                                              w.dn_bias, cfg.alpha, cfg.limit)
+        router = w.router
+    x = S.make_hidden(T, cfg.hidden, seed=11 + T, device=cuda)
+    scores, idx = torch.topk(torch.softmax(torch.nn.functional.linear(x, router).float(), -1), cfg.top_k, -1)
+    if cfg.family == "gpt_oss":
+        scores = scores.bfloat16()
+    one = ops.expert_layer(packed, x, idx, scores.contiguous(), num_experts=cfg.experts)
+    perm = ops.permute(idx, cfg.experts)
+    contrib = X.run_experts(packed, x, perm, scores.contiguous(), K=cfg.top_k, num_experts=cfg.experts,
+                            expert_begin=0)
+    sep = ops.combine(contrib, perm.inverse, idx, order=_lib.ORDER_EXPERT)
+    assert torch.equal(one, sep)
+    assert _lib.device_status(cuda.index) == 0

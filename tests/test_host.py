@@ -163,6 +163,8 @@ def test_efficient_numerics_dispatch(monkeypatch):
     monkeypatch.setattr(X.ops, "combine", lambda contrib, inverse, idx, order: contrib)
     monkeypatch.setattr(X, "run_experts", lambda *a, **k: calls.append("weight_only") or "rows")
     monkeypatch.setattr(X, "run_experts_w8a8", lambda *a, **k: calls.append("w8a8") or "rows")
+    # one GPU: the weight-only formats take the single-call layer
+    monkeypatch.setattr(X.ops, "expert_layer", lambda *a, **k: calls.append("weight_only") or "rows")
     for fmt, want in ((_lib.W_FP8, "w8a8"), (_lib.W_MXFP4, "weight_only"), (_lib.W_BF16, "weight_only")):
         out = X.layer_forward(SimpleNamespace(fmt=fmt, n_experts=4), torch.zeros(3, 64, dtype=torch.bfloat16),
                               torch.zeros(3, 2, dtype=torch.int64), torch.zeros(3, 2), num_experts=4,
