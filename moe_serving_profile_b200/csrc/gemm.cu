@@ -209,6 +209,75 @@ __device__ __forceinline__ float epilogue_gated(int epi, float g, float u, float
   return bf16_rn(t3 * glu);
 }
 
+// MMA issuer of single-issuer launches (one accumulator bank: token tiles of
+// 128 rows or more). It waits once for two consecutive k-blocks' A and B
+// stages, then issues their eight MMAs and two stage releases as
+// straight-line code, specialised at compile time on where A lives and on
+// whether one commit releases both rings. Measured in isolation at 160-token
+// tiles: a barrier wait and tensor fence before every k-block leave the
+// tensor pipe idle about 160 of every 480 cycles (320 cycles of MMAs), one
+// per two k-blocks about 40; conditional branches between MMAs cost the
+// issuing thread tens of cycles each.
+template <bool kTmemA, bool kJoint>
+__device__ void mma_issue_pairs(const GemmParams& p, uint32_t tmem, uint32_t base_u32, const int* prefix,
+                                int total, uint64_t* a_full, uint64_t* a_empty, uint64_t* b_full,
+                                uint64_t* b_empty, uint64_t* acc_full, uint64_t* acc_empty,
+                                uint64_t* mma_done) {
+  Ring ra(p.na), rb(p.nb);
+  int tc = 0;
+  bool ok = true;
+  auto kblock = [&](uint32_t d, int sa, int sb, uint32_t idesc, uint32_t acc) {
+    const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + static_cast<uint32_t>(sb * p.bn * 128));
+    if (kTmemA)
+      umma_kblock_tmem_a(d, tmem + p.a_col0 + static_cast<uint32_t>(sa) * kAStageCols, bdesc, idesc, acc);
+    else
+      umma_kblock_smem_a(d, sdesc_k_sw128(base_u32 + p.a_off + static_cast<uint32_t>(sa) * kATile), bdesc,
+                         idesc, acc);
+    umma_commit(&a_empty[sa]);
+    if (!kJoint) umma_commit(&b_empty[sb]);
+  };
+  for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc) {
+    const int slot = p.acc_slots == 2 ? (tc & 1) : 0;
+    const uint32_t use = p.acc_slots == 2 ? static_cast<uint32_t>(tc >> 1) : static_cast<uint32_t>(tc);
+    const uint32_t idesc = idesc_bf16_f32(128, tile_n(decode_tile(t, prefix, p), p));
+    if (!wait_bounded(&acc_empty[slot], (use & 1u) ^ 1u, p.status)) break;
+    tc_fence_after();
+    const uint32_t d = tmem + static_cast<uint32_t>(slot * p.bn);
+    for (int kb = 0; kb < p.nkb; kb += 2) {
+      const int sa0 = ra.idx, sb0 = rb.idx;
+      const uint32_t pa0 = ra.phase, pb0 = rb.phase;
+      ra.next();
+      rb.next();
+      if (kb + 1 < p.nkb) {
+        const int sa1 = ra.idx, sb1 = rb.idx;
+        const uint32_t pa1 = ra.phase, pb1 = rb.phase;
+        ra.next();
+        rb.next();
+        if (!wait_bounded(&a_full[sa0], pa0, p.status) || !wait_bounded(&b_full[sb0], pb0, p.status) ||
+            !wait_bounded(&a_full[sa1], pa1, p.status) || !wait_bounded(&b_full[sb1], pb1, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        kblock(d, sa0, sb0, idesc, kb > 0 ? 1u : 0u);
+        kblock(d, sa1, sb1, idesc, 1u);
+      } else {
+        if (!wait_bounded(&a_full[sa0], pa0, p.status) || !wait_bounded(&b_full[sb0], pb0, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        kblock(d, sa0, sb0, idesc, kb > 0 ? 1u : 0u);
+      }
+    }
+    if (!ok) break;
+    umma_commit(&acc_full[slot]);
+  }
+  // all issued MMAs have finished before TMEM is released
+  umma_commit(mma_done);
+  wait_bounded(mma_done, 0, p.status);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ GemmParams p) {
@@ -340,7 +409,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // accumulates k-block i into bank i % nacc (nacc even), so the two never
     // share an accumulator; each one alone costs about 75 cycles per MMA of
     // issue time, two overlap. Both commit to acc_full.
-    if (lane == 0) {
+    if (lane == 0 && p.n_issuers == 1 && p.nacc == 1) {
+      const bool tmem_a = p.wfmt != kWBf16 && !p.a_smem;
+      if (tmem_a && p.joint_ab)
+        mma_issue_pairs<true, true>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
+                                    acc_full, acc_empty, mma_done);
+      else if (tmem_a)
+        mma_issue_pairs<true, false>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
+                                     acc_full, acc_empty, mma_done);
+      else if (p.joint_ab)
+        mma_issue_pairs<false, true>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
+                                     acc_full, acc_empty, mma_done);
+      else
+        mma_issue_pairs<false, false>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
+                                      acc_full, acc_empty, mma_done);
+    } else if (lane == 0) {
       const int step = p.n_issuers;
       const int j = warp == kWarpMma ? 0 : 1;
       uint32_t idesc = idesc_bf16_f32(128, p.bn);

@@ -355,6 +355,43 @@ B200_DEVI bool umma_k64_tmem_a_probe(uint32_t tmem_d, uint32_t tmem_a, uint64_t 
   return ok != 0;
 }
 
+// The four K = 16 MMAs of one 64-column k-block, in one asm block: A from
+// tensor memory (columns a, a + 8, a + 16, a + 24) and B by its shared-memory
+// descriptor (advanced 32 bytes per MMA); the first accumulates iff acc != 0.
+B200_DEVI void umma_kblock_tmem_a(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred q0, qt;\n\t.reg .b64 bd;\n\t.reg .b32 ta;\n\t"
+      "setp.ne.b32 q0, %4, 0;\n\t"
+      "setp.eq.b32 qt, %3, %3;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, q0;\n\t"
+      "add.s64 bd, %2, 2;\n\tadd.u32 ta, %1, 8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %3, qt;\n\t"
+      "add.s64 bd, bd, 2;\n\tadd.u32 ta, ta, 8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %3, qt;\n\t"
+      "add.s64 bd, bd, 2;\n\tadd.u32 ta, ta, 8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %3, qt;\n\t}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// As umma_kblock_tmem_a with A by its shared-memory descriptor (advanced 32
+// bytes per MMA, like B).
+B200_DEVI void umma_kblock_smem_a(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred q0, qt;\n\t.reg .b64 ad, bd;\n\t"
+      "setp.ne.b32 q0, %4, 0;\n\t"
+      "setp.eq.b32 qt, %3, %3;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q0;\n\t"
+      "add.s64 ad, %1, 2;\n\tadd.s64 bd, %2, 2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, qt;\n\t"
+      "add.s64 ad, ad, 2;\n\tadd.s64 bd, bd, 2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, qt;\n\t"
+      "add.s64 ad, ad, 2;\n\tadd.s64 bd, bd, 2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, qt;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread
 // has completed.
 B200_DEVI void umma_commit(uint64_t* bar) {
@@ -385,6 +422,7 @@ B200_DEVI void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                : "memory");
 }
 B200_DEVI void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 
 // 32 consecutive 32-bit columns of this thread's TMEM lane (32x32b shape:
 // warp w writes lanes 32 * (w % 4) .. + 31, thread i lane 32 * (w % 4) + i).
