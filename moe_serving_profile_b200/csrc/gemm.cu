@@ -209,17 +209,16 @@ __device__ __forceinline__ float epilogue_gated(int epi, float g, float u, float
   return bf16_rn(t3 * glu);
 }
 
-// MMA issuer of single-issuer launches (one accumulator bank: token tiles of
-// 128 rows or more). It waits once for two consecutive k-blocks' A and B
-// stages, then issues their eight MMAs and two stage releases as
-// straight-line code, specialised at compile time on where A lives and on
-// whether one commit releases both rings. Measured in isolation at 160-token
+// MMA issuer of single-issuer launches (one accumulator bank). It waits once
+// for G consecutive k-blocks' A and B stages, then issues their 4G MMAs and G
+// stage releases as straight-line code, specialised at compile time on where
+// A lives and on whether one commit releases both rings. Measured in isolation at 160-token
 // tiles: a barrier wait and tensor fence before every k-block leave the
 // tensor pipe idle about 160 of every 480 cycles (320 cycles of MMAs), one
 // per two k-blocks about 40; conditional branches between MMAs cost the
 // issuing thread tens of cycles each.
-template <bool kTmemA, bool kJoint>
-__device__ void mma_issue_pairs(const GemmParams& p, uint32_t tmem, uint32_t base_u32, const int* prefix,
+template <bool kTmemA, bool kJoint, int G>
+__device__ void mma_issue_groups(const GemmParams& p, uint32_t tmem, uint32_t base_u32, const int* prefix,
                                 int total, uint64_t* a_full, uint64_t* a_empty, uint64_t* b_full,
                                 uint64_t* b_empty, uint64_t* acc_full, uint64_t* acc_empty,
                                 uint64_t* mma_done) {
@@ -243,31 +242,28 @@ __device__ void mma_issue_pairs(const GemmParams& p, uint32_t tmem, uint32_t bas
     if (!wait_bounded(&acc_empty[slot], (use & 1u) ^ 1u, p.status)) break;
     tc_fence_after();
     const uint32_t d = tmem + static_cast<uint32_t>(slot * p.bn);
-    for (int kb = 0; kb < p.nkb; kb += 2) {
-      const int sa0 = ra.idx, sb0 = rb.idx;
-      const uint32_t pa0 = ra.phase, pb0 = rb.phase;
-      ra.next();
-      rb.next();
-      if (kb + 1 < p.nkb) {
-        const int sa1 = ra.idx, sb1 = rb.idx;
-        const uint32_t pa1 = ra.phase, pb1 = rb.phase;
-        ra.next();
-        rb.next();
-        if (!wait_bounded(&a_full[sa0], pa0, p.status) || !wait_bounded(&b_full[sb0], pb0, p.status) ||
-            !wait_bounded(&a_full[sa1], pa1, p.status) || !wait_bounded(&b_full[sb1], pb1, p.status)) {
-          ok = false;
-          break;
+    for (int kb = 0; kb < p.nkb; kb += G) {
+      const int n = min(G, p.nkb - kb);
+      int sa[G], sb[G];
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        sa[i] = ra.idx;
+        sb[i] = rb.idx;
+        if (i < n) {
+          if (ok && (!wait_bounded(&a_full[ra.idx], ra.phase, p.status) ||
+                     !wait_bounded(&b_full[rb.idx], rb.phase, p.status)))
+            ok = false;
+          ra.next();
+          rb.next();
         }
-        tc_fence_after();
-        kblock(d, sa0, sb0, idesc, kb > 0 ? 1u : 0u);
-        kblock(d, sa1, sb1, idesc, 1u);
+      }
+      if (!ok) break;
+      tc_fence_after();
+      if (n == G) {
+#pragma unroll
+        for (int i = 0; i < G; ++i) kblock(d, sa[i], sb[i], idesc, (kb + i) > 0 ? 1u : 0u);
       } else {
-        if (!wait_bounded(&a_full[sa0], pa0, p.status) || !wait_bounded(&b_full[sb0], pb0, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        kblock(d, sa0, sb0, idesc, kb > 0 ? 1u : 0u);
+        for (int i = 0; i < n; ++i) kblock(d, sa[i], sb[i], idesc, (kb + i) > 0 ? 1u : 0u);
       }
     }
     if (!ok) break;
@@ -411,18 +407,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // issue time, two overlap. Both commit to acc_full.
     if (lane == 0 && p.n_issuers == 1 && p.nacc == 1) {
       const bool tmem_a = p.wfmt != kWBf16 && !p.a_smem;
-      if (tmem_a && p.joint_ab)
-        mma_issue_pairs<true, true>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
-                                    acc_full, acc_empty, mma_done);
-      else if (tmem_a)
-        mma_issue_pairs<true, false>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
-                                     acc_full, acc_empty, mma_done);
-      else if (p.joint_ab)
-        mma_issue_pairs<false, true>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
-                                     acc_full, acc_empty, mma_done);
-      else
-        mma_issue_pairs<false, false>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty,
-                                      acc_full, acc_empty, mma_done);
+#define B200_ISSUE(TA, J)                                                                           \
+  mma_issue_groups<TA, J, 2>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty, acc_full, \
+                             acc_empty, mma_done)
+      if (tmem_a && p.joint_ab) B200_ISSUE(true, true);
+      else if (tmem_a) B200_ISSUE(true, false);
+      else if (p.joint_ab) B200_ISSUE(false, true);
+      else B200_ISSUE(false, false);
+#undef B200_ISSUE
     } else if (lane == 0) {
       const int step = p.n_issuers;
       const int j = warp == kWarpMma ? 0 : 1;
