@@ -209,6 +209,15 @@ int b200moe_permute_noalloc(int device, void* stream, const long long* indices, 
 #define B200MOE_EPI_SWIGLU 0
 #define B200MOE_EPI_CLAMP_SWIGLU 1
 #define B200MOE_EPI_DOWN 2
+/* The fused MXFP4 path of the reference's efficient GPT-OSS numerics
+ * (matmul_ogs with a fused SwiGLU and fp32 biases, efficient_kernels.py:157-206,
+ * biases cast to fp32 at gpt_oss_parallel.py:438-446): fp32 throughout the
+ * epilogue. CLAMP_SWIGLU_F32 (gated): g = acc_g + bias_g, u = acc_u + bias_u,
+ * g = min(g, limit), u = clamp(u, -limit, limit), out = bf16(g / (1 +
+ * exp(-alpha g)) * (u + 1)). DOWN_F32: out is fp32, out = acc + bias (no
+ * rounding, no row weight; ldo in floats, a multiple of 4). */
+#define B200MOE_EPI_CLAMP_SWIGLU_F32 3
+#define B200MOE_EPI_DOWN_F32 4
 
 typedef struct b200moe_gemm_args {
   /* rows */
@@ -292,6 +301,19 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
                     int order, int experts_per_rank, int expert_lo, int expert_hi,
                     int scale_rows, const void* weights, int weights_bf16, void* out,
                     long long ld_out);
+
+/* The scatter-reduce of the reference's fused MXFP4 path (matmul_ogs with
+ * gammas and a scatter index, efficient_kernels.py:195-205), replacing the
+ * index_add_-order combine there: rows are the fp32 outputs of
+ * B200MOE_EPI_DOWN_F32 (acc + bias), and
+ *   out[t, :] = bf16( sum over k = 0 .. K-1 in order of
+ *                     fp32(weights[t*K+k]) * rows[inverse[t*K+k], :] )
+ * in fp32 with one rounding, over the slots whose expert is in
+ * [expert_lo, expert_hi). weights fp32 or bf16 [T][K]. H % 4 == 0. */
+int b200moe_combine_f32(int device, void* stream, const float* rows, long long ld_rows,
+                        const int* inverse, const long long* indices, int T, int K, int H,
+                        int expert_lo, int expert_hi, const void* weights, int weights_bf16, void* out,
+                        long long ld_out);
 
 /* ------------------------------------------------------------ row gather
  * dst[i, :H] = src[map[i] / div, :H] for i < n (bf16 rows; a negative

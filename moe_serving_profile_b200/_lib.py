@@ -20,7 +20,7 @@ STATUS_WAIT_TIMEOUT, STATUS_BAD_TILE, STATUS_BAD_INDEX, STATUS_PEER_TIMEOUT = 1,
 
 ROUTER_QWEN3, ROUTER_GPT_OSS, ROUTER_NATIVE = 0, 1, 2
 W_BF16, W_FP8, W_MXFP4 = 0, 1, 2
-EPI_SWIGLU, EPI_CLAMP_SWIGLU, EPI_DOWN = 0, 1, 2
+EPI_SWIGLU, EPI_CLAMP_SWIGLU, EPI_DOWN, EPI_CLAMP_SWIGLU_F32, EPI_DOWN_F32 = 0, 1, 2, 3, 4
 ORDER_EXPERT, ORDER_RANK_SLOT = 0, 1
 PERMUTE_SCRATCH_BYTES = 1 << 20
 
@@ -37,6 +37,7 @@ EXPORTED = (
     "b200moe_expert_gemm",
     "b200moe_w8a8_gemm",
     "b200moe_combine",
+    "b200moe_combine_f32",
     "b200moe_gather_rows",
     "b200moe_gather_rows_range",
     "b200moe_a2a_recv_plan",
@@ -172,6 +173,11 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_combine.argtypes = [
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
         c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_longlong,
+    ]
+    lib.b200moe_combine_f32.restype = c_int
+    lib.b200moe_combine_f32.argtypes = [
+        c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+        c_void_p, c_int, c_void_p, c_longlong,
     ]
     lib.b200moe_gather_rows.restype = c_int
     lib.b200moe_gather_rows.argtypes = [

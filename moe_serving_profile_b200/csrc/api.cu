@@ -261,9 +261,12 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   B200_CHECK(a->offsets && a->weight && a->b_src && a->out, "offsets, weight, b_src, out are required");
   B200_CHECK(a->wfmt >= B200MOE_W_BF16 && a->wfmt <= B200MOE_W_MXFP4, "bad weight format %d", a->wfmt);
   B200_CHECK(a->planes == 1 || a->planes == 2, "planes must be 1 or 2");
-  B200_CHECK(a->epilogue >= B200MOE_EPI_SWIGLU && a->epilogue <= B200MOE_EPI_DOWN, "bad epilogue");
-  B200_CHECK((a->epilogue == B200MOE_EPI_DOWN) == (a->planes == 1),
-             "gated epilogues need planes == 2, the down epilogue planes == 1");
+  B200_CHECK(a->epilogue >= B200MOE_EPI_SWIGLU && a->epilogue <= B200MOE_EPI_DOWN_F32, "bad epilogue");
+  const bool down_epi = a->epilogue == B200MOE_EPI_DOWN || a->epilogue == B200MOE_EPI_DOWN_F32;
+  B200_CHECK(down_epi == (a->planes == 1),
+             "gated epilogues need planes == 2, the down epilogues planes == 1");
+  B200_CHECK(a->epilogue != B200MOE_EPI_DOWN_F32 || (a->row_weight == nullptr && a->ldo % 4 == 0),
+             "the fp32 down epilogue takes no row weights and needs ldo %% 4 == 0");
   B200_CHECK(a->n_experts >= 1 && a->expert_begin >= 0, "bad expert range");
   if (a->n_experts > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "at most 1024 experts per launch");
   B200_CHECK(a->feat_pad >= 128 && a->feat_pad % 128 == 0, "feat_pad must be a positive multiple of 128");
@@ -604,6 +607,23 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
   B200_CUDA(b200::launch_combine(static_cast<cudaStream_t>(stream), rows, ld_rows, inverse, indices,
                                  T, K, H, order, experts_per_rank, expert_lo, expert_hi, scale_rows,
                                  weights, weights_bf16, out, ld_out));
+  return B200MOE_OK;
+}
+
+int b200moe_combine_f32(int device, void* stream, const float* rows, long long ld_rows,
+                        const int* inverse, const long long* indices, int T, int K, int H,
+                        int expert_lo, int expert_hi, const void* weights, int weights_bf16, void* out,
+                        long long ld_out) {
+  B200_CHECK(T >= 0 && K >= 1 && H >= 4, "bad sizes");
+  if (H % 4 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "combine_f32 needs H %% 4 == 0");
+  if (T == 0) return B200MOE_OK;
+  B200_CHECK(rows && inverse && indices && weights && out, "rows, inverse, indices, weights and out are required");
+  B200_CHECK(aligned16(rows) && ld_rows % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0 && ld_out % 4 == 0,
+             "rows must be 16-byte aligned (ld %% 4 == 0), out 8-byte aligned (ld %% 4 == 0)");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_combine_f32(static_cast<cudaStream_t>(stream), rows, ld_rows, inverse, indices, T, K,
+                                     H, expert_lo, expert_hi, weights, weights_bf16, out, ld_out));
   return B200MOE_OK;
 }
 

@@ -82,6 +82,39 @@ __global__ void __launch_bounds__(128) combine_kernel(
   }
 }
 
+// out[t] = bf16( sum over the token's slots k in order of fp32(w[t, k]) *
+// rows[inverse[t*K + k]] ), in fp32 with one rounding; only experts in
+// [lo, hi). The scatter-reduce of the fused MXFP4 path (matmul_ogs with
+// gammas, efficient_kernels.py:195-205).
+__global__ void __launch_bounds__(128) combine_f32_kernel(
+    const float* __restrict__ rows, long long ld_rows, const int* __restrict__ inverse,
+    const long long* __restrict__ indices, int T, int K, int H, int lo, int hi,
+    const void* __restrict__ weights, int weights_bf16, __nv_bfloat16* __restrict__ out,
+    long long ld_out) {
+  const int t = blockIdx.x;
+  const int nvec = H >> 2;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+      const long long e = indices[(long long)t * K + k];
+      const int r = inverse[(long long)t * K + k];
+      if (r < 0 || e < lo || e >= hi) continue;
+      const float w = weights_bf16
+                          ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(weights)[(long long)t * K + k])
+                          : reinterpret_cast<const float*>(weights)[(long long)t * K + k];
+      const float4 y = __ldg(reinterpret_cast<const float4*>(rows + r * ld_rows) + v);
+      acc.x += y.x * w;
+      acc.y += y.y * w;
+      acc.z += y.z * w;
+      acc.w += y.w * w;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(acc.x, acc.y);
+    o.y = pack_bf16x2(acc.z, acc.w);
+    reinterpret_cast<uint2*>(out + t * ld_out)[v] = o;
+  }
+}
+
 __global__ void __launch_bounds__(128) gather_rows_kernel(const __nv_bfloat16* __restrict__ src,
                                                            long long ld_src,
                                                            const int* __restrict__ map, int div,
@@ -133,6 +166,15 @@ cudaError_t launch_gather_rows_range(cudaStream_t st, const void* src, long long
   gather_rows_range_kernel<<<blocks, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(src), ld_src,
                                                    map, div, n, H, static_cast<__nv_bfloat16*>(dst),
                                                    ld_dst, offsets, expert_lo, expert_hi);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_f32(cudaStream_t st, const float* rows, long long ld_rows,
+                               const int* inverse, const long long* indices, int T, int K, int H,
+                               int lo, int hi, const void* weights, int weights_bf16, void* out,
+                               long long ld_out) {
+  combine_f32_kernel<<<T, 128, 0, st>>>(rows, ld_rows, inverse, indices, T, K, H, lo, hi, weights,
+                                        weights_bf16, static_cast<__nv_bfloat16*>(out), ld_out);
   return cudaGetLastError();
 }
 

@@ -53,7 +53,7 @@ constexpr uint32_t kAStageCols = 32;        // TMEM columns per A stage (64 bf16
 enum { kScaleHalf = 0, kScaleChunk = 1, kScaleMx = 2 };
 
 enum { kWBf16 = 0, kWFp8 = 1, kWMx = 2 };
-enum { kEpiSwiglu = 0, kEpiClamp = 1, kEpiDown = 2 };
+enum { kEpiSwiglu = 0, kEpiClamp = 1, kEpiDown = 2, kEpiClampF32 = 3, kEpiDownF32 = 4 };
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -197,6 +197,16 @@ __device__ __forceinline__ float epilogue_gated(int epi, float g, float u, float
     const float gb = bf16_rn(g);
     const float ub = bf16_rn(u);
     return bf16_rn(silu_bf16(gb) * ub);
+  }
+  if (epi == kEpiClampF32) {
+    // fp32 throughout, one rounding: fp32 accumulator + fp32 bias, clamp,
+    // gate * sigmoid(alpha * gate) * (up + 1)
+    float gf = g + bg;
+    float uf = u + bu;
+    gf = gf > limit ? limit : gf;
+    uf = uf < -limit ? -limit : (uf > limit ? limit : uf);
+    const float sg = gf / (1.f + expf(-alpha * gf));
+    return bf16_rn(sg * (uf + 1.f));
   }
   float gb = bf16_rn(bf16_rn(g) + bg);
   float ub = bf16_rn(bf16_rn(u) + bu);
@@ -652,6 +662,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c0 + j < tl.nrows && tl.ft * 64 + c8 < p.n_feat)
             *reinterpret_cast<uint4*>(p.out + (long long)(tl.row0 + c0 + j) * p.ldo + tl.ft * 64 + c8) =
                 *reinterpret_cast<const uint4*>(st + j * 64 + c8);
+        }
+      } else if (p.epi == kEpiDownF32) {
+        // fp32 rows acc + bias, unrounded: each warp stages its 32 features x
+        // 16 tokens (2 KB, two alternating buffers in the exchange and
+        // staging areas) and writes 16 rows x 128 bytes with 16-byte stores
+        float* fst = reinterpret_cast<float*>(sbase + p.x_off) + q * 1024;   // [2][16][32] f32 of this warp
+        float* out0 = reinterpret_cast<float*>(p.out) + (long long)tl.row0 * p.ldo;
+        for (int c0 = 0, ci = 0; c0 < ncols; c0 += 16, ++ci) {
+          float acc[16];
+          load_acc(tq + slot * p.nacc * p.bn + c0, p.bn, bank0, p.nacc, p.nbanks, acc);
+          float* st = fst + (ci & 1) * 512;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) st[j * 32 + lane] = acc[j] + b0;
+          __syncwarp();
+          // lane l, pass i: token row (l + 32 i) / 8, features 4 ((l + 32 i) & 7) .. + 3
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = lane + 32 * i;
+            const int j = c0 + (c >> 3);
+            const int fo = tl.ft * 128 + 32 * q + 4 * (c & 7);
+            if (j < tl.nrows && fo < p.n_feat)
+              *reinterpret_cast<float4*>(out0 + (long long)j * p.ldo + fo) =
+                  *reinterpret_cast<const float4*>(st + (c >> 3) * 32 + 4 * (c & 7));
+          }
         }
       } else {
         // Each warp stages its 32 features x 16 tokens in its own buffer

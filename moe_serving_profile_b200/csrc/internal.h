@@ -66,6 +66,11 @@ cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            int scale_rows, const void* weights, int weights_bf16, void* out,
                            long long ld_out);
 
+cudaError_t launch_combine_f32(cudaStream_t st, const float* rows, long long ld_rows,
+                               const int* inverse, const long long* indices, int T, int K, int H,
+                               int lo, int hi, const void* weights, int weights_bf16, void* out,
+                               long long ld_out);
+
 // Exchange-buffer layout of the fused combine + all-reduce (p2p.cu).
 constexpr int kP2PBlocks = 1024;    // block b owns rows t = b (mod 1024)
 constexpr int kP2PMaxRanks = 8;

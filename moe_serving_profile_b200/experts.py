@@ -72,7 +72,8 @@ def run_experts(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
 
 def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K: int,
             num_experts: int, expert_begin: int, b_map_div: int | None = None,
-            tokens: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+            tokens: int | None = None, out: torch.Tensor | None = None,
+            epilogue: int | None = None) -> torch.Tensor:
     """Gated projection of every routed row: act [T*K, I_p] bf16."""
     T = hidden.shape[0] if tokens is None else tokens
     R = perm.perm_src.numel()
@@ -92,8 +93,8 @@ def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K:
                     max_rows=R, wfmt=w.fmt, planes=2, feat_pad=w.i_pad, n_feat=w.inter,
                     k_pad=w.h_k, weight=w.w1, fp8_block=w.block, b_src=b_src,
                     k_valid=hidden.shape[1], b_map=b_map, b_div=b_div,
-                    epilogue=w.gated_epilogue, bias=w.b1, alpha=w.alpha, limit=w.limit, out=act,
-                    token_tile=bn)
+                    epilogue=w.gated_epilogue if epilogue is None else epilogue, bias=w.b1,
+                    alpha=w.alpha, limit=w.limit, out=act, token_tile=bn)
     return act
 
 
@@ -153,6 +154,30 @@ def run_experts_w8a8(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutati
     return contrib
 
 
+def run_experts_mxfp4_efficient(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
+                                weights: torch.Tensor, indices: torch.Tensor, *, K: int, num_experts: int,
+                                expert_begin: int) -> torch.Tensor:
+    """The reference's fused MXFP4 experts (grouped_mxfp4, matmul_ogs with a
+    fused clamped SwiGLU and fp32 biases; moe_serving/efficient_kernels.py:157-206,
+    biases made fp32 at gpt_oss_parallel.py:438-446): the gate/up epilogue
+    works in fp32 and rounds once to bf16, the down projection keeps
+    acc + bias in fp32, and each token's slots are scaled by their routing
+    weights and summed in fp32 in slot order, rounded once. Returns this
+    rank's [T, H] bf16 partial (its experts only)."""
+    T, H = hidden.shape
+    act = gate_up(w, hidden, perm, K=K, num_experts=num_experts, expert_begin=expert_begin, tokens=T,
+                  epilogue=_lib.EPI_CLAMP_SWIGLU_F32)
+    R = perm.perm_src.numel()
+    bn = tile_policy(T, K, num_experts, _max_tile(w))
+    y = torch.empty(R, w.hidden, device=hidden.device, dtype=torch.float32)
+    ops.expert_gemm(offsets=perm.offsets, expert_begin=expert_begin, n_experts=w.n_experts,
+                    max_rows=R, wfmt=w.fmt, planes=1, feat_pad=w.h_f, n_feat=w.hidden,
+                    k_pad=w.i_pad, weight=w.w2, fp8_block=w.block, b_src=act,
+                    k_valid=w.inter, epilogue=_lib.EPI_DOWN_F32, bias=w.b2, out=y, token_tile=bn)
+    return ops.combine_f32(y, perm.inverse, indices, weights, expert_lo=expert_begin,
+                           expert_hi=expert_begin + w.n_experts)
+
+
 def check_inputs(hidden: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor) -> tuple:
     if hidden.dtype != torch.bfloat16:
         raise ValueError(f"b200 experts compute in bfloat16, got hidden {hidden.dtype}")
@@ -180,26 +205,33 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     numerics "fast": each rank combines its own experts and the partial sums
     are all-reduced (moe_serving/qwen3_parallel.py:105-118).
     numerics "efficient": FP8 weights run the W8A8 experts of the reference's
-    grouped_fp8 (moe_serving/efficient_kernels.py:243-274), other formats the
-    weight-only experts (grouped_mxfp4's bf16 x upcast MXFP4, :157-206);
-    combined like "fast".
+    grouped_fp8 (moe_serving/efficient_kernels.py:243-274); GPT-OSS MXFP4
+    weights its fused path (grouped_mxfp4, :157-206: fp32 epilogues and an
+    fp32 slot-order scatter-reduce); both combined like "fast".
     """
     hidden, indices, weights = check_inputs(hidden, indices, weights)
     T, K = indices.shape
     if T == 0:
         return torch.empty_like(hidden)
     size = 1 if parallel is None else parallel.size
+    fused_mx = numerics == "efficient" and w.fmt == _lib.W_MXFP4 and \
+        w.gated_epilogue == _lib.EPI_CLAMP_SWIGLU
     if size == 1 and numerics in ("reference", "fast") or (
-            size == 1 and numerics == "efficient" and w.fmt != _lib.W_FP8):
+            size == 1 and numerics == "efficient" and w.fmt == _lib.W_BF16):
         # one library call: permutation, gather, both GEMMs and the ordered
         # combine (the same kernels and results as the separate calls)
         return ops.expert_layer(w, hidden, indices, weights, num_experts=num_experts,
                                 expert_begin=expert_begin)
     perm = ops.permute(indices, num_experts)
+    if fused_mx:
+        # GPT-OSS MXFP4: the fused path's fp32 epilogues and fp32 slot-order
+        # scatter-reduce (grouped_mxfp4), then the all-reduce of the rank
+        # partials (efficient_kernels.py:206)
+        part = run_experts_mxfp4_efficient(w, hidden, perm, weights, indices, K=K,
+                                           num_experts=num_experts, expert_begin=expert_begin)
+        return part if size == 1 else parallel.reduce(part)
     if numerics == "efficient":
-        # FP8: W8A8 experts (grouped_fp8). MXFP4 / BF16: the weight-only
-        # experts, as matmul_ogs multiplies bf16 activations with upcast
-        # MXFP4 weights (grouped_mxfp4, efficient_kernels.py:157-206). The
+        # FP8: W8A8 experts (grouped_fp8). BF16: the weight-only experts. The
         # rank-local partial sums are all-reduced, the reference's efficient
         # EP exchange (efficient_kernels.py:206, 274).
         run = run_experts_w8a8 if w.fmt == _lib.W_FP8 else run_experts

@@ -220,7 +220,11 @@ def expert_gemm(*, offsets: torch.Tensor, expert_begin: int, n_experts: int, max
                 token_tile: int = 0, split_k: int = 0) -> torch.Tensor:
     device = _dev(weight, "weight")
     _bf16_rows(b_src, "activations")
-    _bf16_rows(out, "output")
+    if epilogue == _lib.EPI_DOWN_F32:
+        if out.dtype != torch.float32 or out.dim() != 2 or out.stride(1) != 1:
+            raise ValueError("the fp32 down epilogue writes a 2D float32 output with contiguous rows")
+    else:
+        _bf16_rows(out, "output")
     a = _lib.GemmArgs()
     a.offsets = _ptr(offsets)
     a.expert_begin = expert_begin
@@ -355,6 +359,26 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *,
         ),
         "combine",
     )
+    return out
+
+
+def combine_f32(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor,
+                *, expert_lo: int = 0, expert_hi: int = 1 << 30,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 out[t] = fp32 sum over the token's slots in order of w * rows[inverse]
+    (fp32 rows of the fp32 down epilogue; b200moe_combine_f32)."""
+    device = _dev(indices, "indices")
+    T, K = indices.shape
+    if rows.dtype != torch.float32 or rows.dim() != 2 or rows.stride(1) != 1:
+        raise ValueError("rows must be a 2D float32 tensor with contiguous rows")
+    H = rows.shape[1]
+    if out is None:
+        out = torch.empty(T, H, device=indices.device, dtype=torch.bfloat16)
+    _bf16_rows(out, "output")
+    check(lib.b200moe_combine_f32(device, _stream(device), _ptr(rows), rows.stride(0), _ptr(inverse),
+                                  _ptr(indices), T, K, H, expert_lo, expert_hi, _ptr(weights),
+                                  int(weights.dtype == torch.bfloat16), _ptr(out), out.stride(0)),
+          "combine_f32")
     return out
 
 

@@ -398,6 +398,35 @@ def gpt_oss_layer(hidden, indices, weights, gu_blocks, gu_scales, gu_bias, dn_bl
     return ordered_expert_merge(hidden, indices, weights, project)
 
 
+def gpt_oss_layer_efficient(hidden, indices, weights, gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales,
+                            dn_bias, alpha, limit):
+    """The reference's efficient GPT-OSS numerics (grouped_mxfp4,
+    moe_serving/efficient_kernels.py:157-206, with biases made fp32 at
+    gpt_oss_parallel.py:438-446), restated from the published algorithm of the
+    fused MXFP4 matmul it calls (the hub kernel is not vendored, so this
+    restatement is not pinned to its outputs): per routed (token, slot), in
+    float64 standing in for fp32 accumulation, gu = x W_gu^T + b_gu; gate =
+    min(gu[0::2], limit), up = clamp(gu[1::2], -limit, limit); the
+    intermediate bf16(gate / (1 + exp(-alpha gate)) * (up + 1)); y = a W_dn^T +
+    b_dn; out[t] = bf16(sum over slots k in order of w[t, k] * y)."""
+    T, K = indices.shape
+    x = hidden.double()
+    out = torch.zeros(T, hidden.shape[1], dtype=torch.float64)
+    wd = weights.double()
+    for e in torch.unique(indices, sorted=True).tolist():
+        rows = torch.nonzero(indices == e)          # (token, slot) pairs, token-major
+        t, k = rows[:, 0], rows[:, 1]
+        wgu = decode_mxfp4_torch(gu_blocks[e], gu_scales[e], torch.float64)   # [2I, H]
+        wdn = decode_mxfp4_torch(dn_blocks[e], dn_scales[e], torch.float64)   # [H, I]
+        gu = x[t] @ wgu.T + gu_bias[e].double()
+        gate = gu[:, 0::2].clamp(max=limit)
+        up = gu[:, 1::2].clamp(min=-limit, max=limit)
+        a = (gate / (1 + torch.exp(-alpha * gate)) * (up + 1)).to(torch.bfloat16).double()
+        y = a @ wdn.T + dn_bias[e].double()
+        out.index_put_((t,), y * wd[t, k, None], accumulate=True)
+    return out.to(torch.bfloat16)
+
+
 def routed_forward_ranks(hiddens, gate_weight, gate_up, down, top_k, renormalize=True,
                          routes=None):
     """moe_serving/moe.py:171-224 (simulate_ranks) with the exchange of

@@ -220,3 +220,58 @@ def test_expert_layer_one_call_equals_separate_calls(cuda, name, T):
     sep = ops.combine(contrib, perm.inverse, idx, order=_lib.ORDER_EXPERT)
     assert torch.equal(one, sep)
     assert _lib.device_status(cuda.index) == 0
+
+
+@pytest.mark.parametrize("T", [16, 2048])
+def test_gpt_oss_efficient_layer_keeps_fp32_intermediates(cuda, T):
+    """numerics="efficient" for GPT-OSS MXFP4 (the reference's fused
+    grouped_mxfp4 path): fp32 gate/up epilogue with fp32 biases and one bf16
+    rounding of the intermediate, fp32 down + bias, fp32 slot-order
+    scatter-reduce. Against the float64 restatement of that algorithm
+    (oracle.gpt_oss_layer_efficient): only fp32 summation order differs, so
+    relative L2 <= 2e-3 and max |error| <= 2^-6 max |ref|."""
+    cfg = S.CONFIGS["gpt-oss-20b"]
+    w = S.make_gpt_oss(cfg, seed=41)
+    x = S.make_hidden(T, cfg.hidden, seed=42 + T)
+    _, scores, idx = oracle.gpt_oss_router(x, w.router, w.router_bias, cfg.top_k)
+    m = gpt_module(cfg, w, cuda, "efficient")
+    out = m(x.to(cuda), idx.to(cuda), scores.to(cuda)).cpu()
+    ref = oracle.gpt_oss_layer_efficient(x, idx, scores, w.gu_blocks, w.gu_scales, w.gu_bias, w.dn_blocks,
+                                         w.dn_scales, w.dn_bias, cfg.alpha, cfg.limit)
+    r, mx = rel_l2(out, ref), max_abs(out, ref)
+    print(f"\ngpt-oss-20b efficient T={T}: rel_l2={r:.2e} max_abs={mx:.2e}")
+    assert out.isfinite().all()
+    assert r <= 2e-3 and mx <= 2 ** -6 * float(ref.float().abs().max())
+    assert _lib.device_status(cuda.index) == 0
+
+
+def test_fp32_down_epilogue_and_slot_order_combine_exact(cuda):
+    """EPI_DOWN_F32 writes acc + bias unrounded and b200moe_combine_f32 sums
+    w * row over a token's slots in fp32: with integer data, integer biases
+    and power-of-two weights every value is exact, so both are bit-exact."""
+    from moe_serving_profile_b200 import layout, ops
+    g = torch.Generator().manual_seed(5)
+    E, H, I, T, K = 4, 256, 192, 40, 2
+    wv = torch.randint(-4, 5, (E, H, I), generator=g).bfloat16()
+    bias = torch.randint(-8, 9, (E, H), generator=g).bfloat16()
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).long()
+    wts = torch.pow(2.0, torch.randint(-3, 2, (T, K), generator=g).float())
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    R = T * K
+    act = torch.zeros(R, 256, dtype=torch.bfloat16)
+    act[:, :I] = torch.randint(-3, 4, (R, I), generator=g).bfloat16()
+    w2 = torch.zeros(E, 256, 256, dtype=torch.bfloat16)
+    w2[:, :H, :I] = wv
+    b2 = torch.zeros(E, 256, dtype=torch.bfloat16)
+    b2[:, :H] = bias
+    y = torch.zeros(R, H, dtype=torch.float32, device=cuda)
+    ops.expert_gemm(offsets=offsets.to(cuda), expert_begin=0, n_experts=E, max_rows=R, wfmt=_lib.W_BF16,
+                    planes=1, feat_pad=256, n_feat=H, k_pad=256, weight=w2.to(cuda), b_src=act.to(cuda),
+                    k_valid=I, epilogue=_lib.EPI_DOWN_F32, bias=b2.to(cuda), out=y)
+    e_of_row = torch.repeat_interleave(torch.arange(E), counts.long())
+    exact = torch.einsum("ri,rhi->rh", act[:, :I].double(), wv.double()[e_of_row]) + bias.double()[e_of_row]
+    assert torch.equal(y.cpu(), exact.float())
+    out = ops.combine_f32(y, inv.to(cuda), idx.to(cuda), wts.to(cuda))
+    want = (exact[inv.long()].view(T, K, H) * wts.double()[..., None]).sum(1)
+    assert torch.equal(out.cpu(), want.to(torch.bfloat16))
+    assert _lib.device_status(cuda.index) == 0

@@ -148,10 +148,10 @@ def test_w8a8_paths_refuse_before_device_work():
 
 
 def test_efficient_numerics_dispatch(monkeypatch):
-    """numerics="efficient" runs the W8A8 experts for FP8 weights and the
-    weight-only experts for MXFP4 / BF16 (the reference's grouped_mxfp4
-    multiplies bf16 activations with upcast MXFP4 weights); GPT-OSS needs
-    MXFP4 storage for it, as the reference's check_runtime does."""
+    """numerics="efficient" runs the W8A8 experts for FP8 weights, the fused
+    MXFP4 path (fp32 epilogues, the reference's grouped_mxfp4) for GPT-OSS
+    MXFP4 weights and the weight-only experts for BF16; GPT-OSS needs MXFP4
+    storage for it, as the reference's check_runtime does."""
     from types import SimpleNamespace
 
     from moe_serving_profile_b200 import experts as X
@@ -163,10 +163,13 @@ def test_efficient_numerics_dispatch(monkeypatch):
     monkeypatch.setattr(X.ops, "combine", lambda contrib, inverse, idx, order: contrib)
     monkeypatch.setattr(X, "run_experts", lambda *a, **k: calls.append("weight_only") or "rows")
     monkeypatch.setattr(X, "run_experts_w8a8", lambda *a, **k: calls.append("w8a8") or "rows")
-    # one GPU: the weight-only formats take the single-call layer
+    # one GPU: BF16 weights take the single-call layer; GPT-OSS MXFP4 the
+    # fused path with fp32 epilogues (grouped_mxfp4)
     monkeypatch.setattr(X.ops, "expert_layer", lambda *a, **k: calls.append("weight_only") or "rows")
-    for fmt, want in ((_lib.W_FP8, "w8a8"), (_lib.W_MXFP4, "weight_only"), (_lib.W_BF16, "weight_only")):
-        out = X.layer_forward(SimpleNamespace(fmt=fmt, n_experts=4), torch.zeros(3, 64, dtype=torch.bfloat16),
+    monkeypatch.setattr(X, "run_experts_mxfp4_efficient", lambda *a, **k: calls.append("mxfp4_f32") or "rows")
+    for fmt, want in ((_lib.W_FP8, "w8a8"), (_lib.W_MXFP4, "mxfp4_f32"), (_lib.W_BF16, "weight_only")):
+        out = X.layer_forward(SimpleNamespace(fmt=fmt, n_experts=4, gated_epilogue=_lib.EPI_CLAMP_SWIGLU),
+                              torch.zeros(3, 64, dtype=torch.bfloat16),
                               torch.zeros(3, 2, dtype=torch.int64), torch.zeros(3, 2), num_experts=4,
                               expert_begin=0, numerics="efficient")
         assert out == "rows" and calls[-1] == want
