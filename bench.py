@@ -443,7 +443,8 @@ def stage_breakdown(cfg, router, packed, xs, parallel, rank, world, stream, reps
 # "replicated": every rank routes all tokens, runs its experts and the
 # contribution rows are gathered over NVLink for the ordered global-expert
 # combine (reference numerics, parallel_numerics.py:13-36).
-EP_LEGS = (("qwen3-235b-a22b", "a2a"), ("gpt-oss-120b", "a2a"), ("gpt-oss-120b", "replicated"))
+EP_LEGS = (("qwen3-30b-a3b", "a2a"), ("qwen3-235b-a22b", "a2a"), ("gpt-oss-120b", "a2a"),
+           ("gpt-oss-120b", "replicated"))
 
 
 def ep_leg(args, name, mode, world, rank, dev, stream, flush, pg):
@@ -461,12 +462,15 @@ def ep_leg(args, name, mode, world, rank, dev, stream, flush, pg):
     local = SimpleNamespace(num_experts=el, weights=packed)
     plan = native.ExpertPlan(E, world, rank)
     a2a = mode == "a2a"
-    shard = {T: (T // world if a2a else T) for T in cfg.batches}
-    coll = native.PeerCollective(max_tokens=max(shard.values())) if (a2a and world > 1) else native.SingleRank()
+    # all-to-all: rank r routes tokens [r T / N, (r + 1) T / N) of each batch
+    # (a batch smaller than N leaves some ranks without tokens)
+    span = {T: ((rank * T) // world, ((rank + 1) * T) // world) if a2a else (0, T) for T in cfg.batches}
+    cap = max(-(-T // world) for T in cfg.batches)
+    coll = native.PeerCollective(max_tokens=cap) if (a2a and world > 1) else native.SingleRank()
     xs = {}
     for T in cfg.batches:
         x = S.make_hidden(T, cfg.hidden, seed=2000 + T, device=dev)
-        xs[T] = x[rank * shard[T]:(rank + 1) * shard[T]].contiguous() if a2a else x
+        xs[T] = x[span[T][0]:span[T][1]].contiguous()
 
     def call(T):
         _, scores, idx = router(xs[T])
@@ -483,7 +487,10 @@ def ep_leg(args, name, mode, world, rank, dev, stream, flush, pg):
             _, scores, idx = router(xs[T])
             if a2a:
                 perm = ops.permute(idx, E)
-                y = X.run_experts(full, xs[T], perm, None, K=K, num_experts=E, expert_begin=0)
+                # the token tile of the all-to-all's GEMMs: the global batch,
+                # estimated as this rank's share times the group size
+                y = X.run_experts(full, xs[T], perm, None, K=K, num_experts=E, expert_begin=0,
+                                  tile_tokens=xs[T].shape[0] * world)
                 ref = ops.combine(y, perm.inverse, idx, order=_lib.ORDER_RANK_SLOT, experts_per_rank=el,
                                   weights=scores.to(torch.bfloat16).contiguous())
             else:
@@ -743,38 +750,56 @@ def main():
     # Copies run on their own streams: every batch's tokens go host -> device
     # on copy_in up front, each output goes device -> host on copy_out as soon
     # as its layer call ends, so transfers overlap other batches' compute.
+    # Device token buffers alternate between two sets, so the next step's
+    # uploads overlap this step's compute. Batches run with the largest in
+    # the middle: its upload hides behind the batches before it and its
+    # download behind those after it; the smallest runs last.
     copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    dev_x = {T: torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=dev) for T in batches}
+    dev_x = [{T: torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=dev) for T in batches}
+             for _ in range(2)]
+    rest = sorted(batches)
+    big = rest.pop()
+    smallest = rest.pop(0) if rest else None
+    second = rest.pop() if rest else None
+    order = rest + [big] + ([second] if second is not None else []) + \
+        ([smallest] if smallest is not None else [])
+    read_done = [None, None]
 
-    def e2e_step():
-        copy_in.wait_stream(stream)   # the previous step's layer calls have read dev_x
+    def e2e_step(i):
+        xs_dev = dev_x[i % 2]
+        if read_done[i % 2] is not None:
+            copy_in.wait_event(read_done[i % 2])   # the layer calls of step i - 2 have read it
         landed = {}
         with torch.cuda.stream(copy_in):
-            for T in batches:
-                dev_x[T].copy_(host_x[T], non_blocking=True)
+            for T in order:
+                xs_dev[T].copy_(host_x[T], non_blocking=True)
                 landed[T] = torch.cuda.Event()
                 landed[T].record(copy_in)
-        for T in batches:
+        for T in order:
             stream.wait_event(landed[T])
             with torch.cuda.stream(stream):
-                o = layer_call(cfg, router, packed, dev_x[T], parallel, rank, world)
+                o = layer_call(cfg, router, packed, xs_dev[T], parallel, rank, world)
             copy_out.wait_stream(stream)
             with torch.cuda.stream(copy_out):
                 host_o[T].copy_(o, non_blocking=True)
                 o.record_stream(copy_out)
-        stream.wait_stream(copy_out)
+        done = torch.cuda.Event()
+        done.record(stream)
+        read_done[i % 2] = done
 
-    for _ in range(2):
-        e2e_step()
+    for i in range(2):
+        e2e_step(i)
+    stream.wait_stream(copy_out)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
     copy_in.wait_stream(stream)   # the timed region starts before the first copy
-    for _ in range(args.steps):
-        e2e_step()
-    e.record(stream)   # after every copy of the last step (stream waited on copy_out)
+    for i in range(args.steps):
+        e2e_step(2 + i)
+    stream.wait_stream(copy_out)
+    e.record(stream)   # after every copy of the last step
     torch.cuda.synchronize(dev)
     e2e_ms = s.elapsed_time(e) / args.steps
     if world > 1:

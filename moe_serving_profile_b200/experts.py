@@ -54,20 +54,25 @@ def _max_tile(w: ExpertWeights) -> int:
 
 def run_experts(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation,
                 weights: torch.Tensor | None, *, K: int, num_experts: int, expert_begin: int,
-                contrib: torch.Tensor | None = None, b_map_div: int | None = None) -> torch.Tensor:
+                contrib: torch.Tensor | None = None, b_map_div: int | None = None,
+                tile_tokens: int | None = None) -> torch.Tensor:
     """Contribution rows [T*K, H] (rows of other ranks' experts are left as given).
 
     ``hidden`` rows are gathered through ``perm.perm_src // K``; ``weights``
     ([T, K], fp32 or bf16) scale the down projection's rows, or are skipped
     when None (the token all-to-all path scales at combine time).
+    ``tile_tokens`` (default: the rows of ``hidden``) is the batch the token
+    tile is chosen for; with the global batch, outputs are bitwise those of
+    one GPU running it whole.
     """
     T, H = hidden.shape
     if H != w.hidden:
         raise ValueError(f"hidden size {H} does not match the experts' {w.hidden}")
+    tokens = T if tile_tokens is None else tile_tokens
     act = gate_up(w, hidden, perm, K=K, num_experts=num_experts, expert_begin=expert_begin,
-                  b_map_div=b_map_div, tokens=T)
+                  b_map_div=b_map_div, tokens=tokens)
     return down(w, act, perm, weights, K=K, num_experts=num_experts, expert_begin=expert_begin,
-                contrib=contrib, tokens=T)
+                contrib=contrib, tokens=tokens)
 
 
 def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K: int,
