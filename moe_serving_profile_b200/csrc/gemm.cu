@@ -648,13 +648,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j) xbuf[(q * 16 + j) * 32 + lane] = acc[j];
           named_bar_sync(1, 128);
           uint16_t* st = stage + (ci & 1) * 16 * 64;     // [16][64]
+          // every exchange read before any staging store: both go through
+          // generic pointers, so interleaved they would serialise on the
+          // compiler's aliasing assumption
+          float gv[8], uv[8];
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
-            const int j = jb + jj;
-            const float g = xbuf[((q & 1) * 16 + j) * 32 + lane];
-            const float u = xbuf[((2 + (q & 1)) * 16 + j) * 32 + lane];
-            const float a = epilogue_gated(p.epi, g, u, bg, bu, p.alpha, p.limit);
-            st[j * 64 + fl] = static_cast<uint16_t>(__float_as_uint(a) >> 16);
+            gv[jj] = xbuf[((q & 1) * 16 + jb + jj) * 32 + lane];
+            uv[jj] = xbuf[((2 + (q & 1)) * 16 + jb + jj) * 32 + lane];
+          }
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const float a = epilogue_gated(p.epi, gv[jj], uv[jj], bg, bu, p.alpha, p.limit);
+            st[(jb + jj) * 64 + fl] = static_cast<uint16_t>(__float_as_uint(a) >> 16);
           }
           named_bar_sync(1, 128);
           const int j = te >> 3;
@@ -698,13 +704,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           float acc[16];
           load_acc(tq + slot * p.nacc * p.bn + c0, p.bn, bank0, p.nacc, p.nbanks, acc);
           uint16_t* st = wst + (ci & 1) * 512;
+          // the chunk's routing weights read before any staging store (generic
+          // pointers: interleaved, each load would wait for the last store)
+          float wv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) wv[j] = scaled ? rowv[c0 + j] : 1.f;
+          uint32_t yb[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float y = bf16_rn(acc[j]);
             if (p.bias != nullptr) y = bf16_rn(y + b0);
-            if (scaled) y = bf16_rn(y * rowv[c0 + j]);
-            st[j * 32 + lane] = static_cast<uint16_t>(__float_as_uint(y) >> 16);
+            if (scaled) y = bf16_rn(y * wv[j]);
+            yb[j] = __float_as_uint(y) >> 16;
           }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) st[j * 32 + lane] = static_cast<uint16_t>(yb[j]);
           __syncwarp();
           // lane l, pass i: chunk row (l + 32 i) / 4, features 8 ((l + 32 i) & 3) .. + 7
 #pragma unroll
