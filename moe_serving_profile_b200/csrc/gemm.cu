@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 32 * kWarpTma) {
     // quantised weights: a raw stage is drained, and an A stage filled, by
     // the four warps of one converter group (a_smem: by all eight)
-    const uint32_t group = p.wfmt == kWBf16 ? 1u : (p.a_smem ? 8u : 4u);
+    const uint32_t group = p.wfmt == kWBf16 ? 1u : ((p.a_smem || p.n_issuers == 1) ? 8u : 4u);
     for (int i = 0; i < p.nr; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], group);
@@ -786,6 +786,63 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(a + swz(row, 4 * h + j)) =
               make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
         fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[ar.idx]);
+        rr.next();
+        ar.next();
+      }
+    }
+  } else if (warp >= kWarpConv && p.wfmt != kWBf16 && p.n_issuers == 1) {
+    // ------------------------------------------------ converters (one issuer)
+    // All eight warps convert every k-block, in order: warp w writes TMEM
+    // lane quarter w % 4 (lane i: weight row 32 (w % 4) + i) and column half
+    // h = (w - 8) / 4 of the A stage (k values 32 h .. 32 h + 31, TMEM
+    // columns 16 h .. 16 h + 15). Half a row per lane halves the latency of a
+    // k-block's conversion against one four-warp group per k-block.
+    const int qw = warp & 3;
+    const int h = (warp - kWarpConv) >> 2;
+    const int row = qw * 32 + lane;
+    const int half = row >> 6;                           // gate/up plane or down half
+    const uint32_t tq = tmem + (static_cast<uint32_t>(qw * 32) << 16) + p.a_col0 + static_cast<uint32_t>(h * 16);
+    Ring rr(p.nr), ar(p.na);
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      for (int kb = 0; kb < p.nkb; ++kb) {
+        if (!wait_spin(&raw_full[rr.idx], rr.phase, p.status, 32) ||
+            !wait_spin(&a_empty[ar.idx], ar.phase ^ 1u, p.status, 32)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* stage = sbase + p.raw_off + rr.idx * p.stage_bytes;
+        uint32_t o[16];
+        if (p.wfmt == kWFp8) {
+          const uint8_t* raw = stage + row * 64;
+          const float* sc = reinterpret_cast<const float*>(stage + kRawFp8);
+          const int sw = (row >> 1) & 3;
+          uint4 qv[2];
+          float scale[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int c = 2 * h + j;
+            qv[j] = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
+            scale[j] = p.scale_form == kScaleHalf ? sc[half] : sc[row * 4 + c];
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) fp8x16_cvt(qv[j], scale[j], *reinterpret_cast<uint32_t(*)[8]>(o + 8 * j));
+        } else {
+          const uint8_t* raw = stage + row * 32;
+          const int sw = (row >> 2) & 1;
+          const uint32_t sx = *reinterpret_cast<const unsigned short*>(stage + kRawMx + row * 2);
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + ((h ^ sw) << 4));
+          mx32_cvt(qv, (sx >> (8 * h)) & 0xffu, o);
+        }
+        // the raw bytes and scales are in registers: release the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rr.idx]);
+        tmem_st16(tq + static_cast<uint32_t>(ar.idx) * kAStageCols, o);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[ar.idx]);
         rr.next();
