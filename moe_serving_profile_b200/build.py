@@ -18,7 +18,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libb200moe.so"
-SOURCES = ["api.cu", "router.cu", "permute.cu", "gemm.cu", "combine.cu", "a2a.cu", "a2a_p2p.cu", "p2p.cu", "w8a8.cu"]
+SOURCES = ["api.cu", "router.cu", "permute.cu", "gemm.cu", "decode.cu", "combine.cu", "a2a.cu", "a2a_p2p.cu", "p2p.cu", "w8a8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

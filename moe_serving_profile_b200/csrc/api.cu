@@ -322,6 +322,66 @@ int b200moe_expert_gemm(int device, void* stream, const b200moe_gemm_args* a) {
   const uint32_t blob_bytes = a->wfmt == B200MOE_W_FP8 ? 8192u + (fp8_half ? 16u : 2048u)
                               : (a->wfmt == B200MOE_W_MXFP4 ? 4096u + 256u : 0u);
   const uint32_t rpb = (blob_bytes + 1023u) & ~1023u;
+  if (a->wfmt != B200MOE_W_BF16 && (bn == 16 || bn == 32) && a->b_map == nullptr) {
+    // short token tiles over contiguous permuted rows: the register-operand
+    // decode kernel (decode.cu). Shared memory: nr weight stages (blob on a
+    // 128-byte boundary), nr token boxes of bn x 128 bytes from a 1024-byte
+    // boundary, the warp pairs' double-buffered accumulator exchange (4
+    // pairs x 2 x 32 lanes x bn / 2 floats), then full/empty barriers per stage,
+    // the tile total and the tile prefix.
+    b200::DecodeParams d{};
+    d.offsets = a->offsets;
+    d.expert_begin = a->expert_begin;
+    d.n_experts = a->n_experts;
+    d.bn = bn;
+    d.wfmt = a->wfmt;
+    d.gated = gated ? 1 : 0;
+    d.feat_tiles = feat_tiles;
+    d.feat_pad = a->feat_pad;
+    d.n_feat = a->n_feat;
+    d.nkb = a->k_pad / 64;
+    d.wblob = static_cast<const uint8_t*>(a->weight);
+    d.blob_bytes = blob_bytes;
+    d.scale_form = a->wfmt == B200MOE_W_MXFP4 ? 2 : (fp8_half ? 0 : 1);
+    d.epi = a->epilogue;
+    d.bias = static_cast<const __nv_bfloat16*>(a->bias);
+    d.alpha = a->alpha;
+    d.limit = a->limit;
+    d.row_w = a->row_weight;
+    d.row_w_bf16 = a->row_weight_bf16;
+    d.row_src = a->row_src;
+    d.out = a->out;
+    d.ldo = a->ldo;
+    d.status = sp;
+    d.stage_bytes = (blob_bytes + 127u) & ~127u;
+    const uint32_t tok_stage = static_cast<uint32_t>(bn) * 128u;
+    const uint32_t xb = 4u * 2u * 32u * static_cast<uint32_t>(bn) * 4u;
+    const uint32_t tail = 8u + 4u * static_cast<uint32_t>(a->n_experts + 1);
+    const uint32_t room = b200::kDecodeSmemMax - 1024u - 1024u - xb - tail;
+    d.nr = std::min<int>(32, static_cast<int>(room / (d.stage_bytes + tok_stage + 16u))) & ~1;
+    if (d.nr < 4) return fail(B200MOE_ERR_UNSUPPORTED, "decode shared memory plan does not fit");
+    d.tok_off = (static_cast<uint32_t>(d.nr) * d.stage_bytes + 1023u) & ~1023u;
+    d.x_off = d.tok_off + static_cast<uint32_t>(d.nr) * tok_stage;
+    d.bar_off = d.x_off + xb;
+    const uint32_t smem = d.bar_off + 16u * static_cast<uint32_t>(d.nr) + tail + 1024u;   // + alignment slack
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    CUtensorMap tmap;
+    std::memset(&tmap, 0, sizeof(tmap));
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a->k_valid), static_cast<cuuint64_t>(a->b_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a->ldb) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(bn)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a->b_src), dims, strides, box,
+                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "activation tensor map failed (%d)", (int)cr);
+    const int grid = static_cast<int>(std::min<long long>(g_sm_count[device], tiles_ub));
+    const int e = b200::launch_decode_gemm(tmap, d, grid, smem, static_cast<cudaStream_t>(stream));
+    if (e != 0) return fail(B200MOE_ERR_CUDA, "decode GEMM launch failed: %s",
+                            cudaGetErrorString(static_cast<cudaError_t>(e)));
+    return B200MOE_OK;
+  }
   const uint32_t a_stage = 128u * 128u;
   const uint32_t b_stage = static_cast<uint32_t>(bn) * 128u;
   // epilogue: exchange buffer (8 KB), two bf16 staging chunks (8 KB), row weights (1 KB)
@@ -782,7 +842,10 @@ LayerPlan layer_plan(const b200moe_layer_args* a) {
   LayerPlan p{};
   p.R = a->T * a->K;
   p.bn = layer_tile(a->T, a->K, a->E, a->wfmt);
-  p.gather = p.bn >= 64;
+  // permuted rows gathered once: for large tiles (plain 2D TMA tiles
+  // instead of per-row gathers) and for the decode kernel of quantised
+  // weights, which reads contiguous rows only
+  p.gather = p.bn >= 64 || a->wfmt != B200MOE_W_BF16;
   const size_t R = static_cast<size_t>(p.R);
   const size_t i_pad = static_cast<size_t>((a->I + 127) / 128 * 128);
   const size_t h_k = static_cast<size_t>((a->H + 63) / 64 * 64);

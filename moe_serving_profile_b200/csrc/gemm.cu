@@ -31,6 +31,7 @@
 //               + 31) that tcgen05.mma reads as its A operand. Four A stages
 //               per group let a group run ahead of the MMA's consumption.
 // All rings are phase-tracked mbarriers; every wait is bounded (see ptx.cuh).
+#include "expert_math.cuh"
 #include "gemm_params.h"
 #include "ptx.cuh"
 
@@ -47,13 +48,7 @@ constexpr int kWarpB = 2;
 constexpr int kWarpEpi = 4;      // warps 4..7
 constexpr int kWarpConv = 8;     // warps 8..15
 constexpr uint32_t kATile = 128u * 128u;    // 128 rows x 64 bf16
-constexpr uint32_t kRawFp8 = 128u * 64u;    // 128 rows x 64 e4m3
-constexpr uint32_t kRawMx = 128u * 32u;     // 128 rows x 64 e2m1
 constexpr uint32_t kAStageCols = 32;        // TMEM columns per A stage (64 bf16 / lane)
-enum { kScaleHalf = 0, kScaleChunk = 1, kScaleMx = 2 };
-
-enum { kWBf16 = 0, kWFp8 = 1, kWMx = 2 };
-enum { kEpiSwiglu = 0, kEpiClamp = 1, kEpiDown = 2, kEpiClampF32 = 3, kEpiDownF32 = 4 };
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -111,65 +106,6 @@ __device__ __forceinline__ int tile_n(const Tile& tl, const GemmParams& p) {
   return p.a_smem ? ((tl.nrows + 15) & ~15) : p.bn;
 }
 
-// 2^(s-127) as the fp32 value torch's ldexp multiplies by (exact, including
-// the subnormal s = 0 and the overflow s = 255).
-__device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
-  if (s == 0u) return __uint_as_float(0x00400000u);
-  if (s == 255u) return __uint_as_float(0x7f800000u);
-  return __uint_as_float(s << 23);
-}
-
-// Two f16 (one word, element 0 low) -> two fp32 (exact).
-__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& x, float& y) {
-  asm("{\n\t.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
-      "cvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
-      : "=f"(x), "=f"(y) : "r"(h));
-}
-
-// 16 e4m3 -> 16 bf16 = bf16(fp32(w) * scale) through the hardware e4m3 -> f16
-// conversion (exact), an exact f16 -> fp32 widening, one fp32 multiply and
-// one round to bf16: the reference's arithmetic for every scale.
-__device__ __forceinline__ void fp8x16_cvt(const uint4& q, float scale, uint32_t (&o)[8]) {
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t h01, h23;
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
-        : "=r"(h01), "=r"(h23) : "r"(w[i]));
-    float a0, a1, a2, a3;
-    f16x2_to_f32(h01, a0, a1);
-    f16x2_to_f32(h23, a2, a3);
-    mul2_f32(a0, a1, scale);
-    mul2_f32(a2, a3, scale);
-    o[2 * i] = pack_bf16x2(a0, a1);
-    o[2 * i + 1] = pack_bf16x2(a2, a3);
-  }
-}
-
-// 32 e2m1 (16 bytes, element 0 in the low nibble) -> 32 bf16 =
-// e2m1 * 2^(S-127) through the hardware e2m1 -> f16 conversion (exact); the
-// power-of-two scale and the bf16 rounding are exact too.
-__device__ __forceinline__ void mx32_cvt(const uint4& q, uint32_t sexp, uint32_t (&o)[16]) {
-  const float s = ue8m0_to_f32(sexp);
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t h[4];
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3]) : "r"(w[i]));
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      float lo, hi;
-      f16x2_to_f32(h[b], lo, hi);
-      mul2_f32(lo, hi, s);
-      o[4 * i + b] = pack_bf16x2(lo, hi);
-    }
-  }
-}
-
 // 16 accumulator columns of this thread's TMEM lane summed over the banks
 // the tile wrote (bank b at column offset b * stride): bank0, bank0 + 1, ...
 // (mod nacc), nbanks of them, in that order.
@@ -189,51 +125,27 @@ __device__ __forceinline__ void load_acc(uint32_t taddr, int stride, int bank0, 
   }
 }
 
-__device__ __forceinline__ float silu_bf16(float g) { return bf16_rn(g / (1.f + expf(-g))); }
-
-__device__ __forceinline__ float epilogue_gated(int epi, float g, float u, float bg, float bu,
-                                                float alpha, float limit) {
-  if (epi == kEpiSwiglu) {
-    const float gb = bf16_rn(g);
-    const float ub = bf16_rn(u);
-    return bf16_rn(silu_bf16(gb) * ub);
-  }
-  if (epi == kEpiClampF32) {
-    // fp32 throughout, one rounding: fp32 accumulator + fp32 bias, clamp,
-    // gate * sigmoid(alpha * gate) * (up + 1)
-    float gf = g + bg;
-    float uf = u + bu;
-    gf = gf > limit ? limit : gf;
-    uf = uf < -limit ? -limit : (uf > limit ? limit : uf);
-    const float sg = gf / (1.f + expf(-alpha * gf));
-    return bf16_rn(sg * (uf + 1.f));
-  }
-  float gb = bf16_rn(bf16_rn(g) + bg);
-  float ub = bf16_rn(bf16_rn(u) + bu);
-  gb = gb > limit ? limit : gb;
-  ub = ub < -limit ? -limit : (ub > limit ? limit : ub);
-  const float t1 = bf16_rn(gb * alpha);
-  const float t2 = bf16_rn(1.f / (1.f + expf(-t1)));
-  const float glu = bf16_rn(gb * t2);
-  const float t3 = bf16_rn(ub + 1.f);
-  return bf16_rn(t3 * glu);
-}
-
-// MMA issuer of single-issuer launches (one accumulator bank). It waits once
-// for G consecutive k-blocks' A and B stages, then issues their 4G MMAs and G
-// stage releases as straight-line code, specialised at compile time on where
-// A lives and on whether one commit releases both rings. Measured in isolation at 160-token
-// tiles: a barrier wait and tensor fence before every k-block leave the
-// tensor pipe idle about 160 of every 480 cycles (320 cycles of MMAs), one
-// per two k-blocks about 40; conditional branches between MMAs cost the
-// issuing thread tens of cycles each.
+// MMA issuer j of `step` (1 or 2). Issuer j takes the CTA's k-blocks
+// i = j, j + step, ... (A / B stages j + step * r) and accumulates k-block i
+// into bank i % nacc of the tile's slot (nacc = 1, 2 or 4; with two issuers
+// nacc is even, so the two never share a bank). It waits once for G of its
+// k-blocks' A and B stages, then issues their 4G MMAs and G stage releases
+// as straight-line code, specialised at compile time on where A lives and on
+// whether one commit releases both rings. Measured in isolation: a barrier
+// wait and tensor fence before every k-block leave the tensor pipe idle
+// about 160 of every 480 cycles at 160-token tiles, one per two k-blocks
+// about 40; a conditional branch between MMAs costs the issuing thread tens
+// of cycles (a loop with one runtime-conditional commit: 443 against 227
+// cycles per k-block of 16-token MMAs); one thread issues a 16..64-token
+// k-block in about 227 cycles, two together one per 156..192 cycles.
 template <bool kTmemA, bool kJoint, int G>
 __device__ void mma_issue_groups(const GemmParams& p, uint32_t tmem, uint32_t base_u32, const int* prefix,
                                 int total, uint64_t* a_full, uint64_t* a_empty, uint64_t* b_full,
                                 uint64_t* b_empty, uint64_t* acc_full, uint64_t* acc_empty,
-                                uint64_t* mma_done) {
-  Ring ra(p.na), rb(p.nb);
+                                uint64_t* mma_done, int j, int step) {
+  Ring ra(p.na / step), rb(p.nb / step);
   int tc = 0;
+  int i0 = 0;   // CTA-wide index of the tile's first k-block
   bool ok = true;
   auto kblock = [&](uint32_t d, int sa, int sb, uint32_t idesc, uint32_t acc) {
     const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + static_cast<uint32_t>(sb * p.bn * 128));
@@ -245,23 +157,25 @@ __device__ void mma_issue_groups(const GemmParams& p, uint32_t tmem, uint32_t ba
     umma_commit(&a_empty[sa]);
     if (!kJoint) umma_commit(&b_empty[sb]);
   };
-  for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc) {
+  for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc, i0 += p.nkb) {
     const int slot = p.acc_slots == 2 ? (tc & 1) : 0;
     const uint32_t use = p.acc_slots == 2 ? static_cast<uint32_t>(tc >> 1) : static_cast<uint32_t>(tc);
     const uint32_t idesc = idesc_bf16_f32(128, tile_n(decode_tile(t, prefix, p), p));
     if (!wait_bounded(&acc_empty[slot], (use & 1u) ^ 1u, p.status)) break;
     tc_fence_after();
-    const uint32_t d = tmem + static_cast<uint32_t>(slot * p.bn);
-    for (int kb = 0; kb < p.nkb; kb += G) {
-      const int n = min(G, p.nkb - kb);
+    const uint32_t d0 = tmem + static_cast<uint32_t>(slot * p.nacc * p.bn);
+    const int kb0 = (j - i0) & (step - 1);                     // this issuer's first k-block
+    const int mine = kb0 < p.nkb ? (p.nkb - kb0 + step - 1) / step : 0;
+    for (int m = 0; m < mine; m += G) {
+      const int n = min(G, mine - m);
       int sa[G], sb[G];
 #pragma unroll
       for (int i = 0; i < G; ++i) {
-        sa[i] = ra.idx;
-        sb[i] = rb.idx;
+        sa[i] = j + step * ra.idx;
+        sb[i] = j + step * rb.idx;
         if (i < n) {
-          if (ok && (!wait_bounded(&a_full[ra.idx], ra.phase, p.status) ||
-                     !wait_bounded(&b_full[rb.idx], rb.phase, p.status)))
+          if (ok && (!wait_bounded(&a_full[sa[i]], ra.phase, p.status) ||
+                     !wait_bounded(&b_full[sb[i]], rb.phase, p.status)))
             ok = false;
           ra.next();
           rb.next();
@@ -269,11 +183,19 @@ __device__ void mma_issue_groups(const GemmParams& p, uint32_t tmem, uint32_t ba
       }
       if (!ok) break;
       tc_fence_after();
+      // bank and accumulate flag of each k-block: arithmetic, no branches
+      uint32_t d[G], acc[G];
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const int kb = kb0 + (m + i) * step;
+        d[i] = d0 + static_cast<uint32_t>(((i0 + kb) & (p.nacc - 1)) * p.bn);
+        acc[i] = kb >= p.nacc ? 1u : 0u;   // a bank's first k-block of the tile overwrites
+      }
       if (n == G) {
 #pragma unroll
-        for (int i = 0; i < G; ++i) kblock(d, sa[i], sb[i], idesc, (kb + i) > 0 ? 1u : 0u);
+        for (int i = 0; i < G; ++i) kblock(d[i], sa[i], sb[i], idesc, acc[i]);
       } else {
-        for (int i = 0; i < n; ++i) kblock(d, sa[i], sb[i], idesc, (kb + i) > 0 ? 1u : 0u);
+        for (int i = 0; i < n; ++i) kblock(d[i], sa[i], sb[i], idesc, acc[i]);
       }
     }
     if (!ok) break;
@@ -413,103 +335,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // With two issuers, issuer j (warp 1 or 3) takes the CTA's k-blocks
     // i = j, j + 2, ... (the A stages converter group j fills) and
     // accumulates k-block i into bank i % nacc (nacc even), so the two never
-    // share an accumulator; each one alone costs about 75 cycles per MMA of
-    // issue time, two overlap. Both commit to acc_full.
-    if (lane == 0 && p.n_issuers == 1 && p.nacc == 1) {
+    // share an accumulator; one thread issues a short-tile k-block in about
+    // 227 cycles, two together one per 156..192. Both commit to acc_full.
+    if (lane == 0) {
       const bool tmem_a = p.wfmt != kWBf16 && !p.a_smem;
+      const int j = warp == kWarpMma ? 0 : 1;
 #define B200_ISSUE(TA, J)                                                                           \
   mma_issue_groups<TA, J, 2>(p, tmem, base_u32, prefix, total, a_full, a_empty, b_full, b_empty, acc_full, \
-                             acc_empty, mma_done)
+                             acc_empty, mma_done, j, p.n_issuers)
       if (tmem_a && p.joint_ab) B200_ISSUE(true, true);
       else if (tmem_a) B200_ISSUE(true, false);
       else if (p.joint_ab) B200_ISSUE(false, true);
       else B200_ISSUE(false, false);
 #undef B200_ISSUE
-    } else if (lane == 0) {
-      const int step = p.n_issuers;
-      const int j = warp == kWarpMma ? 0 : 1;
-      uint32_t idesc = idesc_bf16_f32(128, p.bn);
-      Ring ra(p.na / step), rb(p.nb / step);
-      int tc = 0;
-      int i0 = 0;   // CTA-wide index of the tile's first k-block
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++tc, i0 += p.nkb) {
-        // accumulator slots: two (the epilogue of tile t overlaps the main
-        // loop of tile t + 1) or one when a 256-token tile fills them both
-        const int slot = p.acc_slots == 2 ? (tc & 1) : 0;
-        const uint32_t use = p.acc_slots == 2 ? static_cast<uint32_t>(tc >> 1) : static_cast<uint32_t>(tc);
-        if (p.a_smem) idesc = idesc_bf16_f32(128, tile_n(decode_tile(t, prefix, p), p));
-        if (!wait_bounded(&acc_empty[slot], (use & 1u) ^ 1u, p.status)) break;
-        tc_fence_after();
-        // tile slot `slot` owns accumulator banks slot * nacc .. + nacc - 1.
-        // Stages are released two of this issuer's k-blocks at a time: a
-        // commit costs about as much as an MMA, back-to-back commits about one.
-        const uint32_t d0 = tmem + static_cast<uint32_t>(slot * p.nacc * p.bn);
-        int pa0 = 0, pa1 = 0, pb0 = 0, pb1 = 0, npend = 0;
-        const int kb0 = (j - i0) & (step - 1);   // step is 1 or 2
-        // readiness of the next k-block's A and B is probed before this
-        // k-block's MMAs are issued, so the barrier read's latency overlaps
-        // the MMA issue; the blocking wait runs only if the probe said no
-        bool ready = false;
-        for (int kb = kb0; kb < p.nkb; kb += step) {
-          const int bank = (i0 + kb) & (p.nacc - 1);   // nacc is 1, 2 or 4
-          const bool first = kb < p.nacc;   // this bank's first k-block of the tile
-          const uint32_t d = d0 + static_cast<uint32_t>(bank * p.bn);
-          const int sa = j + step * ra.idx, sb = j + step * rb.idx;
-          if (!ready && (!wait_spin(&a_full[sa], ra.phase, p.status) ||
-                         !wait_spin(&b_full[sb], rb.phase, p.status))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          Ring na_ = ra, nb_ = rb;   // the next k-block's stages, probed during this one's MMAs
-          na_.next();
-          nb_.next();
-          const bool more = kb + step < p.nkb;
-          const uint64_t bdesc = sdesc_k_sw128(base_u32 + p.b_off + sb * p.bn * 128);
-          if (p.wfmt == kWBf16 || p.a_smem) {
-            ready = more && mbar_test_wait(&a_full[j + step * na_.idx], na_.phase) &&
-                    mbar_test_wait(&b_full[j + step * nb_.idx], nb_.phase);
-            const uint64_t adesc = sdesc_k_sw128(base_u32 + p.a_off + sa * kATile);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
-          } else {
-            const uint32_t at = tmem + p.a_col0 + static_cast<uint32_t>(sa) * kAStageCols;
-            // without a next k-block in this tile the probe reads the current,
-            // completed barriers and its answer is discarded
-            const bool probe = umma_k64_tmem_a_probe(
-                d, at, bdesc, idesc, first ? 0u : 1u,
-                more ? &a_full[j + step * na_.idx] : &a_full[sa], more ? na_.phase : ra.phase,
-                more ? &b_full[j + step * nb_.idx] : &b_full[sb], more ? nb_.phase : rb.phase);
-            ready = more && probe;
-          }
-          if (npend == 0) {
-            pa0 = sa;
-            pb0 = sb;
-          } else {
-            pa1 = sa;
-            pb1 = sb;
-          }
-          ++npend;
-          ra.next();
-          rb.next();
-          if (npend == 2 || p.a_smem || kb + step >= p.nkb) {
-            umma_commit(&a_empty[pa0]);
-            if (npend == 2) umma_commit(&a_empty[pa1]);
-            if (!p.joint_ab) {
-              umma_commit(&b_empty[pb0]);
-              if (npend == 2) umma_commit(&b_empty[pb1]);
-            }
-            npend = 0;
-          }
-        }
-        if (!ok) break;
-        umma_commit(&acc_full[slot]);
-      }
-      // all issued MMAs have finished before TMEM is released
-      umma_commit(mma_done);
-      wait_bounded(mma_done, 0, p.status);
     }
   } else if (warp == kWarpB) {
     // ------------------------------------------------ token-row TMA producer

@@ -1,7 +1,9 @@
 // Kernel parameters of the grouped expert GEMM (host-filled, passed by value).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace b200 {
@@ -68,5 +70,45 @@ struct GemmParams {
 
 // Address of the grouped GEMM kernel (for cudaLaunchKernelExC).
 const void* gemm_kernel_ptr();
+
+// Kernel parameters of the register-operand decode GEMM (quantised weights,
+// token tiles of 16 or 32 rows). Weights, epilogue and tile order as
+// GemmParams; token rows are contiguous permuted rows, read through a 2D
+// tensor map (64-column boxes of bn rows, 128-byte swizzle).
+struct DecodeParams {
+  const int* offsets;
+  int expert_begin, n_experts;
+  int bn;            // 16 or 32 token rows per tile
+  int wfmt, gated, feat_tiles, feat_pad, n_feat, nkb;
+  const uint8_t* wblob;
+  uint32_t blob_bytes;
+  int scale_form;
+  int epi;
+  const __nv_bfloat16* bias;
+  float alpha, limit;
+  const void* row_w;
+  int row_w_bf16;
+  const int* row_src;
+  void* out;
+  long long ldo;
+  int* status;
+  // ring of nr stages (nr even): weight blobs every stage_bytes from 0, the
+  // token boxes (bn x 128 bytes each) from tok_off (1024-byte aligned); the
+  // warp pairs' accumulator exchange at x_off; barriers and the tile prefix
+  // at bar_off
+  int nr;
+  uint32_t stage_bytes, tok_off, x_off, bar_off;
+};
+
+// Largest dynamic shared memory of a decode GEMM launch, and the device
+// ordinals the launcher tracks.
+constexpr uint32_t kDecodeSmemMax = 232448u - 1024u;
+constexpr int kDecodeMaxDevices = 64;
+
+// Launch the decode GEMM: one CTA of 576 threads per SM, smem bytes of
+// dynamic shared memory (at most kDecodeSmemMax), tmap the token rows'
+// tensor map. Returns a cudaError_t.
+int launch_decode_gemm(const CUtensorMap& tmap, const DecodeParams& p, int grid, uint32_t smem,
+                       cudaStream_t stream);
 
 }  // namespace b200

@@ -321,40 +321,6 @@ B200_DEVI void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc
       : "memory");
 }
 
-// Four umma_bf16_tmem_a of one 64-column k-block (A columns a, a+8, a+16,
-// a+24; B descriptor advanced by 32 bytes per MMA; the first accumulates
-// only if acc0 != 0), with the test_waits of two mbarriers issued ahead of
-// them: returns whether both phases had completed. The barrier reads are in
-// flight while the MMAs issue instead of stalling the thread before them.
-B200_DEVI bool umma_k64_tmem_a_probe(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                     uint32_t acc0, uint64_t* bar_a, uint32_t pa, uint64_t* bar_b,
-                                     uint32_t pb) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred qa, qb, q0, qt;\n\t.reg .b64 bd;\n\t.reg .b32 ta;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 qa, [%1], %2;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 qb, [%3], %4;\n\t"
-      "setp.ne.b32 q0, %9, 0;\n\t"
-      "setp.eq.b32 qt, %8, %8;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%5], [%6], %7, %8, q0;\n\t"
-      "add.s64 bd, %7, 2;\n\t"
-      "add.u32 ta, %6, 8;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%5], [ta], bd, %8, qt;\n\t"
-      "add.s64 bd, bd, 2;\n\t"
-      "add.u32 ta, ta, 8;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%5], [ta], bd, %8, qt;\n\t"
-      "add.s64 bd, bd, 2;\n\t"
-      "add.u32 ta, ta, 8;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%5], [ta], bd, %8, qt;\n\t"
-      "and.pred qa, qa, qb;\n\t"
-      "selp.u32 %0, 1, 0, qa;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar_a)), "r"(pa), "r"(smem_u32(bar_b)), "r"(pb), "r"(tmem_d), "r"(tmem_a),
-        "l"(bdesc), "r"(idesc), "r"(acc0)
-      : "memory");
-  return ok != 0;
-}
-
 // The four K = 16 MMAs of one 64-column k-block, in one asm block: A from
 // tensor memory (columns a, a + 8, a + 16, a + 24) and B by its shared-memory
 // descriptor (advanced 32 bytes per MMA); the first accumulates iff acc != 0.
@@ -471,6 +437,36 @@ B200_DEVI void st_cluster_f32x4(uint32_t addr, float a, float b, float c, float 
                "f"(c), "f"(d)
                : "memory");
 }
+
+// ---------------------------------------------------------------- register-operand MMA
+// D += A (16 x 16 bf16, row-major fragments) x B (16 x 8 bf16, column-major
+// fragments), fp32 accumulators. Lane l holds group g = l / 4, t = l % 4:
+// a0 = A[g][2t..2t+1], a1 = A[g+8][2t..2t+1], a2 = A[g][2t+8..+9],
+// a3 = A[g+8][2t+8..+9]; b0 = B[2t..2t+1][g], b1 = B[2t+8..+9][g];
+// d0, d1 = D[g][2t..2t+1], d2, d3 = D[g+8][2t..2t+1].
+B200_DEVI void mma_16816_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 16-byte global -> shared copy through L2 (cp.async.cg); the bytes past
+// src_bytes (0..16) are zero-filled.
+B200_DEVI void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued so far has
+// landed (counts toward the barrier's expected arrivals).
+B200_DEVI void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+B200_DEVI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // ---------------------------------------------------------------- numerics
 // Round-to-nearest-even float -> bf16, returned as a float holding the bf16

@@ -86,9 +86,10 @@ def gate_up(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutation, *, K:
     bn = tile_policy(T, K, num_experts, _max_tile(w))
     div = K if b_map_div is None else b_map_div
     act = torch.empty(R, w.i_pad, device=dev, dtype=torch.bfloat16) if out is None else out
-    if bn >= 64:
-        # large token tiles: gather the routed rows once into permuted order
-        # so the GEMM reads them as plain 2D tiles instead of per-row gathers
+    if bn >= 64 or w.fmt != _lib.W_BF16:
+        # gather the routed rows once into permuted order: large token tiles
+        # read them as plain 2D tiles instead of per-row gathers, and the
+        # decode kernel of quantised weights reads contiguous rows only
         b_src = ops.gather_rows(hidden, perm.perm_src, div, offsets=perm.offsets,
                                 expert_lo=expert_begin, expert_hi=expert_begin + w.n_experts)
         b_map, b_div = None, 1
