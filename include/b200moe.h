@@ -302,6 +302,24 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
                     int scale_rows, const void* weights, int weights_bf16, void* out,
                     long long ld_out);
 
+/* The shared expert as one more routed slot of every token (the shared
+ * expert of moe_serving/moe.py:84-95, added to the routed output at
+ * moe.py:161-162), so that one permutation, one pair of grouped GEMMs and
+ * one combine cover both: for t < T,
+ *   out_indices[t][k] = indices[t][k], out_weights[t][k] = bf16(weights[t][k])
+ *     for k < K (weights fp32 or bf16 [T][K]);
+ *   out_indices[t][K] = shared_expert,
+ *   out_weights[t][K] = bf16(1 / (1 + exp(-f32(score_logit[t * ld_logit]))))
+ *     (score_logit: the bf16 [T, 1] output of F.linear(hidden, score); the
+ *     value torch.sigmoid gives for it).
+ * out_indices int64 [T][K+1], out_weights bf16 [T][K+1]. K < 32. With the
+ * shared expert packed as expert shared_expert of the launch and the combine
+ * in RANK_SLOT order over K + 1 slots, the result is bitwise the routed sum
+ * plus the shared expert's output (one more bf16 add). */
+int b200moe_append_shared_slot(int device, void* stream, const long long* indices, const void* weights,
+                               int weights_bf16, const void* score_logit, long long ld_logit, int T, int K,
+                               long long shared_expert, long long* out_indices, void* out_weights);
+
 /* The scatter-reduce of the reference's fused MXFP4 path (matmul_ogs with
  * gammas and a scatter index, efficient_kernels.py:195-205), replacing the
  * index_add_-order combine there: rows are the fp32 outputs of

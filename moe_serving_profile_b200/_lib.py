@@ -38,6 +38,7 @@ EXPORTED = (
     "b200moe_w8a8_gemm",
     "b200moe_combine",
     "b200moe_combine_f32",
+    "b200moe_append_shared_slot",
     "b200moe_gather_rows",
     "b200moe_gather_rows_range",
     "b200moe_a2a_recv_plan",
@@ -178,6 +179,11 @@ def _load() -> ctypes.CDLL:
     lib.b200moe_combine_f32.argtypes = [
         c_int, c_void_p, c_void_p, c_longlong, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
         c_void_p, c_int, c_void_p, c_longlong,
+    ]
+    lib.b200moe_append_shared_slot.restype = c_int
+    lib.b200moe_append_shared_slot.argtypes = [
+        c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_longlong, c_int, c_int, c_longlong, c_void_p,
+        c_void_p,
     ]
     lib.b200moe_gather_rows.restype = c_int
     lib.b200moe_gather_rows.argtypes = [

@@ -670,6 +670,20 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
   return B200MOE_OK;
 }
 
+int b200moe_append_shared_slot(int device, void* stream, const long long* indices, const void* weights,
+                               int weights_bf16, const void* score_logit, long long ld_logit, int T, int K,
+                               long long shared_expert, long long* out_indices, void* out_weights) {
+  B200_CHECK(T >= 0 && K >= 1 && K < 32, "bad sizes (1 <= K < 32)");
+  B200_CHECK(shared_expert >= 0 && ld_logit >= 1, "bad shared expert id or logit stride");
+  if (T == 0) return B200MOE_OK;
+  B200_CHECK(indices && weights && score_logit && out_indices && out_weights, "all pointers are required");
+  int rc = use_device(device, nullptr);
+  if (rc) return rc;
+  B200_CUDA(b200::launch_append_shared_slot(static_cast<cudaStream_t>(stream), indices, weights, weights_bf16,
+                                            score_logit, ld_logit, T, K, shared_expert, out_indices, out_weights));
+  return B200MOE_OK;
+}
+
 int b200moe_combine_f32(int device, void* stream, const float* rows, long long ld_rows,
                         const int* inverse, const long long* indices, int T, int K, int H,
                         int expert_lo, int expert_hi, const void* weights, int weights_bf16, void* out,

@@ -155,6 +155,31 @@ __global__ void __launch_bounds__(128) gather_rows_range_kernel(
   }
 }
 
+// The shared expert as one more routed slot of every token: slot K of row t
+// is expert `shared` with weight bf16(1 / (1 + exp(-f32(logit[t])))), the
+// value torch.sigmoid gives for the bf16 score logit; slots 0..K-1 copy the
+// routed expert ids and their weights rounded to bf16.
+__global__ void __launch_bounds__(256) append_shared_slot_kernel(
+    const long long* __restrict__ indices, const void* __restrict__ weights, int weights_bf16,
+    const __nv_bfloat16* __restrict__ logit, long long ld_logit, int T, int K, long long shared,
+    long long* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_w) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int K1 = K + 1;
+  if (i >= (long long)T * K1) return;
+  const long long t = i / K1;
+  const int k = static_cast<int>(i - t * K1);
+  if (k < K) {
+    const long long j = t * K + k;
+    out_idx[i] = indices[j];
+    out_w[i] = weights_bf16 ? reinterpret_cast<const __nv_bfloat16*>(weights)[j]
+                            : __float2bfloat16_rn(reinterpret_cast<const float*>(weights)[j]);
+  } else {
+    const float x = __bfloat162float(logit[t * ld_logit]);
+    out_idx[i] = shared;
+    out_w[i] = __float2bfloat16_rn(1.f / (1.f + expf(-x)));
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_gather_rows_range(cudaStream_t st, const void* src, long long ld_src,
@@ -200,4 +225,17 @@ cudaError_t launch_gather_rows(cudaStream_t st, const void* src, long long ld_sr
   return cudaGetLastError();
 }
 
+cudaError_t launch_append_shared_slot(cudaStream_t st, const long long* indices, const void* weights,
+                                      int weights_bf16, const void* logit, long long ld_logit, int T, int K,
+                                      long long shared, long long* out_idx, void* out_w) {
+  const long long n = (long long)T * (K + 1);
+  if (n == 0) return cudaSuccess;
+  append_shared_slot_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
+      indices, weights, weights_bf16, static_cast<const __nv_bfloat16*>(logit), ld_logit, T, K, shared, out_idx,
+      static_cast<__nv_bfloat16*>(out_w));
+  return cudaGetLastError();
+}
+
+
 }  // namespace b200
+

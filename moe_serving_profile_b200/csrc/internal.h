@@ -60,6 +60,9 @@ cudaError_t launch_a2a_recv_plan(cudaStream_t st, const int* counts, int ep, int
                                  int* offsets, int* map_in, int* map_back, int sm_count,
                                  int* status);
 
+cudaError_t launch_append_shared_slot(cudaStream_t st, const long long* indices, const void* weights,
+                                      int weights_bf16, const void* logit, long long ld_logit, int T, int K,
+                                      long long shared, long long* out_idx, void* out_w);
 cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            const int* inverse, const long long* indices, int T, int K, int H,
                            int order, int experts_per_rank, int expert_lo, int expert_hi,

@@ -25,6 +25,7 @@ projection, bf16(bf16(silu(gate)) * up), bf16 down projection.
 
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 
 import torch
@@ -32,7 +33,7 @@ import torch.distributed as dist
 
 from moe_serving_profile_b200 import _lib, ops
 from moe_serving_profile_b200.experts import _max_tile, check_inputs, run_experts, tile_policy
-from moe_serving_profile_b200.layout import bf16_experts
+from moe_serving_profile_b200.layout import ExpertWeights, bf16_experts
 from moe_serving_profile_b200.router import native_route
 
 
@@ -269,13 +270,15 @@ class _Send:
     index: torch.Tensor
     weight: torch.Tensor       # bf16 [T, K]
     perm: ops.Permutation
-    rows: torch.Tensor         # [T*K, H] grouped by destination rank
+    rows: torch.Tensor | None  # [T*K, H] grouped by destination rank (None: no exchange)
 
 
-def _prepare(hidden, expert_index, expert_weight, num_experts) -> _Send:
+def _prepare(hidden, expert_index, expert_weight, num_experts, exchange: bool = True) -> _Send:
     hidden, index, weight = check_inputs(hidden, expert_index, expert_weight)
     perm = ops.permute(index, num_experts)
-    rows = ops.gather_rows(hidden, perm.perm_src, index.shape[1])
+    # the packed send rows only when they travel (one rank reads the tokens
+    # through the permutation instead)
+    rows = ops.gather_rows(hidden, perm.perm_src, index.shape[1]) if exchange else None
     # the reference scales by weight.to(rows.dtype) (moe.py:136)
     return _Send(hidden, index, weight.to(hidden.dtype).contiguous(), perm, rows)
 
@@ -353,7 +356,7 @@ def routed_forward(hidden: torch.Tensor, expert_index: torch.Tensor, expert_weig
         # every rank takes part in each exchange, also with no tokens
         h, idx, wt = check_inputs(hidden, expert_index, expert_weight)
         return _routed_forward_peer(h, idx, wt, experts.weights, plan, collective)
-    send = _prepare(hidden, expert_index, expert_weight, plan.num_experts)
+    send = _prepare(hidden, expert_index, expert_weight, plan.num_experts, exchange=ep > 1)
     if ep == 1:
         # no exchange: the experts read the tokens through the permutation
         returned = run_experts(experts.weights, send.hidden, send.perm, None, K=send.index.shape[1],
@@ -383,9 +386,37 @@ def routed_forward(hidden: torch.Tensor, expert_index: torch.Tensor, expert_weig
     return _combine(send, returned, el)
 
 
+def _joint_weights(experts: LocalSwiGLUExperts, shared: SharedSwiGLU) -> ExpertWeights | None:
+    """The shared expert packed as expert E after the E routed experts, so
+    that one grouped launch runs both; None when its intermediate does not fit
+    the routed experts' padded intermediate (then it runs as its own launch).
+    The shared expert's extra features are zero rows of gate / up and zero
+    columns of down: SwiGLU(0, 0) = 0 and adding zero products leaves every
+    sum unchanged, so the result is exact. The routed experts' pack becomes a
+    view of the joint one (no second copy of their weights)."""
+    w, sw = experts.weights, shared.weights
+    if sw.hidden != w.hidden or sw.inter > w.i_pad:
+        return None
+    E = w.n_experts
+    ips = sw.i_pad
+    w1 = torch.zeros((E + 1,) + tuple(w.w1.shape[1:]), device=w.w1.device, dtype=w.w1.dtype)
+    w1[:E] = w.w1
+    w1[E, :, :ips] = sw.w1[0]
+    w2 = torch.zeros((E + 1,) + tuple(w.w2.shape[1:]), device=w.w2.device, dtype=w.w2.dtype)
+    w2[:E] = w.w2
+    w2[E, :, :ips] = sw.w2[0]
+    experts.weights = dataclasses.replace(w, w1=w1[:E], w2=w2[:E])
+    return dataclasses.replace(w, n_experts=E + 1, inter=max(w.inter, sw.inter), w1=w1, w2=w2)
+
+
 class MoELayer(torch.nn.Module):
     """Router + token all-to-all experts + optional shared expert
-    (moe_serving/moe.py:140-168)."""
+    (moe_serving/moe.py:140-168). On one rank a shared expert whose
+    intermediate fits the routed experts' padded intermediate runs inside the
+    routed launch: every token gets one more slot routed to it (expert E,
+    weight sigmoid(hidden . score)), and the ordered combine adds that slot
+    last, which is the reference's ``output + shared(hidden)`` bit for bit.
+    """
 
     def __init__(self, gate_weight: torch.Tensor, experts: LocalSwiGLUExperts, plan: ExpertPlan,
                  top_k: int, renormalize: bool = True, shared: SharedSwiGLU | None = None,
@@ -402,6 +433,22 @@ class MoELayer(torch.nn.Module):
         self.renormalize = renormalize
         self.collective = collective or SingleRank()
         self.layer_id = layer_id
+        self.joint = _joint_weights(experts, shared) if shared is not None and plan.ep_size == 1 else None
+
+    def _joint_forward(self, hidden: torch.Tensor, indices: torch.Tensor,
+                       scores: torch.Tensor) -> torch.Tensor:
+        h, idx, wt = check_inputs(hidden, indices, scores)
+        T, K = idx.shape
+        if T == 0:
+            return h.new_zeros(h.shape)
+        E = self.plan.num_experts
+        # the score projection is the reference's own F.linear (moe.py:95)
+        logit = torch.nn.functional.linear(h, self.shared.score)
+        idx1, w1 = ops.append_shared_slot(idx, wt, logit, E)
+        perm = ops.permute(idx1, E + 1)
+        y = run_experts(self.joint, h, perm, None, K=K + 1, num_experts=E + 1, expert_begin=0)
+        return ops.combine(y, perm.inverse, idx1, order=_lib.ORDER_RANK_SLOT, experts_per_rank=E + 1,
+                           weights=w1)
 
     def forward(self, hidden: torch.Tensor) -> tuple[torch.Tensor, RoutingStats]:
         if self.logits_mode == "exact":
@@ -411,10 +458,13 @@ class MoELayer(torch.nn.Module):
         else:
             out = ops.router(_lib.ROUTER_NATIVE, hidden, self.gate_weight, None, self.top_k,
                              self.renormalize)
-        output = routed_forward(hidden, out.indices, out.scores, self.experts, self.plan,
-                                self.collective)
-        if self.shared is not None:
-            output = output + self.shared(hidden)
+        if self.joint is not None:
+            output = self._joint_forward(hidden, out.indices, out.scores)
+        else:
+            output = routed_forward(hidden, out.indices, out.scores, self.experts, self.plan,
+                                    self.collective)
+            if self.shared is not None:
+                output = output + self.shared(hidden)
         return output, RoutingStats(counts=out.counts.to(torch.int64).cpu(), layer=self.layer_id)
 
 

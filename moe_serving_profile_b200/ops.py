@@ -362,6 +362,31 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *,
     return out
 
 
+def append_shared_slot(indices: torch.Tensor, weights: torch.Tensor, score_logit: torch.Tensor,
+                       shared_expert: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """The routing of [T, K] extended by slot K = ``shared_expert`` with
+    weight bf16(sigmoid(score_logit)) (b200moe_append_shared_slot):
+    int64 [T, K + 1] expert ids and bf16 [T, K + 1] weights. score_logit is
+    the bf16 [T, 1] (or [T]) output of F.linear(hidden, score)."""
+    device = _dev(indices, "indices")
+    if indices.dtype != torch.int64 or indices.dim() != 2 or not indices.is_contiguous():
+        raise ValueError("indices must be a contiguous int64 [T, K] tensor")
+    T, K = indices.shape
+    if weights.shape != indices.shape or weights.dtype not in (torch.float32, torch.bfloat16) \
+            or not weights.is_contiguous():
+        raise ValueError("weights must be a contiguous fp32 or bf16 tensor shaped like indices")
+    logit = score_logit.reshape(T, -1)
+    if logit.dtype != torch.bfloat16 or logit.shape[1] != 1 or logit.device != indices.device:
+        raise ValueError("score_logit must be the bf16 [T, 1] score on the indices' device")
+    out_idx = torch.empty(T, K + 1, device=indices.device, dtype=torch.int64)
+    out_w = torch.empty(T, K + 1, device=indices.device, dtype=torch.bfloat16)
+    check(lib.b200moe_append_shared_slot(device, _stream(device), _ptr(indices), _ptr(weights),
+                                         int(weights.dtype == torch.bfloat16), _ptr(logit), logit.stride(0),
+                                         T, K, shared_expert, _ptr(out_idx), _ptr(out_w)),
+          "append_shared_slot")
+    return out_idx, out_w
+
+
 def combine_f32(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor,
                 *, expert_lo: int = 0, expert_hi: int = 1 << 30,
                 out: torch.Tensor | None = None) -> torch.Tensor:

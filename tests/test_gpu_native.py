@@ -193,3 +193,65 @@ def test_shared_expert_and_layer(cuda, T):
     assert torch.equal(y, routed + shared(hh.to(cuda)))
     sim = native.simulate_ranks([hh.to(cuda)], gate.to(cuda), [experts], K, shared=[shared])
     assert torch.equal(sim[0], y)
+
+
+@pytest.mark.parametrize("T,I_s", [(1, 256), (37, 192), (300, 128)])
+def test_shared_expert_inside_the_routed_launch(cuda, T, I_s):
+    """On one rank a shared expert whose intermediate fits the routed
+    experts' padded intermediate runs as expert E of the routed launch
+    (one more slot per token, weight sigmoid(hidden . score), combined last):
+    bit for bit the routed output plus the separately computed shared
+    expert (moe.py:161-162), and within the layer tolerance of fp32 PyTorch."""
+    H, E, I, K = 512, 16, 256, 4
+    g = torch.Generator().manual_seed(T + I_s)
+    sg = (torch.randn(I_s, H, generator=g) * 0.05).bfloat16()
+    su = (torch.randn(I_s, H, generator=g) * 0.05).bfloat16()
+    sd = (torch.randn(H, I_s, generator=g) * 0.05).bfloat16()
+    sc = (torch.randn(1, H, generator=g) * 0.05).bfloat16()
+    gate_up, down, gate, (hh,) = _case(E, H, I, K, [T], seed=T + 7)
+    shared = native.SharedSwiGLU(sg.to(cuda), su.to(cuda), sd.to(cuda), sc.to(cuda))
+    experts = native.LocalSwiGLUExperts(gate_up.to(cuda), down.to(cuda))
+    plan = native.ExpertPlan(E, 1, 0)
+    layer = native.MoELayer(gate.to(cuda), experts, plan, K, shared=shared)
+    assert layer.joint is not None and layer.joint.n_experts == E + 1
+    x = hh.to(cuda)
+    y, stats = layer(x)
+    idx, wts = native.route(x, gate.to(cuda), K, True)
+    routed = native.routed_forward(x, idx, wts, experts, plan, native.SingleRank())
+    assert torch.equal(y, routed + shared(x))
+    assert torch.equal(stats.counts, torch.bincount(idx.reshape(-1).cpu(), minlength=E))
+    # the appended slot itself: routed ids and bf16 weights, then (E, torch.sigmoid)
+    logit = torch.nn.functional.linear(x, sc.to(cuda))
+    idx1, w1 = ops.append_shared_slot(idx, wts, logit, E)
+    assert torch.equal(idx1[:, :K], idx) and bool((idx1[:, K] == E).all())
+    assert torch.equal(w1[:, :K], wts.to(torch.bfloat16)) and torch.equal(w1[:, K], torch.sigmoid(logit)[:, 0])
+    # fp32 PyTorch of the whole layer on the same routing
+    hf = x.float().cpu()
+    ref = torch.zeros(T, H)
+    for t in range(T):
+        for k in range(K):
+            e = int(idx[t, k])
+            gu = gate_up[e].float() @ hf[t]
+            ref[t] += float(wts[t, k]) * (down[e].float() @ (torch.nn.functional.silu(gu[:I]) * gu[I:]))
+    act = torch.nn.functional.silu(hf @ sg.float().T) * (hf @ su.float().T)
+    ref += torch.sigmoid(hf @ sc.float().T) * (act @ sd.float().T)
+    _close(y.cpu(), ref.bfloat16(), "layer with the shared expert inside the routed launch")
+    assert _lib.device_status(cuda.index) == 0
+
+
+def test_shared_expert_too_wide_runs_as_its_own_launch(cuda):
+    """A shared intermediate beyond the routed experts' padded one keeps the
+    separate launch (the routed pack is left as it was)."""
+    H, E, I, K = 512, 8, 128, 2
+    gate_up, down, gate, (hh,) = _case(E, H, I, K, [24], seed=5)
+    g = torch.Generator().manual_seed(6)
+    w = lambda *s: (torch.randn(*s, generator=g) * 0.05).bfloat16().to(cuda)
+    shared = native.SharedSwiGLU(w(256, H), w(256, H), w(H, 256), w(1, H))
+    experts = native.LocalSwiGLUExperts(gate_up.to(cuda), down.to(cuda))
+    layer = native.MoELayer(gate.to(cuda), experts, native.ExpertPlan(E, 1, 0), K, shared=shared)
+    assert layer.joint is None
+    x = hh.to(cuda)
+    y, _ = layer(x)
+    idx, wts = native.route(x, gate.to(cuda), K, True)
+    assert torch.equal(y, native.routed_forward(x, idx, wts, experts, native.ExpertPlan(E, 1, 0),
+                                                native.SingleRank()) + shared(x))

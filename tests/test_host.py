@@ -354,3 +354,35 @@ def test_checkpoint_loader_gpt_oss_slices_the_expert_axis(tmp_path):
                                         w.dn_blocks[1:3], w.dn_scales[1:3], w.dn_bias[1:3], 1.702, 7.0)
     assert torch.equal(got.w1, want.w1) and torch.equal(got.w2, want.w2)
     assert torch.equal(got.b1, want.b1) and torch.equal(got.b2, want.b2)
+
+
+def test_shared_expert_joins_the_routed_pack_when_it_fits():
+    """MoELayer's joint pack (host arithmetic on CPU tensors): the shared
+    expert is expert E, zero-padded to the routed experts' intermediate; the
+    routed pack becomes a view of the joint one; a wider shared expert keeps
+    its own launch."""
+    from moe_serving_profile_b200 import native
+
+    E, H, I = 4, 128, 256
+    g = torch.Generator().manual_seed(3)
+    gate_up = torch.randn(E, 2 * I, H, generator=g).bfloat16()
+    down = torch.randn(E, H, I, generator=g).bfloat16()
+    w = lambda *s: torch.randn(*s, generator=g).bfloat16()
+    experts = native.LocalSwiGLUExperts(gate_up, down)
+    before = experts.weights.w1.clone(), experts.weights.w2.clone()
+    sg, su, sd = w(192, H), w(192, H), w(H, 192)
+    joint = native._joint_weights(experts, native.SharedSwiGLU(sg, su, sd, w(1, H)))
+    assert joint.n_experts == E + 1 and joint.inter == I and joint.i_pad == experts.weights.i_pad
+    assert torch.equal(joint.w1[:E], before[0]) and torch.equal(joint.w2[:E], before[1])
+    assert experts.weights.w1.data_ptr() == joint.w1.data_ptr() and experts.weights.n_experts == E
+    assert torch.equal(joint.w1[E, 0, :192, :H], sg) and torch.equal(joint.w1[E, 1, :192, :H], su)
+    assert not joint.w1[E, :, 192:].any() and not joint.w2[E, :, 192:].any()
+    assert torch.equal(joint.w2[E, :H, :192], sd)
+    wide = native.SharedSwiGLU(w(384, H), w(384, H), w(H, 384), w(1, H))
+    assert native._joint_weights(native.LocalSwiGLUExperts(gate_up, down), wide) is None
+
+
+def test_append_shared_slot_refuses_bad_shapes():
+    idx = torch.zeros(3, 2, dtype=torch.int64)
+    with pytest.raises(ValueError):
+        ops.append_shared_slot(idx, torch.zeros(3, 2), torch.zeros(3, 1, dtype=torch.bfloat16), 4)
