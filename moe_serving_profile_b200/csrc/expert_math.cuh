@@ -97,14 +97,17 @@ __device__ __forceinline__ void mx16_cvt(const uint2& q, uint32_t sexp, uint32_t
   }
 }
 
-__device__ __forceinline__ float silu_bf16(float g) { return bf16_rn(g / (1.f + expf(-g))); }
+// The epilogue roundings use the hardware conversion (bf16r): these warps
+// share the SM's issue slots with the converter warps, and the integer form
+// takes four operations a value.
+__device__ __forceinline__ float silu_bf16(float g) { return bf16r(g / (1.f + expf(-g))); }
 
 __device__ __forceinline__ float epilogue_gated(int epi, float g, float u, float bg, float bu,
                                                 float alpha, float limit) {
   if (epi == kEpiSwiglu) {
-    const float gb = bf16_rn(g);
-    const float ub = bf16_rn(u);
-    return bf16_rn(silu_bf16(gb) * ub);
+    const float gb = bf16r(g);
+    const float ub = bf16r(u);
+    return bf16r(silu_bf16(gb) * ub);
   }
   if (epi == kEpiClampF32) {
     // fp32 throughout, one rounding: fp32 accumulator + fp32 bias, clamp,
@@ -114,17 +117,17 @@ __device__ __forceinline__ float epilogue_gated(int epi, float g, float u, float
     gf = gf > limit ? limit : gf;
     uf = uf < -limit ? -limit : (uf > limit ? limit : uf);
     const float sg = gf / (1.f + expf(-alpha * gf));
-    return bf16_rn(sg * (uf + 1.f));
+    return bf16r(sg * (uf + 1.f));
   }
-  float gb = bf16_rn(bf16_rn(g) + bg);
-  float ub = bf16_rn(bf16_rn(u) + bu);
+  float gb = bf16r(bf16r(g) + bg);
+  float ub = bf16r(bf16r(u) + bu);
   gb = gb > limit ? limit : gb;
   ub = ub < -limit ? -limit : (ub > limit ? limit : ub);
-  const float t1 = bf16_rn(gb * alpha);
-  const float t2 = bf16_rn(1.f / (1.f + expf(-t1)));
-  const float glu = bf16_rn(gb * t2);
-  const float t3 = bf16_rn(ub + 1.f);
-  return bf16_rn(t3 * glu);
+  const float t1 = bf16r(gb * alpha);
+  const float t2 = bf16r(1.f / (1.f + expf(-t1)));
+  const float glu = bf16r(gb * t2);
+  const float t3 = bf16r(ub + 1.f);
+  return bf16r(t3 * glu);
 }
 
 }  // namespace b200
