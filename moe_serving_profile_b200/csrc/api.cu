@@ -810,7 +810,7 @@ int b200moe_gather_rows_range(int device, void* stream, const void* src, long lo
   if (rc) return rc;
   B200_CUDA(b200::launch_gather_rows_range(static_cast<cudaStream_t>(stream), src, ld_src, map, div,
                                            n, H, dst, ld_dst, offsets, expert_lo, expert_hi,
-                                           8 * g_sm_count[device]));
+                                           32 * g_sm_count[device]));
   return B200MOE_OK;
 }
 

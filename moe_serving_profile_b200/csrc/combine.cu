@@ -16,34 +16,42 @@ __global__ void __launch_bounds__(128) combine_kernel(
     int hi, int scale_rows, const void* __restrict__ weights, int weights_bf16,
     __nv_bfloat16* __restrict__ out, long long ld_out) {
   const int t = blockIdx.x;
-  // Gather and order the token's contributions (redundantly per thread; K is small).
-  int rsel[kMaxK];
-  long long key[kMaxK];
-  float wsel[kMaxK];
-  int n = 0;
-  for (int k = 0; k < K; ++k) {
-    const long long e = indices[(long long)t * K + k];
-    const int r = inverse[(long long)t * K + k];
-    if (r < 0 || e < lo || e >= hi) continue;
-    long long kk = (order == 0) ? e * kMaxK + k : (e / epr) * kMaxK + k;
+  // The token's contributions in order: lane k of warp 0 reads slot k, its
+  // rank among the valid slots (keys are distinct) is its position, and the
+  // sorted rows and weights go to shared memory for the whole block.
+  __shared__ int s_row[kMaxK];
+  __shared__ float s_w[kMaxK];
+  __shared__ int s_n;
+  if (threadIdx.x < 32) {
+    const int k = threadIdx.x;
+    bool valid = false;
+    long long kk = 0;
+    int r = -1;
     float wv = 1.f;
-    if (scale_rows) {
-      wv = weights_bf16
-               ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(weights)[(long long)t * K + k])
-               : reinterpret_cast<const float*>(weights)[(long long)t * K + k];
+    if (k < K) {
+      const long long e = indices[(long long)t * K + k];
+      r = inverse[(long long)t * K + k];
+      valid = !(r < 0 || e < lo || e >= hi);
+      kk = (order == 0) ? e * kMaxK + k : (e / epr) * kMaxK + k;
+      if (valid && scale_rows)
+        wv = weights_bf16
+                 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(weights)[(long long)t * K + k])
+                 : reinterpret_cast<const float*>(weights)[(long long)t * K + k];
     }
-    // insertion sort by key (stable; keys are distinct)
-    int p = n++;
-    while (p > 0 && key[p - 1] > kk) {
-      key[p] = key[p - 1];
-      rsel[p] = rsel[p - 1];
-      wsel[p] = wsel[p - 1];
-      --p;
+    const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+    int pos = 0;
+    for (int j = 0; j < K; ++j) {
+      const long long kj = __shfl_sync(0xffffffffu, kk, j);
+      if (((vmask >> j) & 1u) && kj < kk) ++pos;
     }
-    key[p] = kk;
-    rsel[p] = r;
-    wsel[p] = wv;
+    if (valid) {
+      s_row[pos] = r;
+      s_w[pos] = wv;
+    }
+    if (k == 0) s_n = __popc(vmask);
   }
+  __syncthreads();
+  const int n = s_n;
   const int nvec = H >> 3;
   for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
     float acc[8];
@@ -55,7 +63,7 @@ __global__ void __launch_bounds__(128) combine_kernel(
       uint4 q[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (i0 + u < n) q[u] = __ldg(reinterpret_cast<const uint4*>(rows + rsel[i0 + u] * ld_rows) + v);
+        if (i0 + u < n) q[u] = __ldg(reinterpret_cast<const uint4*>(rows + s_row[i0 + u] * ld_rows) + v);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         if (i0 + u >= n) break;
@@ -65,8 +73,8 @@ __global__ void __launch_bounds__(128) combine_kernel(
           float c0 = __uint_as_float(wd[j] << 16);
           float c1 = __uint_as_float(wd[j] & 0xffff0000u);
           if (scale_rows) {
-            c0 = bf16r(c0 * wsel[i0 + u]);
-            c1 = bf16r(c1 * wsel[i0 + u]);
+            c0 = bf16r(c0 * s_w[i0 + u]);
+            c1 = bf16r(c1 * s_w[i0 + u]);
           }
           acc[2 * j] = bf16r(acc[2 * j] + c0);
           acc[2 * j + 1] = bf16r(acc[2 * j + 1] + c1);
