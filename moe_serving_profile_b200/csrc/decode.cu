@@ -26,10 +26,10 @@
 //               token columns. At the end of a tile one warp of a pair hands
 //               its partial sums to the other through shared memory, which
 //               adds them and runs the epilogue from registers (the two
-//               warps take the epilogues of alternate tiles). Sixteen warps keep the conversion pipes busy:
-//               the exact e4m3 -> bf16 conversion of one k-block (8192
-//               values) takes about 290 cycles with 8 warps resident and 140
-//               with 32.
+//               warps take the epilogues of alternate tiles). Sixteen warps
+//               keep the conversion pipes busy: the exact e4m3 -> bf16
+//               conversion of one k-block (8192 values) takes about 290
+//               cycles with 8 warps resident and 140 with 32.
 // k-slot mapping: lane (g, t) (g = lane / 4, t = lane % 4) holds physical
 // columns 16 t .. 16 t + 15 of its rows, one 16-byte chunk (FP8) or 8 bytes
 // (MXFP4); MMA step s (0..3) uses physical columns 16 t + 4 s .. + 3 as its
