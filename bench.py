@@ -758,9 +758,18 @@ def main():
                 "kernel_ms": round(kms, 4)}
 
     # ---- end to end through the public modules with host buffers
-    host_x = {T: xs[T].cpu().pin_memory() for T in batches}
-    host_o = {T: torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory() for T in batches}
-    h2d = sum(T * cfg.hidden * 2 for T in batches)
+    # On N GPUs every token crosses the host link once per step: rank r
+    # uploads rows [r c, (r + 1) c) of each batch (c = ceil(T / N), the last
+    # slice padded), an all-gather over NVLink replicates the tokens the
+    # replicated-token layer needs on every rank, and rank r reads back the
+    # same rows of the (replicated) output. (Every rank copying whole batches
+    # made host memory traffic, not the layer, set the pace from 4 GPUs.)
+    chunk = {T: -(-T // world) for T in batches}
+    lo_hi = {T: (min(T, rank * chunk[T]), min(T, (rank + 1) * chunk[T])) for T in batches}
+    host_x = {T: xs[T][lo_hi[T][0]:lo_hi[T][1]].cpu().pin_memory() for T in batches}
+    host_o = {T: torch.empty(lo_hi[T][1] - lo_hi[T][0], cfg.hidden, dtype=torch.bfloat16).pin_memory()
+              for T in batches}
+    h2d = sum((lo_hi[T][1] - lo_hi[T][0]) * cfg.hidden * 2 for T in batches)
     d2h = h2d
 
     # Copies run on their own streams: every batch's tokens go host -> device
@@ -771,7 +780,8 @@ def main():
     # the middle: its upload hides behind the batches before it and its
     # download behind those after it; the smallest runs last.
     copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    dev_x = [{T: torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=dev) for T in batches}
+    # (N GPUs: the all-gather's padded buffer, chunk rows per rank)
+    dev_x = [{T: torch.empty(chunk[T] * world, cfg.hidden, dtype=torch.bfloat16, device=dev) for T in batches}
              for _ in range(2)]
     rest = sorted(batches)
     big = rest.pop()
@@ -788,16 +798,27 @@ def main():
         landed = {}
         with torch.cuda.stream(copy_in):
             for T in order:
-                xs_dev[T].copy_(host_x[T], non_blocking=True)
+                r0, r1 = lo_hi[T]
+                if world > 1:
+                    mine = xs_dev[T][rank * chunk[T]:(rank + 1) * chunk[T]]
+                    if r1 > r0:
+                        mine[:r1 - r0].copy_(host_x[T], non_blocking=True)
+                else:
+                    xs_dev[T].copy_(host_x[T], non_blocking=True)
                 landed[T] = torch.cuda.Event()
                 landed[T].record(copy_in)
         for T in order:
             stream.wait_event(landed[T])
             with torch.cuda.stream(stream):
-                o = layer_call(cfg, router, packed, xs_dev[T], parallel, rank, world)
+                if world > 1:
+                    full = xs_dev[T]
+                    dist.all_gather_into_tensor(full, full[rank * chunk[T]:(rank + 1) * chunk[T]].clone())
+                o = layer_call(cfg, router, packed, xs_dev[T][:T], parallel, rank, world)
             copy_out.wait_stream(stream)
             with torch.cuda.stream(copy_out):
-                host_o[T].copy_(o, non_blocking=True)
+                r0, r1 = lo_hi[T]
+                if r1 > r0:
+                    host_o[T].copy_(o[r0:r1], non_blocking=True)
                 o.record_stream(copy_out)
         done = torch.cuda.Event()
         done.record(stream)
