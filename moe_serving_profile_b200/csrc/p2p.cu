@@ -141,27 +141,39 @@ __global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_con
   const int owner = b % p.world;   // two-shot: the rank that finishes this block's rows
 
   // ---- 1. partial sums of this block's rows, pushed to the inbox(es)
+  // The row's local contributions in (expert, slot) order: lane k of warp 0
+  // reads slot k, its rank among the valid slots (keys are distinct) is its
+  // position, and the sorted rows and slots go to shared memory for the block.
+  __shared__ int s_row[kMaxK];
+  __shared__ int s_slot[kMaxK];
+  __shared__ int s_n;
   for (int t = b; t < p.T; t += kP2PBlocks) {   // gridDim.x == min(T, kP2PBlocks)
-    int rsel[kMaxK];
-    int ksel[kMaxK];
-    long long key[kMaxK];
-    int n = 0;
-    for (int k = 0; k < p.K; ++k) {
-      const long long e = p.indices[(long long)t * p.K + k];
-      const int r = p.inverse[(long long)t * p.K + k];
-      if (r < 0 || e < p.lo || e >= p.hi) continue;
-      const long long kk = e * kMaxK + k;
-      int q = n++;   // insertion sort by (expert, slot)
-      while (q > 0 && key[q - 1] > kk) {
-        key[q] = key[q - 1];
-        rsel[q] = rsel[q - 1];
-        ksel[q] = ksel[q - 1];
-        --q;
+    __syncthreads();   // the previous row's list is no longer read
+    if (threadIdx.x < 32) {
+      const int k = threadIdx.x;
+      bool valid = false;
+      long long kk = 0;
+      int r = -1;
+      if (k < p.K) {
+        const long long e = p.indices[(long long)t * p.K + k];
+        r = p.inverse[(long long)t * p.K + k];
+        valid = !(r < 0 || e < p.lo || e >= p.hi);
+        kk = e * kMaxK + k;
       }
-      key[q] = kk;
-      rsel[q] = r;
-      ksel[q] = k;
+      const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+      int pos = 0;
+      for (int j = 0; j < p.K; ++j) {
+        const long long kj = __shfl_sync(0xffffffffu, kk, j);
+        if (((vmask >> j) & 1u) && kj < kk) ++pos;
+      }
+      if (valid) {
+        s_row[pos] = r;
+        s_slot[pos] = k;
+      }
+      if (k == 0) s_n = __popc(vmask);
     }
+    __syncthreads();
+    const int n = s_n;
     for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
       float acc[8];
 #pragma unroll
@@ -171,13 +183,13 @@ __global__ void __launch_bounds__(128) combine_allreduce_kernel(const __grid_con
         uint4 qv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-          if (i0 + u < n) qv[u] = __ldg(reinterpret_cast<const uint4*>(p.rows + rsel[i0 + u] * p.ld_rows) + v);
+          if (i0 + u < n) qv[u] = __ldg(reinterpret_cast<const uint4*>(p.rows + s_row[i0 + u] * p.ld_rows) + v);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           if (i0 + u >= n) break;
           float wv = 1.f;
           if (p.scale_rows) {
-            const long long wi = (long long)t * p.K + ksel[i0 + u];
+            const long long wi = (long long)t * p.K + s_slot[i0 + u];
             wv = p.weights_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.weights)[wi])
                                 : reinterpret_cast<const float*>(p.weights)[wi];
           }
