@@ -137,28 +137,46 @@ __global__ void __launch_bounds__(1024) permute_hist_kernel(const long long* __r
 }
 
 // chist[c][e] -> absolute first position of expert e's rows in chunk c.
+// Warp w scans the chunks of experts w, w + 32, ..., its lanes taking 32
+// chunks at a time with a carry (one thread per expert walking every chunk
+// serially cost 11 us at 4096 tokens x 8 slots); then one block-wide scan
+// over the experts' totals, and every entry gets its expert's offset.
 __global__ void __launch_bounds__(1024) permute_scan_kernel(int E, int nchunks,
                                                              int* __restrict__ chist,
                                                              int* __restrict__ counts,
                                                              int* __restrict__ offsets) {
   __shared__ int scratch[40];
-  const int tid = threadIdx.x;
-  int s = 0;
-  if (tid < E) {
-    for (int c = 0; c < nchunks; ++c) {
-      const int v = chist[(long long)c * E + tid];
-      chist[(long long)c * E + tid] = s;
-      s += v;
+  __shared__ int s_tot[1024];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = warp; e < E; e += 32) {
+    int carry = 0;
+    for (int c0 = 0; c0 < nchunks; c0 += 32) {
+      const int c = c0 + lane;
+      const int v = c < nchunks ? chist[(long long)c * E + e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (c < nchunks) chist[(long long)c * E + e] = carry + incl - v;
+      carry += __shfl_sync(kFull, incl, 31);
     }
+    if (lane == 0) s_tot[e] = carry;
   }
+  __syncthreads();
+  const int s = tid < E ? s_tot[tid] : 0;
   int total;
   const int ex = block_exclusive_scan(s, E, scratch, &total);
   if (tid < E) {
     counts[tid] = s;
     offsets[tid] = ex;
-    for (int c = 0; c < nchunks; ++c) chist[(long long)c * E + tid] += ex;
+    s_tot[tid] = ex;   // every thread read its total before the scan's barriers
   }
   if (tid == 0) offsets[E] = total;
+  __syncthreads();
+  const long long n = (long long)nchunks * E;
+  for (long long i = tid; i < n; i += blockDim.x) chist[i] += s_tot[static_cast<int>(i % E)];
 }
 
 __global__ void __launch_bounds__(1024) permute_place_kernel(const long long* __restrict__ idx,
