@@ -324,6 +324,11 @@ __device__ __forceinline__ float butterfly_sum(float v, int K) {
 // torch's warp softmax: lane-sequential sums over e = lane + 32 i, then a
 // xor-butterfly across lanes, probs = exp(x - max) / sum) or the bf16 logits
 // (GPT_OSS). Sums over the k selected values use butterfly_sum.
+// NL: keys per lane (experts e = lane + 32 i, i < NL), the smallest of 1, 4, 8,
+// 16 that covers E: entries past E are -inf and change no sum or selection,
+// so every NL gives the same result; with 16 for every E, the loops of a
+// 128-expert router ran four times the entries they needed.
+template <int NL>
 __global__ void __launch_bounds__(256) router_select_kernel(const void* __restrict__ logits,
                                                              int T, int E, int K, int mode,
                                                              int normalize, float* probs,
@@ -334,9 +339,9 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
 
-  float key[kMaxPerLane];
+  float key[NL];
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < NL; ++i) {
     const int e = lane + 32 * i;
     float v = -INFINITY;
     if (e < E) {
@@ -352,19 +357,19 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
     // ---- softmax over all E (fp32): the keys become the probabilities
     float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) mx = fmaxf(mx, key[i]);
+    for (int i = 0; i < NL; ++i) mx = fmaxf(mx, key[i]);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
     float lsum = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NL; ++i) {
       key[i] = (lane + 32 * i < E) ? expf(key[i] - mx) : 0.f;
       lsum += key[i];
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NL; ++i) {
       const int e = lane + 32 * i;
       key[i] = key[i] / lsum;
       if (mode == kQwen3 && probs != nullptr && e < E) probs[(long long)t * E + e] = key[i];
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
   for (int k = 0; k < K; ++k) {
     unsigned long long best = 0ull;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NL; ++i) {
       const int e = lane + 32 * i;
       if (e < E && !((taken >> i) & 1u)) {
         const unsigned long long c =
@@ -395,7 +400,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(const void* __restri
     if ((e_sel & 31) == lane) taken |= 1u << (e_sel >> 5);
     float vsel = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
+    for (int i = 0; i < NL; ++i)
       if (lane + 32 * i == e_sel) vsel = key[i];
     vsel = __shfl_sync(kFull, vsel, e_sel & 31);
     if (lane == k) {
@@ -535,9 +540,14 @@ cudaError_t launch_router_select(cudaStream_t st, int mode, const void* logits, 
                                  long long* indices, int* counts) {
   if (T == 0) return cudaSuccess;
   const int blocks = (T + 7) / 8;
-  router_select_kernel<<<blocks, 256, 0, st>>>(logits, T, E, K, mode, normalize,
-                                               static_cast<float*>(probs), scores, indices,
-                                               counts);
+#define B200_SELECT(NL_)                                                                           \
+  router_select_kernel<NL_><<<blocks, 256, 0, st>>>(logits, T, E, K, mode, normalize,           \
+                                                    static_cast<float*>(probs), scores, indices, counts)
+  if (E <= 32) B200_SELECT(1);
+  else if (E <= 128) B200_SELECT(4);
+  else if (E <= 256) B200_SELECT(8);
+  else B200_SELECT(kMaxPerLane);
+#undef B200_SELECT
   return cudaGetLastError();
 }
 
