@@ -292,9 +292,19 @@ int b200moe_w8a8_gemm(int device, void* stream, const b200moe_gemm_args* args, c
  * sum of the reference's fast mode, qwen3_parallel.py:105-118).
  * scale_rows != 0: the contribution is bf16(f32(c) * w[t*K+k]) (weights fp32
  * or bf16); otherwise rows are already scaled (EPI_DOWN with row_weight).
+ *   order B200MOE_ORDER_SLOT_SUM: the local combine of the reference's W8A8
+ *     path (grouped_fp8, moe_serving/efficient_kernels.py:269-273:
+ *     values * weights.to(bf16), masked rows 0, then
+ *     values[inverse].reshape(T, K, H).sum(1)). The contribution of slot k is
+ *     bf16(f32(c) * f32(bf16(w[t*K+k]))) with scale_rows (c as is without);
+ *     slots that are dropped or outside [expert_lo, expert_hi) are +0. The
+ *     sum is torch's CUDA reduction over the slot dimension: fp32
+ *     accumulators a[k % 4] += contribution in ascending k, then
+ *     ((a0 + a1) + a2) + a3, rounded once to bf16. experts_per_rank unused.
  */
 #define B200MOE_ORDER_EXPERT 0
 #define B200MOE_ORDER_RANK_SLOT 1
+#define B200MOE_ORDER_SLOT_SUM 2
 
 int b200moe_combine(int device, void* stream, const void* rows, long long ld_rows,
                     const int* inverse, const long long* indices, int T, int K, int H,

@@ -21,7 +21,7 @@ STATUS_WAIT_TIMEOUT, STATUS_BAD_TILE, STATUS_BAD_INDEX, STATUS_PEER_TIMEOUT = 1,
 ROUTER_QWEN3, ROUTER_GPT_OSS, ROUTER_NATIVE = 0, 1, 2
 W_BF16, W_FP8, W_MXFP4 = 0, 1, 2
 EPI_SWIGLU, EPI_CLAMP_SWIGLU, EPI_DOWN, EPI_CLAMP_SWIGLU_F32, EPI_DOWN_F32 = 0, 1, 2, 3, 4
-ORDER_EXPERT, ORDER_RANK_SLOT = 0, 1
+ORDER_EXPERT, ORDER_RANK_SLOT, ORDER_SLOT_SUM = 0, 1, 2
 PERMUTE_SCRATCH_BYTES = 1 << 20
 
 EXPORTED = (

@@ -655,8 +655,10 @@ int b200moe_combine(int device, void* stream, const void* rows, long long ld_row
                     const void* weights, int weights_bf16, void* out, long long ld_out) {
   B200_CHECK(T >= 0 && K >= 1 && H >= 8, "bad sizes");
   if (K > 32 || H % 8 != 0) return fail(B200MOE_ERR_UNSUPPORTED, "combine needs K <= 32 and H %% 8 == 0");
-  B200_CHECK(order == B200MOE_ORDER_EXPERT || order == B200MOE_ORDER_RANK_SLOT, "bad order");
-  B200_CHECK(order == B200MOE_ORDER_EXPERT || experts_per_rank >= 1, "experts_per_rank must be >= 1");
+  B200_CHECK(order == B200MOE_ORDER_EXPERT || order == B200MOE_ORDER_RANK_SLOT ||
+                 order == B200MOE_ORDER_SLOT_SUM,
+             "bad order");
+  B200_CHECK(order != B200MOE_ORDER_RANK_SLOT || experts_per_rank >= 1, "experts_per_rank must be >= 1");
   if (T == 0) return B200MOE_OK;
   B200_CHECK(out && inverse && indices && rows, "rows, out, inverse and indices are required");
   B200_CHECK(!scale_rows || weights, "scale_rows needs weights");

@@ -90,6 +90,81 @@ __global__ void __launch_bounds__(128) combine_kernel(
   }
 }
 
+// Slot-sum combine (order SLOT_SUM): out[t] = bf16 of torch's CUDA sum over
+// the slot dimension of the [T, K, H] contributions, the local combine of the
+// W8A8 path (efficient_kernels.py:269-273). A thread keeps four fp32
+// accumulators per column, slot k adding into a[k % 4] in ascending k, and
+// folds them as ((a0 + a1) + a2) + a3: the order in which torch's reduction
+// kernel sums a strided dimension within one thread (four accumulators in
+// flight). A contribution is bf16(c * bf16(w)) with scaling; slots that are
+// dropped or outside [lo, hi) add +0, which leaves an fp32 sum that started
+// at +0 unchanged, so they are skipped.
+__global__ void __launch_bounds__(128) combine_slot_sum_kernel(
+    const __nv_bfloat16* __restrict__ rows, long long ld_rows, const int* __restrict__ inverse,
+    const long long* __restrict__ indices, int T, int K, int H, int lo, int hi, int scale_rows,
+    const void* __restrict__ weights, int weights_bf16, __nv_bfloat16* __restrict__ out,
+    long long ld_out) {
+  const int t = blockIdx.x;
+  __shared__ int s_row[kMaxK];
+  __shared__ float s_w[kMaxK];
+  if (threadIdx.x < K) {
+    const int k = threadIdx.x;
+    const long long e = indices[(long long)t * K + k];
+    const int r = inverse[(long long)t * K + k];
+    const bool valid = !(r < 0 || e < lo || e >= hi);
+    float wv = 1.f;
+    if (valid && scale_rows)
+      wv = weights_bf16
+               ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(weights)[(long long)t * K + k])
+               : bf16r(reinterpret_cast<const float*>(weights)[(long long)t * K + k]);
+    s_row[k] = valid ? r : -1;
+    s_w[k] = wv;
+  }
+  __syncthreads();
+  const int nvec = H >> 3;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float acc[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[a][j] = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 4) {
+      uint4 q[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+        if (k0 + a < K && s_row[k0 + a] >= 0)
+          q[a] = __ldg(reinterpret_cast<const uint4*>(rows + s_row[k0 + a] * ld_rows) + v);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        if (k0 + a >= K || s_row[k0 + a] < 0) continue;
+        const float w = s_w[k0 + a];
+        const uint32_t wd[4] = {q[a].x, q[a].y, q[a].z, q[a].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float c0 = __uint_as_float(wd[j] << 16);
+          float c1 = __uint_as_float(wd[j] & 0xffff0000u);
+          if (scale_rows) {
+            c0 = bf16r(__fmul_rn(c0, w));
+            c1 = bf16r(__fmul_rn(c1, w));
+          }
+          acc[a][2 * j] = __fadd_rn(acc[a][2 * j], c0);
+          acc[a][2 * j + 1] = __fadd_rn(acc[a][2 * j + 1], c1);
+        }
+      }
+    }
+    float s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      s[j] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][j], acc[1][j]), acc[2][j]), acc[3][j]);
+    uint4 o;
+    o.x = pack_bf16x2(s[0], s[1]);
+    o.y = pack_bf16x2(s[2], s[3]);
+    o.z = pack_bf16x2(s[4], s[5]);
+    o.w = pack_bf16x2(s[6], s[7]);
+    reinterpret_cast<uint4*>(out + t * ld_out)[v] = o;
+  }
+}
+
 // out[t] = bf16( sum over the token's slots k in order of fp32(w[t, k]) *
 // rows[inverse[t*K + k]] ), in fp32 with one rounding; only experts in
 // [lo, hi). The scatter-reduce of the fused MXFP4 path (matmul_ogs with
@@ -217,6 +292,12 @@ cudaError_t launch_combine(cudaStream_t st, const void* rows, long long ld_rows,
                            int scale_rows, const void* weights, int weights_bf16, void* out,
                            long long ld_out) {
   if (T == 0) return cudaSuccess;
+  if (order == 2) {
+    combine_slot_sum_kernel<<<T, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(rows), ld_rows, inverse,
+                                               indices, T, K, H, expert_lo, expert_hi, scale_rows, weights,
+                                               weights_bf16, static_cast<__nv_bfloat16*>(out), ld_out);
+    return cudaGetLastError();
+  }
   combine_kernel<<<T, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(rows), ld_rows, inverse,
                                     indices, T, K, H, order, experts_per_rank, expert_lo,
                                     expert_hi, scale_rows, weights, weights_bf16,

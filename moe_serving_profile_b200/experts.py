@@ -130,7 +130,9 @@ def run_experts_w8a8(w: ExpertWeights, hidden: torch.Tensor, perm: ops.Permutati
     moe_serving/efficient_kernels.py:243-274): the routed token rows and the
     gated activations are quantised to e4m3 per (row, 128-column group) and
     multiplied with the e4m3 weights on the tensor cores; FP32 block scales
-    of both sides are applied per group in fp32."""
+    of both sides are applied per group in fp32. With ``weights`` the rows
+    are bf16(bf16(y) * w); grouped_fp8's own combine takes them unscaled
+    (weights None) and scales them by bf16(w) in the slot-sum combine."""
     if w.fmt != _lib.W_FP8 or w.block[1] != 128 or w.block[0] % 64:
         raise ValueError("W8A8 needs FP8 weights with scale blocks of 128 columns (rows a multiple of 64)")
     T, H = hidden.shape
@@ -211,9 +213,10 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
     numerics "fast": each rank combines its own experts and the partial sums
     are all-reduced (moe_serving/qwen3_parallel.py:105-118).
     numerics "efficient": FP8 weights run the W8A8 experts of the reference's
-    grouped_fp8 (moe_serving/efficient_kernels.py:243-274); GPT-OSS MXFP4
-    weights its fused path (grouped_mxfp4, :157-206: fp32 epilogues and an
-    fp32 slot-order scatter-reduce); both combined like "fast".
+    grouped_fp8 (moe_serving/efficient_kernels.py:243-274) with its fp32
+    slot-sum combine; GPT-OSS MXFP4 weights its fused path (grouped_mxfp4,
+    :157-206: fp32 epilogues and an fp32 slot-order scatter-reduce); the
+    rank partials of both are all-reduced.
     """
     hidden, indices, weights = check_inputs(hidden, indices, weights)
     T, K = indices.shape
@@ -236,12 +239,21 @@ def layer_forward(w: ExpertWeights, hidden: torch.Tensor, indices: torch.Tensor,
         part = run_experts_mxfp4_efficient(w, hidden, perm, weights, indices, K=K,
                                            num_experts=num_experts, expert_begin=expert_begin)
         return part if size == 1 else parallel.reduce(part)
+    if numerics == "efficient" and w.fmt == _lib.W_FP8:
+        # W8A8 experts (grouped_fp8) with its local combine: unscaled rows
+        # times bf16 routing weights, fp32 sum over each token's slots, one
+        # rounding (efficient_kernels.py:269-273), then the all-reduce of the
+        # rank partials (:274)
+        y = run_experts_w8a8(w, hidden, perm, None, K=K, num_experts=num_experts, expert_begin=expert_begin)
+        part = ops.combine(y, perm.inverse, indices, order=_lib.ORDER_SLOT_SUM, expert_lo=expert_begin,
+                           expert_hi=expert_begin + w.n_experts, weights=weights)
+        return part if size == 1 else parallel.reduce(part)
     if numerics == "efficient":
-        # FP8: W8A8 experts (grouped_fp8). BF16: the weight-only experts. The
-        # rank-local partial sums are all-reduced, the reference's efficient
-        # EP exchange (efficient_kernels.py:206, 274).
-        run = run_experts_w8a8 if w.fmt == _lib.W_FP8 else run_experts
-        contrib = run(w, hidden, perm, weights, K=K, num_experts=num_experts, expert_begin=expert_begin)
+        # BF16 weights: the weight-only experts; the rank-local partial sums
+        # are all-reduced, the reference's efficient EP exchange
+        # (efficient_kernels.py:206, 274).
+        contrib = run_experts(w, hidden, perm, weights, K=K, num_experts=num_experts,
+                              expert_begin=expert_begin)
         if size == 1:
             return ops.combine(contrib, perm.inverse, indices, order=_lib.ORDER_EXPERT)
         return parallel.combine_reduce(contrib, perm.inverse, indices, expert_begin,

@@ -181,6 +181,37 @@ def combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, *,
     return _bf16_tensor(out, (T, H))
 
 
+def slot_sum(values: torch.Tensor) -> torch.Tensor:
+    """bf16 [T, K, H] -> bf16 [T, H]: torch's CUDA ``sum(1)`` over the slot
+    dimension, restated. With the slots strided (H elements apart) each
+    output is reduced by one thread with four fp32 accumulators in flight:
+    slot k adds into a[k % 4] in ascending k, then ((a0 + a1) + a2) + a3,
+    one rounding to bf16. Pinned to torch's recorded CUDA outputs
+    (tests/golden/slot_sum_torch_cuda.pt)."""
+    T, K, H = values.shape
+    acc = torch.zeros(4, T, H, dtype=torch.float32)
+    for k in range(K):
+        acc[k % 4] = acc[k % 4] + values[:, k].float()
+    return (((acc[0] + acc[1]) + acc[2]) + acc[3]).to(torch.bfloat16)
+
+
+def w8a8_local_combine(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor,
+                       weights: torch.Tensor | None, lo: int = 0, hi: int = 1 << 62) -> torch.Tensor:
+    """The local combine of grouped_fp8 (moe_serving/efficient_kernels.py:269-273):
+    contribution rows in permuted order times bf16 routing weights (one bf16
+    rounding), rows of dropped slots and of experts outside [lo, hi) zero,
+    then slot_sum over each token's K slots."""
+    T, K = indices.shape
+    inv = inverse.long().reshape(-1)
+    e = indices.reshape(-1).long()
+    valid = (inv >= 0) & (e >= lo) & (e < hi)
+    vals = rows[inv.clamp(min=0)]
+    if weights is not None:
+        vals = vals * weights.reshape(-1, 1).to(torch.bfloat16)
+    vals = vals.masked_fill(~valid[:, None], 0)
+    return slot_sum(vals.reshape(T, K, -1))
+
+
 def f32_to_e4m3_c(values: torch.Tensor) -> torch.Tensor:
     """e4m3fn codes (uint8) of fp32 values from the C encoder (round to
     nearest even, saturating at +-448)."""
@@ -353,19 +384,22 @@ def qwen_w8a8_project(x: torch.Tensor, gate_w, gate_s, up_w, up_s, down_w, down_
 
 def qwen_w8a8_layer(hidden, indices, weights, gate_w, gate_s, up_w, up_s, down_w, down_s, block,
                     k_pad_h: int | None = None, k_pad_i: int | None = None):
-    """W8A8 Qwen3 expert layer on one rank: the per-expert math of grouped_fp8
-    with the contributions bf16(y * w) added in ascending expert order (the
-    combine the GEMM path shares with the reference numerics)."""
+    """W8A8 Qwen3 expert layer on one rank, grouped_fp8
+    (moe_serving/efficient_kernels.py:243-273): each routed (token, slot)
+    row through qwen_w8a8_project, the contributions bf16(y * bf16(w)),
+    summed over each token's slots by slot_sum (fp32, one rounding)."""
+    T, K = indices.shape
     H = hidden.shape[1]
     inter = gate_w.shape[1]
     k_pad_h = -(-H // 64) * 64 if k_pad_h is None else k_pad_h
     k_pad_i = -(-inter // 128) * 128 if k_pad_i is None else k_pad_i
-
-    def project(e, x):
-        return qwen_w8a8_project(x, gate_w[e], gate_s[e], up_w[e], up_s[e], down_w[e], down_s[e], block,
-                                 k_pad_h, k_pad_i)
-
-    return ordered_expert_merge(hidden, indices, weights, project)
+    values = torch.zeros(T, K, H, dtype=torch.bfloat16)
+    for e in torch.unique(indices, sorted=True).tolist():
+        tok, slot = torch.where(indices == e)
+        y = qwen_w8a8_project(hidden[tok], gate_w[e], gate_s[e], up_w[e], up_s[e], down_w[e], down_s[e],
+                              block, k_pad_h, k_pad_i)
+        values[tok, slot] = y * weights[tok, slot, None].to(torch.bfloat16)
+    return slot_sum(values)
 
 
 _E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]

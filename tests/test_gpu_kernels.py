@@ -249,6 +249,48 @@ def test_combine_bit_exact(cuda, order, scale):
     assert torch.equal(out.cpu(), ref)
 
 
+@pytest.mark.parametrize("T,K,H,wdtype,lo,hi", [
+    (777, 8, 2048, torch.float32, 0, 128), (300, 8, 2880, torch.bfloat16, 16, 80),
+    (129, 4, 2880, torch.float32, 0, 128), (64, 6, 512, torch.float32, 32, 96),
+    (33, 1, 256, torch.bfloat16, 0, 128), (5, 32, 1024, torch.float32, 0, 128)])
+def test_combine_slot_sum_equals_torch(cuda, T, K, H, wdtype, lo, hi):
+    """Order SLOT_SUM against grouped_fp8's own combine run with torch on the
+    same GPU (efficient_kernels.py:269-273: rows times bf16 weights, masked
+    rows zero, values[inverse].reshape(T, K, H).sum(1)) and against the
+    oracle, bit for bit, on rows whose exponents make the fp32 summation order
+    visible in the bf16 result; dropped slots and rank ranges included."""
+    from tests.golden.make_slot_sum_golden import spread_values
+
+    E = 128
+    g = torch.Generator().manual_seed(T * K + H)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).long()
+    idx[3, 0] = -1                                          # a dropped slot
+    wts = (torch.rand(T, K, generator=g) * 1.5).to(wdtype)
+    wts[::2] = wts[::2, :1].clone()        # equal weights: the scaled +B / -B pair cancels
+    counts, offsets, perm, inv = oracle.permute(idx, E)
+    # token t's slot k holds values[t, k] (a token's slots share the +B / -B pair)
+    values = spread_values(T, K, H, seed=H + K).reshape(T * K, H)
+    rows = torch.zeros(T * K, H, dtype=torch.bfloat16)
+    kept = inv >= 0
+    rows[inv[kept].long()] = values[kept]
+    out = ops.combine(rows.to(cuda), inv.to(cuda), idx.to(cuda), order=_lib.ORDER_SLOT_SUM,
+                      expert_lo=lo, expert_hi=hi, weights=wts.to(cuda))
+    unscaled = ops.combine(rows.to(cuda), inv.to(cuda), idx.to(cuda), order=_lib.ORDER_SLOT_SUM,
+                           expert_lo=lo, expert_hi=hi)
+    _status_clean(cuda)
+    # the reference's expression, torch on the GPU
+    r, ic, w = rows.to(cuda), inv.long().to(cuda), wts.to(cuda)
+    e = idx.to(cuda).reshape(-1)
+    valid = (ic >= 0) & (e >= lo) & (e < hi)
+    vals = r[ic.clamp(min=0)] * w.reshape(-1, 1).to(torch.bfloat16)
+    vals.masked_fill_(~valid[:, None], 0)
+    want = vals.reshape(T, K, H).sum(1)
+    assert torch.equal(out, want)
+    plain = r[ic.clamp(min=0)].masked_fill(~valid[:, None], 0).reshape(T, K, H).sum(1)
+    assert torch.equal(unscaled, plain)
+    assert torch.equal(out.cpu(), oracle.w8a8_local_combine(rows, inv, idx, wts, lo, hi))
+
+
 def _p2p_buffer(cuda, t_cap, H, world):
     import ctypes
     ptr = ctypes.c_void_p()

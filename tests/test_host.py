@@ -148,7 +148,8 @@ def test_w8a8_paths_refuse_before_device_work():
 
 
 def test_efficient_numerics_dispatch(monkeypatch):
-    """numerics="efficient" runs the W8A8 experts for FP8 weights, the fused
+    """numerics="efficient" runs the W8A8 experts (with the slot-sum combine)
+    for FP8 weights, the fused
     MXFP4 path (fp32 epilogues, the reference's grouped_mxfp4) for GPT-OSS
     MXFP4 weights and the weight-only experts for BF16; GPT-OSS needs MXFP4
     storage for it, as the reference's check_runtime does."""
@@ -158,9 +159,9 @@ def test_efficient_numerics_dispatch(monkeypatch):
     from moe_serving_profile_b200 import gpt_oss
     from moe_serving_profile_b200.parallel import ParallelGroup
 
-    calls = []
+    calls, orders = [], []
     monkeypatch.setattr(X.ops, "permute", lambda idx, E: SimpleNamespace(inverse=None))
-    monkeypatch.setattr(X.ops, "combine", lambda contrib, inverse, idx, order: contrib)
+    monkeypatch.setattr(X.ops, "combine", lambda contrib, inverse, idx, order, **k: orders.append(order) or contrib)
     monkeypatch.setattr(X, "run_experts", lambda *a, **k: calls.append("weight_only") or "rows")
     monkeypatch.setattr(X, "run_experts_w8a8", lambda *a, **k: calls.append("w8a8") or "rows")
     # one GPU: BF16 weights take the single-call layer; GPT-OSS MXFP4 the
@@ -173,6 +174,9 @@ def test_efficient_numerics_dispatch(monkeypatch):
                               torch.zeros(3, 2, dtype=torch.int64), torch.zeros(3, 2), num_experts=4,
                               expert_begin=0, numerics="efficient")
         assert out == "rows" and calls[-1] == want
+        if fmt == _lib.W_FP8:
+            # grouped_fp8's local combine: bf16-weighted rows, fp32 slot sum
+            assert orders[-1] == _lib.ORDER_SLOT_SUM
     conf = SimpleNamespace(num_local_experts=4, swiglu_alpha=1.702, swiglu_limit=7.0)
     gpt_oss.ParallelExperts(conf, ParallelGroup(1), "mxfp4", "efficient")
     with pytest.raises(ValueError, match="mxfp4"):

@@ -121,6 +121,24 @@ def test_synthetic_quantisers_roundtrip():
     assert float((dec - w).norm() / w.norm()) < 0.15
 
 
+def test_oracle_slot_sum_matches_torch_cuda():
+    """oracle.slot_sum (four fp32 accumulators, slot k into a[k % 4], then
+    ((a0 + a1) + a2) + a3) reproduces torch's CUDA sum over the slot
+    dimension, recorded on a B200 by tests/golden/make_slot_sum_golden.py on
+    values whose bf16 result depends on the summation order (K = 1 .. 32); a
+    plain left-to-right fp32 sum does not."""
+    g = torch.load(GOLDEN / "slot_sum_torch_cuda.pt", weights_only=False)
+    order_visible = 0
+    for name, c in g["cases"].items():
+        got = oracle.slot_sum(c["values"])
+        assert torch.equal(got.view(torch.int16), c["sum"].view(torch.int16)), name
+        seq = torch.zeros(c["values"][:, 0].shape)
+        for k in range(c["values"].shape[1]):
+            seq = seq + c["values"][:, k].float()
+        order_visible += int(not torch.equal(seq.bfloat16(), c["sum"]))
+    assert order_visible >= 6
+
+
 def test_oracle_selection_matches_torch_cuda():
     """The oracle's top-k (slot order of equal values included) and its
     butterfly sum reproduce torch's CUDA topk / sum, recorded on a B200 by
