@@ -24,12 +24,20 @@
 //               rows (gate/up) or a 2D tile of contiguous rows (down)
 //   warps 4-7   epilogue (TMEM lane quarters 0-3): activation / bias /
 //               routing weight, bf16 stores
-//   warps 8-15  converters (quantised weights): two groups of four warps;
-//               group g converts the CTA's k-blocks g, g + 2, g + 4, ...,
-//               each lane one weight row, and writes the bf16 tile into a
-//               tensor-memory A stage (warp w owns TMEM lanes 32 (w % 4) ..
-//               + 31) that tcgen05.mma reads as its A operand. Four A stages
-//               per group let a group run ahead of the MMA's consumption.
+//   warps 8-15  converters (quantised weights), in one of three forms:
+//               - two MMA issuers (token tiles up to 64 rows): two groups of
+//                 four warps; group g converts the CTA's k-blocks g, g + 2,
+//                 ..., each lane one weight row, into tensor-memory A stages
+//                 (warp w owns TMEM lanes 32 (w % 4) .. + 31) that
+//                 tcgen05.mma reads as its A operand; four A stages per
+//                 group let a group run ahead of the MMA's consumption;
+//               - one issuer (128- and 160-row tiles): all eight warps
+//                 convert every k-block, half a weight row per lane, into
+//                 the same tensor-memory A stages;
+//               - 256-row tiles (a_smem): all eight warps convert every
+//                 k-block into 128-byte-swizzled shared-memory A stages, so
+//                 that the whole tensor memory holds two 256-column
+//                 accumulator slots.
 // All rings are phase-tracked mbarriers; every wait is bounded (see ptx.cuh).
 #include "expert_math.cuh"
 #include "gemm_params.h"
