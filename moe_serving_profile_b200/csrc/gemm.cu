@@ -34,7 +34,8 @@
 //               - one issuer (128- and 160-row tiles): all eight warps
 //                 convert every k-block, half a weight row per lane, into
 //                 the same tensor-memory A stages;
-//               - 256-row tiles (a_smem): all eight warps convert every
+//               - 256-row tiles (a_smem; only when the caller asks for
+//                 them): all eight warps convert every
 //                 k-block into 128-byte-swizzled shared-memory A stages, so
 //                 that the whole tensor memory holds two 256-column
 //                 accumulator slots.
