@@ -177,6 +177,22 @@ def test_efficient_numerics_dispatch(monkeypatch):
         if fmt == _lib.W_FP8:
             # grouped_fp8's local combine: bf16-weighted rows, fp32 slot sum
             assert orders[-1] == _lib.ORDER_SLOT_SUM
+    # two ranks, W8A8: the rank's experts [4, 8) are combined locally (slot
+    # sum, routing weights applied there, not in the down GEMM), then the
+    # [T, H] partials are all-reduced (efficient_kernels.py:269-274)
+    seen = {}
+    monkeypatch.setattr(X, "run_experts_w8a8",
+                        lambda w, h, perm, weights, **k: seen.update(gemm_weights=weights) or "rows")
+    monkeypatch.setattr(X.ops, "combine",
+                        lambda rows, inverse, idx, order, **k: seen.update(order=order, **k) or "partial")
+    group = SimpleNamespace(size=2, reduce=lambda t: seen.update(reduced=t) or "reduced")
+    wts = torch.rand(3, 2)
+    out = X.layer_forward(SimpleNamespace(fmt=_lib.W_FP8, n_experts=4, gated_epilogue=_lib.EPI_SWIGLU),
+                          torch.zeros(3, 64, dtype=torch.bfloat16), torch.zeros(3, 2, dtype=torch.int64), wts,
+                          num_experts=8, expert_begin=4, parallel=group, numerics="efficient")
+    assert out == "reduced" and seen["reduced"] == "partial" and seen["gemm_weights"] is None
+    assert seen["order"] == _lib.ORDER_SLOT_SUM and (seen["expert_lo"], seen["expert_hi"]) == (4, 8)
+    assert seen["weights"] is wts
     conf = SimpleNamespace(num_local_experts=4, swiglu_alpha=1.702, swiglu_limit=7.0)
     gpt_oss.ParallelExperts(conf, ParallelGroup(1), "mxfp4", "efficient")
     with pytest.raises(ValueError, match="mxfp4"):
