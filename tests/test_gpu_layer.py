@@ -149,6 +149,9 @@ def test_qwen3_235b_skewed_layer(cuda):
     _, scores, idx = router(x)
     cv = S.expert_load_cv(router.last_counts)
     print(f"\nqwen3-235b T={T}: expert_load_cv={cv:.3f}")
+    # the skew the workload names: expert_load_cv ~ 0.5 (seeded CPU draws of
+    # this shape give 0.49-0.57; the band leaves room for sampling noise)
+    assert 0.35 < cv < 0.75
     m = qwen_module(cfg, w, cuda)
     out = m(x, idx, scores)
     ref = _qwen_ref(w, x, idx, scores, cfg, cuda)
