@@ -38,6 +38,20 @@ def test_library_exports_every_declared_symbol():
     assert _lib.lib.b200moe_gemm_args_size() == ctypes.sizeof(_lib.GemmArgs)
 
 
+def test_binding_constants_match_the_header():
+    """Every status, format, epilogue, router mode and combine order of the
+    header has the same value in the ctypes binding."""
+    header = (ROOT / "include" / "b200moe.h").read_text()
+    consts = dict(re.findall(r"^#define B200MOE_([A-Z0-9_]+) (\d+)\b", header, re.M))
+    checked = 0
+    for name, value in consts.items():
+        if name == "H_":
+            continue
+        assert getattr(_lib, name) == int(value), name
+        checked += 1
+    assert checked >= 20 and consts["ORDER_SLOT_SUM"] == "2"
+
+
 def test_permute_workspace_is_host_arithmetic():
     n = ctypes.c_size_t(0)
     assert _lib.lib.b200moe_permute_workspace(64, 8, 128, ctypes.byref(n)) == _lib.OK
