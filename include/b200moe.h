@@ -333,11 +333,14 @@ int b200moe_append_shared_slot(int device, void* stream, const long long* indice
 /* The scatter-reduce of the reference's fused MXFP4 path (matmul_ogs with
  * gammas and a scatter index, efficient_kernels.py:195-205), replacing the
  * index_add_-order combine there: rows are the fp32 outputs of
- * B200MOE_EPI_DOWN_F32 (acc + bias), and
+ * B200MOE_EPI_DOWN_F32 (acc + bias), each (token, slot) row is scaled by
+ * its routing weight and rounded to bf16 (matmul_ogs's epilogue stores the
+ * gamma-scaled rows in the output dtype), and the token's rows are summed in
+ * fp32 (its grouped reduction):
  *   out[t, :] = bf16( sum over k = 0 .. K-1 in order of
- *                     fp32(weights[t*K+k]) * rows[inverse[t*K+k], :] )
- * in fp32 with one rounding, over the slots whose expert is in
- * [expert_lo, expert_hi). weights fp32 or bf16 [T][K]. H % 4 == 0. */
+ *                     fp32(bf16(rows[inverse[t*K+k], :] * fp32(weights[t*K+k]))) )
+ * over the slots whose expert is in [expert_lo, expert_hi). weights fp32 or
+ * bf16 [T][K]. H % 4 == 0. */
 int b200moe_combine_f32(int device, void* stream, const float* rows, long long ld_rows,
                         const int* inverse, const long long* indices, int T, int K, int H,
                         int expert_lo, int expert_hi, const void* weights, int weights_bf16, void* out,

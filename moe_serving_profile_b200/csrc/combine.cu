@@ -165,10 +165,13 @@ __global__ void __launch_bounds__(128) combine_slot_sum_kernel(
   }
 }
 
-// out[t] = bf16( sum over the token's slots k in order of fp32(w[t, k]) *
-// rows[inverse[t*K + k]] ), in fp32 with one rounding; only experts in
-// [lo, hi). The scatter-reduce of the fused MXFP4 path (matmul_ogs with
-// gammas, efficient_kernels.py:195-205).
+// out[t] = bf16( sum over the token's slots k in order of
+// fp32(bf16(rows[inverse[t*K + k]] * fp32(w[t, k]))) ), in fp32 with one
+// final rounding; only experts in [lo, hi). The scatter-reduce of the fused
+// MXFP4 path (matmul_ogs with gammas, efficient_kernels.py:195-205): its
+// epilogue scales each (token, slot) row of acc + bias by the gamma and
+// stores it in the output dtype, then a grouped reduction sums each token's
+// rows in fp32.
 __global__ void __launch_bounds__(128) combine_f32_kernel(
     const float* __restrict__ rows, long long ld_rows, const int* __restrict__ inverse,
     const long long* __restrict__ indices, int T, int K, int H, int lo, int hi,
@@ -186,10 +189,10 @@ __global__ void __launch_bounds__(128) combine_f32_kernel(
                           ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(weights)[(long long)t * K + k])
                           : reinterpret_cast<const float*>(weights)[(long long)t * K + k];
       const float4 y = __ldg(reinterpret_cast<const float4*>(rows + r * ld_rows) + v);
-      acc.x += y.x * w;
-      acc.y += y.y * w;
-      acc.z += y.z * w;
-      acc.w += y.w * w;
+      acc.x += bf16r(__fmul_rn(y.x, w));
+      acc.y += bf16r(__fmul_rn(y.y, w));
+      acc.z += bf16r(__fmul_rn(y.z, w));
+      acc.w += bf16r(__fmul_rn(y.w, w));
     }
     uint2 o;
     o.x = pack_bf16x2(acc.x, acc.y);

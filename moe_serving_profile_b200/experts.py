@@ -169,9 +169,10 @@ def run_experts_mxfp4_efficient(w: ExpertWeights, hidden: torch.Tensor, perm: op
     fused clamped SwiGLU and fp32 biases; moe_serving/efficient_kernels.py:157-206,
     biases made fp32 at gpt_oss_parallel.py:438-446): the gate/up epilogue
     works in fp32 and rounds once to bf16, the down projection keeps
-    acc + bias in fp32, and each token's slots are scaled by their routing
-    weights and summed in fp32 in slot order, rounded once. Returns this
-    rank's [T, H] bf16 partial (its experts only)."""
+    acc + bias in fp32, each (token, slot) row is scaled by its routing
+    weight and rounded to bf16 (the output dtype matmul_ogs stores it in),
+    and each token's rows are summed in fp32 in slot order, rounded once.
+    Returns this rank's [T, H] bf16 partial (its experts only)."""
     T, H = hidden.shape
     act = gate_up(w, hidden, perm, K=K, num_experts=num_experts, expert_begin=expert_begin, tokens=T,
                   epilogue=_lib.EPI_CLAMP_SWIGLU_F32)

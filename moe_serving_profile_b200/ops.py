@@ -390,8 +390,9 @@ def append_shared_slot(indices: torch.Tensor, weights: torch.Tensor, score_logit
 def combine_f32(rows: torch.Tensor, inverse: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor,
                 *, expert_lo: int = 0, expert_hi: int = 1 << 30,
                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """bf16 out[t] = fp32 sum over the token's slots in order of w * rows[inverse]
-    (fp32 rows of the fp32 down epilogue; b200moe_combine_f32)."""
+    """bf16 out[t] = fp32 sum over the token's slots in order of
+    bf16(w * rows[inverse]) (fp32 rows of the fp32 down epilogue, each scaled
+    row rounded to bf16 as matmul_ogs stores it; b200moe_combine_f32)."""
     device = _dev(indices, "indices")
     T, K = indices.shape
     if rows.dtype != torch.float32 or rows.dim() != 2 or rows.stride(1) != 1:

@@ -442,7 +442,14 @@ def gpt_oss_layer_efficient(hidden, indices, weights, gu_blocks, gu_scales, gu_b
     float64 standing in for fp32 accumulation, gu = x W_gu^T + b_gu; gate =
     min(gu[0::2], limit), up = clamp(gu[1::2], -limit, limit); the
     intermediate bf16(gate / (1 + exp(-alpha gate)) * (up + 1)); y = a W_dn^T +
-    b_dn; out[t] = bf16(sum over slots k in order of w[t, k] * y)."""
+    b_dn; each (token, slot) row rounded to bf16 after the routing weight,
+    bf16(w[t, k] * y), as the published matmul_ogs stores its gamma-scaled
+    scatter rows in the output dtype before the grouped reduction; out[t] =
+    bf16(sum over slots of those rows). On the reference's own check of this
+    path (tests/helpers/check_grouped_ep.py shapes) the restatement's relative
+    L2 against the fp32 module is 0.0028-0.0030, the hub kernel's recorded
+    0.0029-0.0030 (tests/validation_results/efficient_grouped_ep.json);
+    without the per-slot rounding it is 0.0023."""
     T, K = indices.shape
     x = hidden.double()
     out = torch.zeros(T, hidden.shape[1], dtype=torch.float64)
@@ -457,7 +464,7 @@ def gpt_oss_layer_efficient(hidden, indices, weights, gu_blocks, gu_scales, gu_b
         up = gu[:, 1::2].clamp(min=-limit, max=limit)
         a = (gate / (1 + torch.exp(-alpha * gate)) * (up + 1)).to(torch.bfloat16).double()
         y = a @ wdn.T + dn_bias[e].double()
-        out.index_put_((t,), y * wd[t, k, None], accumulate=True)
+        out.index_put_((t,), (y * wd[t, k, None]).to(torch.bfloat16).double(), accumulate=True)
     return out.to(torch.bfloat16)
 
 

@@ -229,8 +229,9 @@ def test_expert_layer_one_call_equals_separate_calls(cuda, name, T):
 def test_gpt_oss_efficient_layer_keeps_fp32_intermediates(cuda, T):
     """numerics="efficient" for GPT-OSS MXFP4 (the reference's fused
     grouped_mxfp4 path): fp32 gate/up epilogue with fp32 biases and one bf16
-    rounding of the intermediate, fp32 down + bias, fp32 slot-order
-    scatter-reduce. Against the float64 restatement of that algorithm
+    rounding of the intermediate, fp32 down + bias, each slot's row scaled
+    and rounded to bf16, fp32 slot-order reduce. Against the float64
+    restatement of that algorithm
     (oracle.gpt_oss_layer_efficient): only fp32 summation order differs, so
     relative L2 <= 2e-3 and max |error| <= 2^-6 max |ref|."""
     cfg = S.CONFIGS["gpt-oss-20b"]
@@ -250,8 +251,10 @@ def test_gpt_oss_efficient_layer_keeps_fp32_intermediates(cuda, T):
 
 def test_fp32_down_epilogue_and_slot_order_combine_exact(cuda):
     """EPI_DOWN_F32 writes acc + bias unrounded and b200moe_combine_f32 sums
-    w * row over a token's slots in fp32: with integer data, integer biases
-    and power-of-two weights every value is exact, so both are bit-exact."""
+    bf16(w * row) over a token's slots in fp32: with integer data, integer
+    biases and power-of-two weights the GEMM and every product are exact, the
+    bf16 roundings are those of the exact products, and the fp32 sum of two
+    of them is exact, so both are bit-exact."""
     from moe_serving_profile_b200 import layout, ops
     g = torch.Generator().manual_seed(5)
     E, H, I, T, K = 4, 256, 192, 40, 2
@@ -275,6 +278,6 @@ def test_fp32_down_epilogue_and_slot_order_combine_exact(cuda):
     exact = torch.einsum("ri,rhi->rh", act[:, :I].double(), wv.double()[e_of_row]) + bias.double()[e_of_row]
     assert torch.equal(y.cpu(), exact.float())
     out = ops.combine_f32(y, inv.to(cuda), idx.to(cuda), wts.to(cuda))
-    want = (exact[inv.long()].view(T, K, H) * wts.double()[..., None]).sum(1)
+    want = (exact[inv.long()].view(T, K, H) * wts.double()[..., None]).to(torch.bfloat16).double().sum(1)
     assert torch.equal(out.cpu(), want.to(torch.bfloat16))
     assert _lib.device_status(cuda.index) == 0
