@@ -395,7 +395,10 @@ def _joint_weights(experts: LocalSwiGLUExperts, shared: SharedSwiGLU) -> ExpertW
     sum unchanged, so the result is exact. The routed experts' pack becomes a
     view of the joint one (no second copy of their weights)."""
     w, sw = experts.weights, shared.weights
-    if sw.hidden != w.hidden or sw.inter > w.i_pad:
+    # both packs are bf16 [E][2][I_p][H_k] / [E][H_f][I_p] (LocalSwiGLUExperts
+    # and SharedSwiGLU take bf16 weights only), so the intermediate is axis 2
+    # of both; quantised blobs would need another slicing
+    if w.fmt != _lib.W_BF16 or sw.fmt != _lib.W_BF16 or sw.hidden != w.hidden or sw.inter > w.i_pad:
         return None
     E = w.n_experts
     ips = sw.i_pad
